@@ -1,0 +1,176 @@
+"""ctypes binding of libeii.so (the C ABI of include/eii.h).
+
+The shared library is built in-tree by build.py.  There is no fallback: if the library or a CUDA
+device is missing, calls raise EiiError.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libeii.so")
+
+EII_OK, EII_ERR_ARG, EII_ERR_IO, EII_ERR_CUDA, EII_ERR_DEVICE, EII_ERR_FORMAT = range(6)
+STATUS_NAMES = {0: "EII_OK", 1: "EII_ERR_ARG", 2: "EII_ERR_IO", 3: "EII_ERR_CUDA", 4: "EII_ERR_DEVICE",
+                5: "EII_ERR_FORMAT"}
+
+VOCAB, D_MODEL, N_LAYERS = 49152, 576, 30
+
+
+class EiiError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"{STATUS_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+_P = ctypes.c_void_p
+_SIGS = {
+    "eii_last_error": ([], ctypes.c_char_p),
+    "eii_version": ([], ctypes.c_int),
+    "eii_open": ([ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(_P)], ctypes.c_int),
+    "eii_open_memory": ([_P, ctypes.c_size_t, ctypes.c_int, ctypes.POINTER(_P)], ctypes.c_int),
+    "eii_close": ([_P], None),
+    "eii_forward": ([_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P, _P], ctypes.c_int),
+    "eii_forward_device": ([_P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int64, _P, _P], ctypes.c_int),
+    "eii_embed": ([_P, _P, ctypes.c_int, _P], ctypes.c_int),
+    "eii_block": ([_P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
+    "eii_rmsnorm": ([_P, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
+    "eii_logits": ([_P, _P, ctypes.c_int, _P], ctypes.c_int),
+    "eii_linear": ([_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
+                    ctypes.c_int, ctypes.c_int, _P, _P], ctypes.c_int),
+}
+
+
+def lib():
+    """Load libeii.so once (raises EiiError if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise EiiError(EII_ERR_CUDA, f"{LIB_PATH} is missing; run __graft_entry__.build() first")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in _SIGS.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = L
+    return _lib
+
+
+def check(rc):
+    if rc != EII_OK:
+        raise EiiError(rc, lib().eii_last_error().decode(errors="replace"))
+
+
+def ptr(a):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+class Engine:
+    """One engine handle on one CUDA device (owns the device weights and workspaces)."""
+
+    def __init__(self, model_bin, device=0):
+        h = ctypes.c_void_p()
+        if isinstance(model_bin, (bytes, bytearray, memoryview, np.ndarray)):
+            buf = np.frombuffer(model_bin, dtype=np.uint8) if not isinstance(model_bin, np.ndarray) else model_bin
+            check(lib().eii_open_memory(ptr(buf), buf.nbytes, device, ctypes.byref(h)))
+        else:
+            check(lib().eii_open(os.fsencode(model_bin), device, ctypes.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if self.h:
+            lib().eii_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, ids, embed=False, resid=False, logits=True, digests=False):
+        """ids [n_seq, T] -> dict of int32 states (exported layouts) and uint64 digests."""
+        ids = _c(ids, np.int64)
+        if ids.ndim == 1:
+            ids = ids[None, :]
+        n, T = ids.shape
+        out = {}
+        e = np.empty((n, T, D_MODEL), np.int32) if embed else None
+        r = np.empty((n, N_LAYERS, T, D_MODEL), np.int32) if resid else None
+        lg = np.empty((n, T, VOCAB), np.int32) if logits else None
+        dg = np.empty(n, np.uint64) if digests else None
+        check(lib().eii_forward(self.h, ptr(ids), n, T, ptr(e), ptr(r), ptr(lg), ptr(dg)))
+        for k, v in (("embed", e), ("resid", r), ("logits", lg), ("digests", dg)):
+            if v is not None:
+                out[k] = v
+        return out
+
+    def forward_device(self, ids_ptr, n_seq, T, logits_ptr=None, ld=VOCAB, digests_ptr=None, stream=None):
+        check(lib().eii_forward_device(self.h, ctypes.c_void_p(ids_ptr), n_seq, T,
+                                       ctypes.c_void_p(logits_ptr) if logits_ptr else None, ld,
+                                       ctypes.c_void_p(digests_ptr) if digests_ptr else None,
+                                       ctypes.c_void_p(stream) if stream else None))
+
+    def embed(self, ids):
+        ids = _c(ids, np.int64).reshape(-1)
+        x = np.empty((ids.size, D_MODEL), np.int64)
+        check(lib().eii_embed(self.h, ptr(ids), ids.size, ptr(x)))
+        return x
+
+    def block(self, layer, x, T=None):
+        x = _c(x, np.int64)
+        rows = x.shape[0]
+        T = rows if T is None else T
+        out = np.empty_like(x)
+        check(lib().eii_block(self.h, layer, ptr(x), rows // T, T, ptr(out)))
+        return out
+
+    def rmsnorm(self, x, gain_q, gain_f, f_out, bits_out):
+        x = _c(x, np.int64)
+        g = _c(gain_q, np.int64)
+        out = np.empty_like(x)
+        check(lib().eii_rmsnorm(self.h, ptr(x), x.shape[0], ptr(g), int(gain_f), int(f_out), int(bits_out), ptr(out)))
+        return out
+
+    def logits(self, x):
+        x = _c(x, np.int64)
+        out = np.empty((x.shape[0], VOCAB), np.int64)
+        check(lib().eii_logits(self.h, ptr(x), x.shape[0], ptr(out)))
+        return out
+
+    def linear(self, a, bits_in, W, m, n, f_in, f_out, bits_out, want_acc=True):
+        a = _c(a, np.int64)
+        W = _c(W, np.int8)
+        m = _c(m, np.int64)
+        n = _c(n, np.int64)
+        M, K = a.shape
+        N = W.shape[0]
+        out = np.empty((M, N), np.int64)
+        acc = np.empty((M, N), np.int64) if want_acc else None
+        check(lib().eii_linear(self.h, ptr(a), M, K, int(bits_in), ptr(W), ptr(m), ptr(n), N, int(f_in), int(f_out),
+                               int(bits_out), ptr(out), ptr(acc)))
+        return out, acc
+
+
+def digest_logits(logits):
+    """Host restatement of the device digest (include/eii.h, eii_forward `digests`)."""
+    lg = np.asarray(logits)
+    n, T, V = lg.shape
+    idx = (np.arange(T, dtype=np.uint64)[:, None] * np.uint64(V) + np.arange(V, dtype=np.uint64)[None, :])
+    with np.errstate(over="ignore"):
+        z = idx + np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        z = (z ^ (z >> np.uint64(31))) | np.uint64(1)
+        out = np.empty(n, np.uint64)
+        for s in range(n):
+            out[s] = (lg[s].astype(np.uint32).astype(np.uint64) * z).sum(dtype=np.uint64)
+    return out

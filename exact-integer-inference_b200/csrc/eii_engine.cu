@@ -1,0 +1,846 @@
+// Host side of the B200 engine: model.bin -> device layout, the per-layer launch schedule, and
+// the C ABI declared in include/eii.h.
+//
+// Device layout (all weights resident, about 135 MB):
+//   emb_q   int8 [49152][576]   shared by the embedding gather and the tied-logits GEMM (B operand)
+//   per layer: W_qkv int8 [960][576] (q | k | v rows), W_o [576][576],
+//              W_gu  int8 [3072][576] gate/up interleaved per 128-row tile (64 gate rows j..j+63,
+//                    then the 64 up rows j..j+63) so one GEMM tile yields gate and up of the same
+//                    features for the SiLU-gated epilogue,
+//              W_d   int8 [576][1536];
+//              per output column (m, n + f_in - f_out) as int2; norm gains, SiLU table int32.
+// Activations live in a chunk workspace of R rows (R = sequences in flight x T):
+//   x       int32 [R][576]          residual stream (f = 15)
+//   h       uint8 [2][R][576]       norm output byte planes (INT16)
+//   q,k,v   int16 [R][576|192|192]  RoPE'd q/k and v for attention
+//   ctx     uint8 [Pc][R][576]      attention output planes (Pc = 2 or 4 per layer format)
+//   gated   uint8 [Pm][R][1536]     SiLU-gated product planes (Pm = 2 or 4)
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cerrno>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "eii.h"
+#include "eii_gemm.cuh"
+#include "eii_kernels.cuh"
+
+using namespace eii;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CK(call)                                                                                      \
+    do {                                                                                              \
+        cudaError_t e_ = (call);                                                                      \
+        if (e_ != cudaSuccess)                                                                        \
+            return fail(EII_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+#define TRY(...)                         \
+    do {                                 \
+        int rc_ = (__VA_ARGS__);         \
+        if (rc_ != EII_OK) return rc_;   \
+    } while (0)
+
+constexpr int MODEL_LIN_N[7] = {576, 192, 192, 576, 1536, 1536, 576};
+constexpr int MODEL_LIN_K[7] = {576, 576, 576, 576, 576, 576, 1536};
+
+size_t model_bin_bytes() {
+    size_t n = (size_t)VOCAB * D_MODEL + 2 * (size_t)VOCAB * 8 + D_MODEL * 8 + 16 + (DMAX + 1) * 8 + 2 * ROPE_POS * 32 * 8;
+    size_t per = 24 * 8 + 2 * (D_MODEL * 8 + 8) + 65536 * 8;
+    for (int i = 0; i < 7; ++i) per += (size_t)MODEL_LIN_N[i] * MODEL_LIN_K[i] + 2 * (size_t)MODEL_LIN_N[i] * 8;
+    return n + N_LAYERS * per;
+}
+
+struct Fmt {
+    int bits, f;
+};
+
+struct LayerDev {
+    Fmt h, q, k, v, qr, kr, c, h2, g, u, s, m;
+    int f_m, Pc, Pm;
+    int norm1_shift, norm2_shift, rope_shift_q, rope_shift_k, shift_s, shift_c, gated_shift;
+    int32_t *ln1, *ln2, *silu;
+    int8_t *w_qkv, *w_o, *w_gu, *w_d;
+    int2 *msh_qkv, *msh_o, *msh_gu, *msh_d;
+    CUtensorMap tm_qkv, tm_o, tm_gu, tm_d;
+};
+
+struct ActMaps {
+    CUtensorMap h, ctx2, ctx4, gated2, gated4;
+};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode(EncodeTiledFn* fn) {
+    static EncodeTiledFn cached = nullptr;
+    if (!cached) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t st = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (st != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+            return fail(EII_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(st));
+        cached = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    *fn = cached;
+    return EII_OK;
+}
+
+// K-major uint8 tile maps with 128-byte swizzle, 128 x 128-byte boxes.
+int map_2d(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows) {
+    EncodeTiledFn enc;
+    TRY(get_encode(&enc));
+    cuuint64_t dims[2] = {K, rows};
+    cuuint64_t strides[1] = {K};
+    cuuint32_t box[2] = {128, 128};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(EII_ERR_CUDA, "cuTensorMapEncodeTiled(2d K=%llu rows=%llu) failed: %d",
+                                       (unsigned long long)K, (unsigned long long)rows, (int)r);
+    return EII_OK;
+}
+int map_planes(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint64_t planes) {
+    EncodeTiledFn enc;
+    TRY(get_encode(&enc));
+    cuuint64_t dims[3] = {K, rows, planes};
+    cuuint64_t strides[2] = {K, K * rows};
+    cuuint32_t box[3] = {128, 128, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(EII_ERR_CUDA, "cuTensorMapEncodeTiled(3d K=%llu rows=%llu P=%llu) failed: %d",
+                                       (unsigned long long)K, (unsigned long long)rows, (unsigned long long)planes, (int)r);
+    return EII_OK;
+}
+
+}  // namespace
+
+struct eii_engine {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    int8_t* emb_q = nullptr;
+    int32_t *emb_m = nullptr, *emb_n = nullptr;
+    int2* msh_logits = nullptr;
+    CUtensorMap tm_emb;
+    int32_t* final_q = nullptr;
+    int final_f = 0, f_y = 0, final_shift = 0;
+    int32_t *exp_tab = nullptr, *rope_c = nullptr, *rope_s = nullptr;
+    LayerDev L[N_LAYERS];
+    // chunk workspace
+    int cap_rows = 0;
+    int32_t* x = nullptr;
+    uint8_t* h_planes = nullptr;
+    int16_t *q = nullptr, *k = nullptr, *v = nullptr;
+    uint8_t* ctx_planes = nullptr;
+    uint8_t* gated_planes = nullptr;
+    int32_t* logits_ws = nullptr;
+    int64_t logits_ws_rows = 0;
+    int64_t* ids_dev = nullptr;
+    int64_t ids_cap = 0;
+    int* err_dev = nullptr;
+    std::map<int, ActMaps> maps;
+    std::vector<void*> weights;
+    std::vector<void*> workspace;
+};
+
+namespace {
+
+template <class T>
+int dalloc(std::vector<void*>& owner, T** p, size_t count) {
+    void* q = nullptr;
+    CK(cudaMalloc(&q, count * sizeof(T) + 16));
+    owner.push_back(q);
+    *p = static_cast<T*>(q);
+    return EII_OK;
+}
+
+void free_list(std::vector<void*>& v) {
+    for (void* p : v) cudaFree(p);
+    v.clear();
+}
+
+int free_workspace(eii_engine* e) {
+    free_list(e->workspace);
+    e->cap_rows = 0;
+    e->x = nullptr;
+    e->h_planes = e->ctx_planes = e->gated_planes = nullptr;
+    e->q = e->k = e->v = nullptr;
+    e->logits_ws = nullptr;
+    e->logits_ws_rows = 0;
+    e->maps.clear();
+    return EII_OK;
+}
+
+int ensure_rows(eii_engine* e, int rows) {
+    if (rows <= e->cap_rows) return EII_OK;
+    free_workspace(e);
+    auto& W = e->workspace;
+    TRY(dalloc(W, &e->x, (size_t)rows * D_MODEL));
+    TRY(dalloc(W, &e->h_planes, (size_t)2 * rows * D_MODEL));
+    TRY(dalloc(W, &e->q, (size_t)rows * D_MODEL));
+    TRY(dalloc(W, &e->k, (size_t)rows * 192));
+    TRY(dalloc(W, &e->v, (size_t)rows * 192));
+    TRY(dalloc(W, &e->ctx_planes, (size_t)4 * rows * D_MODEL));
+    TRY(dalloc(W, &e->gated_planes, (size_t)4 * rows * D_FF));
+    e->cap_rows = rows;
+    return EII_OK;
+}
+
+int ensure_logits_ws(eii_engine* e, int rows) {
+    if (rows <= e->logits_ws_rows) return EII_OK;
+    if (e->logits_ws) {
+        for (auto it = e->workspace.begin(); it != e->workspace.end(); ++it)
+            if (*it == e->logits_ws) { cudaFree(*it); e->workspace.erase(it); break; }
+        e->logits_ws = nullptr;
+    }
+    TRY(dalloc(e->workspace, &e->logits_ws, (size_t)rows * VOCAB));
+    e->logits_ws_rows = rows;
+    return EII_OK;
+}
+
+int ensure_ids(eii_engine* e, int64_t n) {
+    if (n <= e->ids_cap) return EII_OK;
+    if (e->ids_dev) {
+        for (auto it = e->workspace.begin(); it != e->workspace.end(); ++it)
+            if (*it == e->ids_dev) { cudaFree(*it); e->workspace.erase(it); break; }
+    }
+    e->ids_dev = nullptr;
+    TRY(dalloc(e->workspace, &e->ids_dev, (size_t)n));
+    e->ids_cap = n;
+    return EII_OK;
+}
+
+int act_maps(eii_engine* e, int rows, const ActMaps** out) {
+    auto it = e->maps.find(rows);
+    if (it == e->maps.end()) {
+        ActMaps am;
+        TRY(map_planes(&am.h, e->h_planes, D_MODEL, rows, 2));
+        TRY(map_planes(&am.ctx2, e->ctx_planes, D_MODEL, rows, 2));
+        TRY(map_planes(&am.ctx4, e->ctx_planes, D_MODEL, rows, 4));
+        TRY(map_planes(&am.gated2, e->gated_planes, D_FF, rows, 2));
+        TRY(map_planes(&am.gated4, e->gated_planes, D_FF, rows, 4));
+        it = e->maps.emplace(rows, am).first;
+    }
+    *out = &it->second;
+    return EII_OK;
+}
+
+template <int P, int KIND>
+int launch_gemm(eii_engine* e, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep, cudaStream_t st) {
+    using C = GemmCfg<P>;
+    static int attr_done_device = -1;
+    if (attr_done_device != e->device) {
+        CK(cudaFuncSetAttribute(k_plane_gemm<P, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_done_device = e->device;
+    }
+    const int tiles = ((ep.M + 127) / 128) * ((ep.N + 127) / 128);
+    const int grid = tiles < e->num_sms ? tiles : e->num_sms;
+    k_plane_gemm<P, KIND><<<grid, C::THREADS, C::SMEM, st>>>(A, B, ep);
+    CK(cudaGetLastError());
+    return EII_OK;
+}
+
+template <int KIND>
+int launch_gemm_p(eii_engine* e, int P, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep,
+                  cudaStream_t st) {
+    if (P == 2) return launch_gemm<2, KIND>(e, A, B, ep, st);
+    if (P == 4) return launch_gemm<4, KIND>(e, A, B, ep, st);
+    return fail(EII_ERR_FORMAT, "unsupported plane count %d", P);
+}
+
+int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, int shift, int bits,
+                uint8_t* planes, int P, int64_t* out64, cudaStream_t st) {
+    const int rows_per_block = 8;
+    k_rmsnorm<<<(rows + rows_per_block - 1) / rows_per_block, 32 * rows_per_block, 0, st>>>(x, rows, gain, shift, bits,
+                                                                                           planes, P, out64);
+    CK(cudaGetLastError());
+    return EII_OK;
+}
+
+int launch_embed(eii_engine* e, const int64_t* ids, int rows, cudaStream_t st) {
+    const int rows_per_block = 8;
+    k_embed<<<(rows + rows_per_block - 1) / rows_per_block, 32 * rows_per_block, 0, st>>>(ids, rows, e->emb_q, e->emb_m,
+                                                                                         e->emb_n, e->x, e->err_dev);
+    CK(cudaGetLastError());
+    return EII_OK;
+}
+
+int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
+    LayerDev& L = e->L[l];
+    const ActMaps* am;
+    TRY(act_maps(e, rows, &am));
+    const int nseq = rows / T;
+    TRY(launch_norm(e, e->x, rows, L.ln1, L.norm1_shift, L.h.bits, e->h_planes, 2, nullptr, st));
+
+    EpiParams ep{};
+    ep.M = rows; ep.N = 960; ep.K = D_MODEL; ep.msh = L.msh_qkv; ep.err = e->err_dev;
+    ep.T = T; ep.q_out = e->q; ep.k_out = e->k; ep.v_out = e->v; ep.rope_c = e->rope_c; ep.rope_s = e->rope_s;
+    ep.bits_q = L.q.bits; ep.bits_k = L.k.bits; ep.bits_v = L.v.bits; ep.bits_qr = L.qr.bits; ep.bits_kr = L.kr.bits;
+    ep.rope_shift_q = L.rope_shift_q; ep.rope_shift_k = L.rope_shift_k;
+    TRY(launch_gemm<2, EPI_QKV>(e, am->h, L.tm_qkv, ep, st));
+
+    AttnParams ap{};
+    ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;
+    ap.M = rows; ap.T = T; ap.shift_s = L.shift_s; ap.shift_c = L.shift_c; ap.bits_c = L.c.bits;
+    const int asmem = attn_smem_bytes(T);
+    k_attention<<<nseq * N_KV, ATTN_WARPS * 32, asmem, st>>>(ap);
+    CK(cudaGetLastError());
+
+    ep = EpiParams{};
+    ep.M = rows; ep.N = D_MODEL; ep.K = D_MODEL; ep.msh = L.msh_o; ep.err = e->err_dev; ep.x = e->x;
+    TRY(launch_gemm_p<EPI_RESID>(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, L.tm_o, ep, st));
+
+    TRY(launch_norm(e, e->x, rows, L.ln2, L.norm2_shift, L.h2.bits, e->h_planes, 2, nullptr, st));
+
+    ep = EpiParams{};
+    ep.M = rows; ep.N = 2 * D_FF; ep.K = D_MODEL; ep.msh = L.msh_gu; ep.err = e->err_dev;
+    ep.silu = L.silu; ep.bits_g = L.g.bits; ep.bits_u = L.u.bits; ep.gated_shift = L.gated_shift;
+    ep.bits_m = L.m.bits; ep.gated_P = L.Pm; ep.gated_planes = e->gated_planes;
+    TRY(launch_gemm<2, EPI_GATEUP>(e, am->h, L.tm_gu, ep, st));
+
+    ep = EpiParams{};
+    ep.M = rows; ep.N = D_MODEL; ep.K = D_FF; ep.msh = L.msh_d; ep.err = e->err_dev; ep.x = e->x;
+    TRY(launch_gemm_p<EPI_RESID>(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, L.tm_d, ep, st));
+    return EII_OK;
+}
+
+int run_logits(eii_engine* e, int rows, int32_t* logits, int64_t ld, cudaStream_t st) {
+    const ActMaps* am;
+    TRY(act_maps(e, rows, &am));
+    TRY(launch_norm(e, e->x, rows, e->final_q, e->final_shift, 16, e->h_planes, 2, nullptr, st));
+    EpiParams ep{};
+    ep.M = rows; ep.N = VOCAB; ep.K = D_MODEL; ep.msh = e->msh_logits; ep.err = e->err_dev;
+    ep.logits = logits; ep.ld_logits = ld;
+    return launch_gemm<2, EPI_LOGITS>(e, am->h, e->tm_emb, ep, st);
+}
+
+int check_device_error(eii_engine* e, cudaStream_t st) {
+    CK(cudaStreamSynchronize(st));
+    int code = 0;
+    CK(cudaMemcpy(&code, e->err_dev, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code) {
+        CK(cudaMemset(e->err_dev, 0, sizeof(int)));
+        if (code == ERR_BAD_TOKEN) return fail(EII_ERR_ARG, "token id outside [0, %d)", VOCAB);
+        return fail(EII_ERR_DEVICE, "kernel reported error %d (bounded wait timed out)", code);
+    }
+    return EII_OK;
+}
+
+int default_chunk_rows() {
+    const char* s = getenv("EII_CHUNK_ROWS");
+    int v = s ? atoi(s) : 0;
+    return v > 0 ? v : 16384;
+}
+
+int chunk_seqs_for(int n_seq, int T) {
+    int cs = default_chunk_rows() / T;
+    if (cs < 1) cs = 1;
+    if (cs > n_seq) cs = n_seq;
+    return cs;
+}
+
+// ------------------------------------------------------------------------- model loading
+struct Reader {
+    const uint8_t* p;
+    size_t left;
+    template <class T>
+    const T* take(size_t count) {
+        const size_t b = count * sizeof(T);
+        if (b > left) return nullptr;
+        const T* r = reinterpret_cast<const T*>(p);
+        p += b;
+        left -= b;
+        return r;
+    }
+};
+
+int narrow32(const int64_t* src, size_t n, std::vector<int32_t>& dst, const char* what) {
+    dst.resize(n);
+    for (size_t i = 0; i < n; ++i) {
+        if (src[i] < INT32_MIN || src[i] > INT32_MAX)
+            return fail(EII_ERR_FORMAT, "%s[%zu] = %lld does not fit int32", what, i, (long long)src[i]);
+        dst[i] = static_cast<int32_t>(src[i]);
+    }
+    return EII_OK;
+}
+
+template <class T>
+int upload(eii_engine* e, T** dst, const T* src, size_t count) {
+    TRY(dalloc(e->weights, dst, count));
+    CK(cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice));
+    return EII_OK;
+}
+
+int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
+    if (nbytes != model_bin_bytes())
+        return fail(EII_ERR_IO, "model.bin has %zu bytes, expected %zu (layout of c/intref.c:8-13)", nbytes, model_bin_bytes());
+    Reader r{data, nbytes};
+    const int8_t* emb_q = r.take<int8_t>((size_t)VOCAB * D_MODEL);
+    const int64_t* emb_m = r.take<int64_t>(VOCAB);
+    const int64_t* emb_n = r.take<int64_t>(VOCAB);
+    const int64_t* fgq = r.take<int64_t>(D_MODEL);
+    const int64_t* fgf = r.take<int64_t>(1);
+    const int64_t* fy = r.take<int64_t>(1);
+    const int64_t* expt = r.take<int64_t>(DMAX + 1);
+    const int64_t* rc = r.take<int64_t>(ROPE_POS * 32);
+    const int64_t* rsn = r.take<int64_t>(ROPE_POS * 32);
+    std::vector<int32_t> tmp;
+    TRY(upload(e, &e->emb_q, emb_q, (size_t)VOCAB * D_MODEL));
+    TRY(narrow32(emb_m, VOCAB, tmp, "emb_m"));
+    TRY(upload(e, &e->emb_m, tmp.data(), VOCAB));
+    TRY(narrow32(emb_n, VOCAB, tmp, "emb_n"));
+    TRY(upload(e, &e->emb_n, tmp.data(), VOCAB));
+    TRY(narrow32(fgq, D_MODEL, tmp, "final_gain"));
+    TRY(upload(e, &e->final_q, tmp.data(), D_MODEL));
+    e->final_f = (int)*fgf;
+    e->f_y = (int)*fy;
+    e->final_shift = 21 + e->final_f - e->f_y;
+    TRY(narrow32(expt, DMAX + 1, tmp, "exp_table"));
+    TRY(upload(e, &e->exp_tab, tmp.data(), DMAX + 1));
+    TRY(narrow32(rc, ROPE_POS * 32, tmp, "rope_cos"));
+    TRY(upload(e, &e->rope_c, tmp.data(), ROPE_POS * 32));
+    TRY(narrow32(rsn, ROPE_POS * 32, tmp, "rope_sin"));
+    TRY(upload(e, &e->rope_s, tmp.data(), ROPE_POS * 32));
+    {
+        std::vector<int2> msh(VOCAB);
+        for (int i = 0; i < VOCAB; ++i) msh[i] = make_int2((int)emb_m[i], (int)(emb_n[i] + e->f_y - 16));
+        TRY(upload(e, &e->msh_logits, msh.data(), VOCAB));
+    }
+    TRY(map_2d(&e->tm_emb, e->emb_q, D_MODEL, VOCAB));
+
+    for (int l = 0; l < N_LAYERS; ++l) {
+        LayerDev& L = e->L[l];
+        const int64_t* fm = r.take<int64_t>(24);
+        const int64_t* ln1 = r.take<int64_t>(D_MODEL);
+        const int64_t* ln1f = r.take<int64_t>(1);
+        const int64_t* ln2 = r.take<int64_t>(D_MODEL);
+        const int64_t* ln2f = r.take<int64_t>(1);
+        const int8_t* wq[7];
+        const int64_t *wm[7], *wn[7];
+        for (int i = 0; i < 7; ++i) {
+            wq[i] = r.take<int8_t>((size_t)MODEL_LIN_N[i] * MODEL_LIN_K[i]);
+            wm[i] = r.take<int64_t>(MODEL_LIN_N[i]);
+            wn[i] = r.take<int64_t>(MODEL_LIN_N[i]);
+        }
+        const int64_t* silu = r.take<int64_t>(65536);
+        if (!silu) return fail(EII_ERR_IO, "model.bin truncated in layer %d", l);
+        Fmt* F[12] = {&L.h, &L.q, &L.k, &L.v, &L.qr, &L.kr, &L.c, &L.h2, &L.g, &L.u, &L.s, &L.m};
+        for (int i = 0; i < 12; ++i) {
+            F[i]->bits = (int)fm[2 * i];
+            F[i]->f = (int)fm[2 * i + 1];
+            if (F[i]->bits != 16 && F[i]->bits != 32)
+                return fail(EII_ERR_FORMAT, "layer %d site %d has %d bits (16 or 32 expected)", l, i, F[i]->bits);
+        }
+        // Engine layout assumptions: norm outputs are two planes; q/k/v/rope outputs are int16;
+        // the gate value indexes the 65536-entry SiLU table (python/intref.py:272).
+        if (L.h.bits != 16 || L.h2.bits != 16) return fail(EII_ERR_FORMAT, "layer %d: norm output must be INT16", l);
+        if (L.q.bits != 16 || L.k.bits != 16 || L.v.bits != 16 || L.qr.bits != 16 || L.kr.bits != 16)
+            return fail(EII_ERR_FORMAT, "layer %d: q/k/v/rope formats must be INT16", l);
+        if (L.g.bits != 16) return fail(EII_ERR_FORMAT, "layer %d: gate_proj must be INT16", l);
+        L.f_m = (L.m.bits == 32) ? (L.m.f < L.s.f + L.u.f ? L.m.f : L.s.f + L.u.f) : L.m.f;
+        L.Pc = L.c.bits / 8;
+        L.Pm = L.m.bits / 8;
+        L.norm1_shift = 21 + (int)*ln1f - L.h.f;
+        L.norm2_shift = 21 + (int)*ln2f - L.h2.f;
+        L.rope_shift_q = 30 + L.q.f - L.qr.f;
+        L.rope_shift_k = 30 + L.k.f - L.kr.f;
+        L.shift_s = L.qr.f + L.kr.f + 3 - F_SCORE;
+        L.shift_c = 16 + L.v.f - L.c.f;
+        L.gated_shift = L.s.f + L.u.f - L.f_m;
+        TRY(narrow32(ln1, D_MODEL, tmp, "ln1"));
+        TRY(upload(e, &L.ln1, tmp.data(), D_MODEL));
+        TRY(narrow32(ln2, D_MODEL, tmp, "ln2"));
+        TRY(upload(e, &L.ln2, tmp.data(), D_MODEL));
+        TRY(narrow32(silu, 65536, tmp, "silu"));
+        TRY(upload(e, &L.silu, tmp.data(), 65536));
+
+        // q | k | v
+        {
+            std::vector<int8_t> w((size_t)960 * D_MODEL);
+            std::vector<int2> msh(960);
+            size_t off = 0;
+            const Fmt outf[3] = {L.q, L.k, L.v};
+            int col = 0;
+            for (int i = 0; i < 3; ++i) {
+                const size_t nb = (size_t)MODEL_LIN_N[i] * D_MODEL;
+                memcpy(w.data() + off, wq[i], nb);
+                off += nb;
+                for (int j = 0; j < MODEL_LIN_N[i]; ++j, ++col)
+                    msh[col] = make_int2((int)wm[i][j], (int)(wn[i][j] + L.h.f - outf[i].f));
+            }
+            TRY(upload(e, &L.w_qkv, w.data(), w.size()));
+            TRY(upload(e, &L.msh_qkv, msh.data(), 960));
+            TRY(map_2d(&L.tm_qkv, L.w_qkv, D_MODEL, 960));
+        }
+        // o
+        {
+            std::vector<int2> msh(D_MODEL);
+            for (int j = 0; j < D_MODEL; ++j) msh[j] = make_int2((int)wm[3][j], (int)(wn[3][j] + L.c.f - F_RES));
+            TRY(upload(e, &L.w_o, wq[3], (size_t)D_MODEL * D_MODEL));
+            TRY(upload(e, &L.msh_o, msh.data(), D_MODEL));
+            TRY(map_2d(&L.tm_o, L.w_o, D_MODEL, D_MODEL));
+        }
+        // gate / up interleaved per 128-row tile
+        {
+            std::vector<int8_t> w((size_t)2 * D_FF * D_MODEL);
+            std::vector<int2> msh(2 * D_FF);
+            for (int t = 0; t < D_FF / 64; ++t) {
+                for (int r2 = 0; r2 < 64; ++r2) {
+                    const int j = 64 * t + r2;
+                    memcpy(w.data() + ((size_t)128 * t + r2) * D_MODEL, wq[4] + (size_t)j * D_MODEL, D_MODEL);
+                    memcpy(w.data() + ((size_t)128 * t + 64 + r2) * D_MODEL, wq[5] + (size_t)j * D_MODEL, D_MODEL);
+                    msh[128 * t + r2] = make_int2((int)wm[4][j], (int)(wn[4][j] + L.h2.f - L.g.f));
+                    msh[128 * t + 64 + r2] = make_int2((int)wm[5][j], (int)(wn[5][j] + L.h2.f - L.u.f));
+                }
+            }
+            TRY(upload(e, &L.w_gu, w.data(), w.size()));
+            TRY(upload(e, &L.msh_gu, msh.data(), 2 * D_FF));
+            TRY(map_2d(&L.tm_gu, L.w_gu, D_MODEL, 2 * D_FF));
+        }
+        // down
+        {
+            std::vector<int2> msh(D_MODEL);
+            for (int j = 0; j < D_MODEL; ++j) msh[j] = make_int2((int)wm[6][j], (int)(wn[6][j] + L.f_m - F_RES));
+            TRY(upload(e, &L.w_d, wq[6], (size_t)D_MODEL * D_FF));
+            TRY(upload(e, &L.msh_d, msh.data(), D_MODEL));
+            TRY(map_2d(&L.tm_d, L.w_d, D_FF, D_MODEL));
+        }
+    }
+    if (r.left != 0) return fail(EII_ERR_IO, "model.bin has %zu trailing bytes", r.left);
+    return EII_OK;
+}
+
+int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
+    if (!out) return fail(EII_ERR_ARG, "out is null");
+    *out = nullptr;
+    int ndev = 0;
+    cudaError_t st = cudaGetDeviceCount(&ndev);
+    if (st != cudaSuccess || ndev == 0) return fail(EII_ERR_CUDA, "no CUDA device (%s)", cudaGetErrorString(st));
+    if (device < 0 || device >= ndev) return fail(EII_ERR_ARG, "device %d out of range [0, %d)", device, ndev);
+    CK(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return fail(EII_ERR_CUDA, "device %d is sm_%d%d; this build needs sm_100", device, prop.major, prop.minor);
+    eii_engine* e = new eii_engine();
+    e->device = device;
+    e->num_sms = prop.multiProcessorCount;
+    int rc = EII_OK;
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) rc = fail(EII_ERR_CUDA, "stream create failed");
+    if (rc == EII_OK) rc = dalloc(e->weights, &e->err_dev, 1);
+    if (rc == EII_OK && cudaMemset(e->err_dev, 0, sizeof(int)) != cudaSuccess) rc = fail(EII_ERR_CUDA, "memset failed");
+    if (rc == EII_OK) rc = load_model(e, static_cast<const uint8_t*>(data), nbytes);
+    if (rc == EII_OK && cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             attn_smem_bytes(ROPE_POS)) != cudaSuccess)
+        rc = fail(EII_ERR_CUDA, "attention smem attribute failed");
+    if (rc != EII_OK) {
+        eii_close(e);
+        return rc;
+    }
+    *out = e;
+    return EII_OK;
+}
+
+int check_forward_args(eii_engine* e, int n_seq, int T) {
+    if (!e) return fail(EII_ERR_ARG, "engine is null");
+    if (n_seq < 1) return fail(EII_ERR_ARG, "n_seq must be >= 1 (got %d)", n_seq);
+    if (T < 1 || T > ROPE_POS) return fail(EII_ERR_ARG, "T must be in [1, %d] (got %d)", ROPE_POS, T);
+    return EII_OK;
+}
+
+int check_ids_host(const int64_t* ids, int64_t n) {
+    for (int64_t i = 0; i < n; ++i)
+        if (ids[i] < 0 || ids[i] >= VOCAB) return fail(EII_ERR_ARG, "ids[%lld] = %lld outside [0, %d)", (long long)i, (long long)ids[i], VOCAB);
+    return EII_OK;
+}
+
+}  // namespace
+
+// =========================================================================================== C ABI
+extern "C" {
+
+const char* eii_last_error(void) { return g_err.c_str(); }
+
+int eii_version(void) { return 100; }
+
+int eii_open_memory(const void* data, size_t nbytes, int device, eii_engine** out) {
+    if (!data) return fail(EII_ERR_ARG, "data is null");
+    return open_common(data, nbytes, device, out);
+}
+
+int eii_open(const char* path, int device, eii_engine** out) {
+    if (!path) return fail(EII_ERR_ARG, "path is null");
+    FILE* f = fopen(path, "rb");
+    if (!f) return fail(EII_ERR_IO, "%s: %s", path, strerror(errno));
+    fseek(f, 0, SEEK_END);
+    const long sz = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    if (sz < 0) { fclose(f); return fail(EII_ERR_IO, "%s: cannot size file", path); }
+    std::vector<uint8_t> buf((size_t)sz);
+    const size_t got = fread(buf.data(), 1, buf.size(), f);
+    fclose(f);
+    if (got != buf.size()) return fail(EII_ERR_IO, "%s: short read", path);
+    return open_common(buf.data(), buf.size(), device, out);
+}
+
+void eii_close(eii_engine* e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    free_list(e->workspace);
+    free_list(e->weights);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+}
+
+int eii_forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int32_t* logits_dev, int64_t ld,
+                       uint64_t* digests_dev, void* stream) {
+    TRY(check_forward_args(e, n_seq, T));
+    if (!ids_dev) return fail(EII_ERR_ARG, "ids_dev is null");
+    if (logits_dev && (ld < VOCAB || (ld % 4) != 0 || (reinterpret_cast<uintptr_t>(logits_dev) & 15)))
+        return fail(EII_ERR_ARG, "logits_dev must be 16-byte aligned with ld >= %d, ld %% 4 == 0", VOCAB);
+    CK(cudaSetDevice(e->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+    const int cs = chunk_seqs_for(n_seq, T);
+    TRY(ensure_rows(e, cs * T));
+    if (!logits_dev && digests_dev) TRY(ensure_logits_ws(e, cs * T));
+    if (digests_dev) CK(cudaMemsetAsync(digests_dev, 0, sizeof(uint64_t) * n_seq, st));
+    for (int s0 = 0; s0 < n_seq; s0 += cs) {
+        const int ns = (n_seq - s0) < cs ? (n_seq - s0) : cs;
+        const int rows = ns * T;
+        TRY(launch_embed(e, ids_dev + (int64_t)s0 * T, rows, st));
+        for (int l = 0; l < N_LAYERS; ++l) TRY(run_layer(e, l, rows, T, st));
+        if (logits_dev || digests_dev) {
+            int32_t* lg = logits_dev ? logits_dev + (int64_t)s0 * T * ld : e->logits_ws;
+            const int64_t lld = logits_dev ? ld : VOCAB;
+            TRY(run_logits(e, rows, lg, lld, st));
+            if (digests_dev) {
+                k_digest<<<rows, 256, 0, st>>>(lg, lld, T, rows, reinterpret_cast<unsigned long long*>(digests_dev + s0));
+                CK(cudaGetLastError());
+            }
+        }
+    }
+    return check_device_error(e, st);
+}
+
+int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* embed_out, int32_t* resid_out,
+                int32_t* logits_out, uint64_t* digests) {
+    TRY(check_forward_args(e, n_seq, T));
+    if (!ids) return fail(EII_ERR_ARG, "ids is null");
+    TRY(check_ids_host(ids, (int64_t)n_seq * T));
+    CK(cudaSetDevice(e->device));
+    cudaStream_t st = e->stream;
+    const int cs = chunk_seqs_for(n_seq, T);
+    TRY(ensure_rows(e, cs * T));
+    TRY(ensure_ids(e, (int64_t)cs * T));
+    if (logits_out || digests) TRY(ensure_logits_ws(e, cs * T));
+    uint64_t* dig_dev = nullptr;
+    std::vector<void*> tmp;
+    if (digests) TRY(dalloc(tmp, &dig_dev, (size_t)cs));
+    int rc = EII_OK;
+    const size_t row_bytes = (size_t)D_MODEL * sizeof(int32_t);
+    for (int s0 = 0; s0 < n_seq && rc == EII_OK; s0 += cs) {
+        const int ns = (n_seq - s0) < cs ? (n_seq - s0) : cs;
+        const int rows = ns * T;
+        if (cudaMemcpyAsync(e->ids_dev, ids + (int64_t)s0 * T, sizeof(int64_t) * rows, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+            rc = fail(EII_ERR_CUDA, "ids upload failed");
+            break;
+        }
+        rc = launch_embed(e, e->ids_dev, rows, st);
+        if (rc == EII_OK && embed_out &&
+            cudaMemcpyAsync(embed_out + (int64_t)s0 * T * D_MODEL, e->x, row_bytes * rows, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            rc = fail(EII_ERR_CUDA, "embed download failed");
+        for (int l = 0; l < N_LAYERS && rc == EII_OK; ++l) {
+            rc = run_layer(e, l, rows, T, st);
+            if (rc == EII_OK && resid_out) {
+                // resid_out is [n_seq][30][T][576]: one T x 576 block per sequence and layer.
+                const size_t blk = row_bytes * T;
+                if (cudaMemcpy2DAsync(resid_out + ((int64_t)s0 * N_LAYERS + l) * T * D_MODEL, blk * N_LAYERS, e->x, blk,
+                                      blk, ns, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                    rc = fail(EII_ERR_CUDA, "residual download failed");
+            }
+        }
+        if (rc == EII_OK && (logits_out || digests)) {
+            rc = run_logits(e, rows, e->logits_ws, VOCAB, st);
+            if (rc == EII_OK && logits_out &&
+                cudaMemcpyAsync(logits_out + (int64_t)s0 * T * VOCAB, e->logits_ws, sizeof(int32_t) * (size_t)rows * VOCAB,
+                                cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                rc = fail(EII_ERR_CUDA, "logits download failed");
+            if (rc == EII_OK && digests) {
+                cudaMemsetAsync(dig_dev, 0, sizeof(uint64_t) * ns, st);
+                k_digest<<<rows, 256, 0, st>>>(e->logits_ws, VOCAB, T, rows, reinterpret_cast<unsigned long long*>(dig_dev));
+                if (cudaGetLastError() != cudaSuccess ||
+                    cudaMemcpyAsync(digests + s0, dig_dev, sizeof(uint64_t) * ns, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                    rc = fail(EII_ERR_CUDA, "digest failed");
+            }
+        }
+        if (rc == EII_OK) rc = check_device_error(e, st);
+    }
+    free_list(tmp);
+    return rc;
+}
+
+int eii_embed(eii_engine* e, const int64_t* ids, int n, int64_t* x_out) {
+    if (!e || !ids || !x_out || n < 1) return fail(EII_ERR_ARG, "bad arguments to eii_embed");
+    TRY(check_ids_host(ids, n));
+    CK(cudaSetDevice(e->device));
+    TRY(ensure_rows(e, n));
+    TRY(ensure_ids(e, n));
+    CK(cudaMemcpyAsync(e->ids_dev, ids, sizeof(int64_t) * n, cudaMemcpyHostToDevice, e->stream));
+    TRY(launch_embed(e, e->ids_dev, n, e->stream));
+    std::vector<int32_t> h((size_t)n * D_MODEL);
+    CK(cudaMemcpyAsync(h.data(), e->x, h.size() * 4, cudaMemcpyDeviceToHost, e->stream));
+    TRY(check_device_error(e, e->stream));
+    for (size_t i = 0; i < h.size(); ++i) x_out[i] = h[i];
+    return EII_OK;
+}
+
+static int upload_x(eii_engine* e, const int64_t* x, int rows) {
+    std::vector<int32_t> h((size_t)rows * D_MODEL);
+    for (size_t i = 0; i < h.size(); ++i) {
+        if (x[i] < INT32_MIN || x[i] > INT32_MAX) return fail(EII_ERR_ARG, "x[%zu] does not fit the INT32 residual", i);
+        h[i] = (int32_t)x[i];
+    }
+    CK(cudaMemcpy(e->x, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+    return EII_OK;
+}
+
+int eii_block(eii_engine* e, int layer, const int64_t* x_in, int n_seq, int T, int64_t* x_out) {
+    TRY(check_forward_args(e, n_seq, T));
+    if (layer < 0 || layer >= N_LAYERS) return fail(EII_ERR_ARG, "layer %d out of range", layer);
+    if (!x_in || !x_out) return fail(EII_ERR_ARG, "null buffer");
+    CK(cudaSetDevice(e->device));
+    const int rows = n_seq * T;
+    TRY(ensure_rows(e, rows));
+    TRY(upload_x(e, x_in, rows));
+    TRY(run_layer(e, layer, rows, T, e->stream));
+    std::vector<int32_t> h((size_t)rows * D_MODEL);
+    CK(cudaMemcpyAsync(h.data(), e->x, h.size() * 4, cudaMemcpyDeviceToHost, e->stream));
+    TRY(check_device_error(e, e->stream));
+    for (size_t i = 0; i < h.size(); ++i) x_out[i] = h[i];
+    return EII_OK;
+}
+
+int eii_rmsnorm(eii_engine* e, const int64_t* x, int rows, const int64_t* gain_q, int gain_f, int f_out, int bits_out,
+                int64_t* out) {
+    if (!e || !x || !gain_q || !out || rows < 1) return fail(EII_ERR_ARG, "bad arguments to eii_rmsnorm");
+    if (bits_out < 2 || bits_out > 64) return fail(EII_ERR_ARG, "bits_out %d out of range", bits_out);
+    CK(cudaSetDevice(e->device));
+    TRY(ensure_rows(e, rows));
+    TRY(upload_x(e, x, rows));
+    std::vector<int32_t> g(D_MODEL);
+    for (int i = 0; i < D_MODEL; ++i) {
+        if (gain_q[i] < INT32_MIN || gain_q[i] > INT32_MAX) return fail(EII_ERR_ARG, "gain does not fit int32");
+        g[i] = (int32_t)gain_q[i];
+    }
+    std::vector<void*> tmp;
+    int32_t* gd;
+    int64_t* od;
+    TRY(dalloc(tmp, &gd, D_MODEL));
+    TRY(dalloc(tmp, &od, (size_t)rows * D_MODEL));
+    int rc = EII_OK;
+    if (cudaMemcpy(gd, g.data(), D_MODEL * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = fail(EII_ERR_CUDA, "gain upload");
+    if (rc == EII_OK) rc = launch_norm(e, e->x, rows, gd, 21 + gain_f - f_out, bits_out, nullptr, 0, od, e->stream);
+    if (rc == EII_OK && cudaMemcpyAsync(out, od, (size_t)rows * D_MODEL * 8, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+        rc = fail(EII_ERR_CUDA, "download failed");
+    if (rc == EII_OK) rc = check_device_error(e, e->stream);
+    free_list(tmp);
+    return rc;
+}
+
+static int linear_device(eii_engine* e, const int64_t* a_dev, int M, int K, int bits_in, const CUtensorMap& tmB,
+                         const int2* msh_dev, int N, int bits_out, int64_t* out_dev, int64_t* acc_dev,
+                         std::vector<void*>& tmp) {
+    const int P = bits_in / 8;
+    uint8_t* planes;
+    TRY(dalloc(tmp, &planes, (size_t)P * M * K));
+    k_split_planes<<<1184, 256, 0, e->stream>>>(a_dev, (int64_t)M * K, P, (int64_t)M * K, planes);
+    CK(cudaGetLastError());
+    CUtensorMap tmA;
+    TRY(map_planes(&tmA, planes, K, M, P));
+    EpiParams ep{};
+    ep.M = M; ep.N = N; ep.K = K; ep.msh = msh_dev; ep.err = e->err_dev; ep.out64 = out_dev; ep.acc64 = acc_dev;
+    ep.bits_out = bits_out;
+    return launch_gemm_p<EPI_LINEAR>(e, P, tmA, tmB, ep, e->stream);
+}
+
+int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const int8_t* W, const int64_t* m,
+               const int64_t* n, int N, int f_in, int f_out, int bits_out, int64_t* out, int64_t* acc) {
+    if (!e || !a || !W || !m || !n || !out) return fail(EII_ERR_ARG, "null argument to eii_linear");
+    if (M < 1 || K < 32 || K > 1536 || K % 32 != 0) return fail(EII_ERR_ARG, "K must be a multiple of 32 in [32, 1536] (got %d)", K);
+    if (N < 16 || N % 16 != 0) return fail(EII_ERR_ARG, "N must be a positive multiple of 16 (got %d)", N);
+    if (bits_in != 16 && bits_in != 32) return fail(EII_ERR_ARG, "bits_in must be 16 or 32 (got %d)", bits_in);
+    if (bits_out < 2 || bits_out > 64) return fail(EII_ERR_ARG, "bits_out %d out of range", bits_out);
+    const int64_t lo = -(int64_t(1) << (bits_in - 1)), hi = (int64_t(1) << (bits_in - 1)) - 1;
+    for (int64_t i = 0; i < (int64_t)M * K; ++i)
+        if (a[i] < lo || a[i] > hi) return fail(EII_ERR_ARG, "a[%lld] outside the signed %d-bit range", (long long)i, bits_in);
+    CK(cudaSetDevice(e->device));
+    std::vector<int2> msh(N);
+    for (int j = 0; j < N; ++j) msh[j] = make_int2((int)m[j], (int)(n[j] + f_in - f_out));
+    std::vector<void*> tmp;
+    int64_t *a_dev, *out_dev, *acc_dev = nullptr;
+    int8_t* w_dev;
+    int2* msh_dev;
+    int rc = EII_OK;
+    rc = dalloc(tmp, &a_dev, (size_t)M * K);
+    if (rc == EII_OK) rc = dalloc(tmp, &out_dev, (size_t)M * N);
+    if (rc == EII_OK && acc) rc = dalloc(tmp, &acc_dev, (size_t)M * N);
+    if (rc == EII_OK) rc = dalloc(tmp, &w_dev, (size_t)N * K);
+    if (rc == EII_OK) rc = dalloc(tmp, &msh_dev, (size_t)N);
+    if (rc == EII_OK && (cudaMemcpy(a_dev, a, (size_t)M * K * 8, cudaMemcpyHostToDevice) != cudaSuccess ||
+                         cudaMemcpy(w_dev, W, (size_t)N * K, cudaMemcpyHostToDevice) != cudaSuccess ||
+                         cudaMemcpy(msh_dev, msh.data(), (size_t)N * sizeof(int2), cudaMemcpyHostToDevice) != cudaSuccess))
+        rc = fail(EII_ERR_CUDA, "upload failed");
+    CUtensorMap tmB;
+    if (rc == EII_OK) rc = map_2d(&tmB, w_dev, K, N);
+    if (rc == EII_OK) rc = linear_device(e, a_dev, M, K, bits_in, tmB, msh_dev, N, bits_out, out_dev, acc_dev, tmp);
+    if (rc == EII_OK && cudaMemcpyAsync(out, out_dev, (size_t)M * N * 8, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+        rc = fail(EII_ERR_CUDA, "download failed");
+    if (rc == EII_OK && acc && cudaMemcpyAsync(acc, acc_dev, (size_t)M * N * 8, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+        rc = fail(EII_ERR_CUDA, "download failed");
+    if (rc == EII_OK) rc = check_device_error(e, e->stream);
+    free_list(tmp);
+    return rc;
+}
+
+int eii_logits(eii_engine* e, const int64_t* x, int rows, int64_t* logits) {
+    if (!e || !x || !logits || rows < 1) return fail(EII_ERR_ARG, "bad arguments to eii_logits");
+    CK(cudaSetDevice(e->device));
+    TRY(ensure_rows(e, rows));
+    TRY(upload_x(e, x, rows));
+    std::vector<void*> tmp;
+    int64_t *y, *out;
+    TRY(dalloc(tmp, &y, (size_t)rows * D_MODEL));
+    int rc = dalloc(tmp, &out, (size_t)rows * VOCAB);
+    if (rc == EII_OK) rc = launch_norm(e, e->x, rows, e->final_q, e->final_shift, 16, nullptr, 0, y, e->stream);
+    if (rc == EII_OK) rc = linear_device(e, y, rows, D_MODEL, 16, e->tm_emb, e->msh_logits, VOCAB, 64, out, nullptr, tmp);
+    if (rc == EII_OK && cudaMemcpyAsync(logits, out, (size_t)rows * VOCAB * 8, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+        rc = fail(EII_ERR_CUDA, "download failed");
+    if (rc == EII_OK) rc = check_device_error(e, e->stream);
+    free_list(tmp);
+    return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,271 @@
+// Bandwidth-bound kernels of the forward pass: embedding gather, RMSNorm to byte planes,
+// integer attention, plane split, logits digest.  Warp-per-row layouts with vectorised,
+// coalesced HBM access; all arithmetic exact int64 (128-bit for the norm total).
+#pragma once
+#include <cstdint>
+
+#include "eii_int.cuh"
+
+namespace eii {
+
+constexpr int D_MODEL = 576, D_FF = 1536, VOCAB = 49152, N_LAYERS = 30;
+constexpr int N_HEADS = 9, N_KV = 3, HEAD_DIM = 64, ROPE_POS = 512, DMAX = 12 * 128;
+constexpr int F_RES = 15, F_SCORE = 7;
+constexpr int64_t EPS_S = 6184753;  // round(1e-5 * 576 * 2^30), python/intref.py:37
+
+enum : int { ERR_BAD_TOKEN = 201 };
+
+// --------------------------------------------------------------------------- embedding
+// x[t,c] = RS(emb_q[id,c] * emb_m[id], emb_n[id] - 15)   (python/intref.py:163-166)
+// One warp per token; lanes cover 576 bytes of the int8 row as 36 x 16-byte chunks.
+__global__ void k_embed(const int64_t* __restrict__ ids, int M, const int8_t* __restrict__ emb_q,
+                        const int32_t* __restrict__ emb_m, const int32_t* __restrict__ emb_n,
+                        int32_t* __restrict__ x, int* err) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= M) return;
+    int64_t id = ids[row];
+    if (id < 0 || id >= VOCAB) {
+        if (lane == 0) atomicCAS(err, 0, ERR_BAD_TOKEN);
+        id = 0;
+    }
+    const int64_t m = emb_m[id];
+    const int sh = emb_n[id] - F_RES;
+    const int4* src = reinterpret_cast<const int4*>(emb_q + id * D_MODEL);
+    int32_t* dst = x + static_cast<int64_t>(row) * D_MODEL;
+    for (int ch = lane; ch < D_MODEL / 16; ch += 32) {
+        const int4 w = __ldg(src + ch);
+        const int8_t* b = reinterpret_cast<const int8_t*>(&w);
+        int32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = static_cast<int32_t>(rs64(static_cast<int64_t>(b[i]) * m, sh));
+        int4* d4 = reinterpret_cast<int4*>(dst + ch * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d4[q] = reinterpret_cast<int4*>(o)[q];
+    }
+}
+
+// --------------------------------------------------------------------------- RMSNorm
+// Exact reciprocal root of python/intref.py:170-177 / c/intref.c:96-104:
+//   S = A 2^32 + B 2^17 + C = sum x^2 (exact, 128-bit), U = isqrt(floor(2^80 / (S + EPS_S))).
+// The quotient is < 2^58 (S + EPS_S >= 2^22); the root is seeded from a double square root and
+// then corrected with exact integer comparisons, so U is the exact integer square root.
+__device__ __forceinline__ int64_t norm_recip_root(int64_t A, int64_t B, int64_t C) {
+    const __int128 S = static_cast<__int128>(A) * (static_cast<__int128>(1) << 32) +
+                       static_cast<__int128>(B) * (static_cast<__int128>(1) << 17) + static_cast<__int128>(C);
+    const unsigned __int128 Tt = static_cast<unsigned __int128>(S) + static_cast<unsigned __int128>(EPS_S);
+    const uint64_t q = static_cast<uint64_t>((static_cast<unsigned __int128>(1) << 80) / Tt);
+    uint64_t s = static_cast<uint64_t>(sqrt(static_cast<double>(q)));
+    while (s > 0 && s * s > q) --s;
+    while ((s + 1) * (s + 1) <= q) ++s;
+    return static_cast<int64_t>(s);
+}
+
+__device__ __forceinline__ int64_t warp_sum64(int64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// out = SAT(RS(3 RS(x U, 16) g, 21 + fw - f_out), bits_out) (python/intref.py:178-181), written
+// as P = bits_out / 8 byte planes [P][M][576] (planes != nullptr) and/or int64 [M,576].
+// One warp per row; lane l owns columns 64 i + 2 l, 64 i + 2 l + 1, i < 9.
+__global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain, int shift_out,
+                          int bits_out, uint8_t* __restrict__ planes, int P, int64_t* __restrict__ out64) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= M) return;
+    const int2* xr = reinterpret_cast<const int2*>(x + static_cast<int64_t>(row) * D_MODEL);
+    int2 v[9];
+    int64_t A = 0, B = 0, C = 0;
+#pragma unroll
+    for (int i = 0; i < 9; ++i) {
+        v[i] = xr[32 * i + lane];
+        const int64_t h0 = v[i].x >> 16, l0 = v[i].x & 0xFFFF, h1 = v[i].y >> 16, l1 = v[i].y & 0xFFFF;
+        A += h0 * h0 + h1 * h1;
+        B += h0 * l0 + h1 * l1;
+        C += l0 * l0 + l1 * l1;
+    }
+    A = warp_sum64(A);
+    B = warp_sum64(B);
+    C = warp_sum64(C);
+    const int64_t U = norm_recip_root(A, B, C);
+#pragma unroll
+    for (int i = 0; i < 9; ++i) {
+        const int c = 64 * i + 2 * lane;
+        const int2 g = __ldg(reinterpret_cast<const int2*>(gain) + 32 * i + lane);
+        const int64_t z0 = rs64(static_cast<int64_t>(v[i].x) * U, 16), z1 = rs64(static_cast<int64_t>(v[i].y) * U, 16);
+        const int64_t o0 = sat64(rs64(z0 * g.x * 3, shift_out), bits_out);
+        const int64_t o1 = sat64(rs64(z1 * g.y * 3, shift_out), bits_out);
+        if (planes) {
+            for (int p = 0; p < P; ++p) {
+                const uint16_t pair = static_cast<uint16_t>(plane_byte(o0, p)) | (static_cast<uint16_t>(plane_byte(o1, p)) << 8);
+                *reinterpret_cast<uint16_t*>(planes + (static_cast<int64_t>(p) * M + row) * D_MODEL + c) = pair;
+            }
+        }
+        if (out64) {
+            out64[static_cast<int64_t>(row) * D_MODEL + c] = o0;
+            out64[static_cast<int64_t>(row) * D_MODEL + c + 1] = o1;
+        }
+    }
+}
+
+// --------------------------------------------------------------------------- attention
+// Integer causal attention of one sequence and one KV group (3 query heads), CUDA cores.
+//   s_ij = SAT16(RS(q_i . k_j, shift_s)), j <= i; rowmax; e = E[rowmax - s] (0 beyond DMAX);
+//   Z = sum e; P = floor((e 65536 + floor(Z/2)) / Z); ctx = SAT(RS(sum_j P v_j, shift_c), bits_c)
+// (python/intref.py:227-254, c/intref.c:160-187).  K and V of the group sit in shared memory as
+// int16 pairs with a 33-word row pitch (conflict-free column access); each warp owns one query
+// row at a time; lanes split the keys for the scores and the 64 dims for P.V.
+// The division by the per-row invariant Z is exact: a double-precision estimate of n / Z
+// (n < 2^47, Z < 2^40) is off by at most one and is corrected with integer remainders.
+struct AttnParams {
+    const int16_t* q;  // [M, 576]
+    const int16_t* k;  // [M, 192]
+    const int16_t* v;  // [M, 192]
+    const int32_t* exp_tab;  // [DMAX + 1]
+    uint8_t* ctx_planes;     // [P][M][576]
+    int P;
+    int M, T;
+    int shift_s, shift_c, bits_c;
+};
+
+constexpr int ATTN_WARPS = 8;
+
+__host__ __device__ constexpr int attn_smem_bytes(int T) {
+    return 2 * T * 33 * 4 + (DMAX + 1 + 3) * 4 + ATTN_WARPS * (T + 32) * 4;
+}
+
+__device__ __forceinline__ int64_t dot_pair(uint32_t a, uint32_t b) {
+    const int32_t a0 = static_cast<int16_t>(a & 0xFFFF), a1 = static_cast<int16_t>(a >> 16);
+    const int32_t b0 = static_cast<int16_t>(b & 0xFFFF), b1 = static_cast<int16_t>(b >> 16);
+    return static_cast<int64_t>(a0) * b0 + static_cast<int64_t>(a1) * b1;
+}
+
+__global__ void __launch_bounds__(ATTN_WARPS * 32) k_attention(AttnParams ap) {
+    extern __shared__ __align__(16) uint32_t sm[];
+    const int T = ap.T;
+    const int seq = blockIdx.x / N_KV, g = blockIdx.x % N_KV;
+    const int64_t row0 = static_cast<int64_t>(seq) * T;
+    uint32_t* Ks = sm;                 // [T][33]
+    uint32_t* Vs = Ks + T * 33;        // [T][33]
+    int32_t* E = reinterpret_cast<int32_t*>(Vs + T * 33);  // [DMAX + 1]
+    int32_t* wbuf = E + DMAX + 1 + 3;  // per warp: [T] scores/probabilities + [32] q row
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+    for (int i = threadIdx.x; i < T * 32; i += blockDim.x) {
+        const int j = i / 32, w = i % 32;
+        Ks[j * 33 + w] = reinterpret_cast<const uint32_t*>(ap.k + (row0 + j) * 192 + g * 64)[w];
+        Vs[j * 33 + w] = reinterpret_cast<const uint32_t*>(ap.v + (row0 + j) * 192 + g * 64)[w];
+    }
+    for (int i = threadIdx.x; i <= DMAX; i += blockDim.x) E[i] = ap.exp_tab[i];
+    __syncthreads();
+
+    int32_t* sc = wbuf + warp * (T + 32);
+    uint32_t* qrow = reinterpret_cast<uint32_t*>(sc + T);
+    for (int item = warp; item < 3 * T; item += ATTN_WARPS) {
+        const int hh = g * 3 + item / T;
+        const int i = item % T;
+        qrow[lane] = reinterpret_cast<const uint32_t*>(ap.q + (row0 + i) * D_MODEL + hh * 64)[lane];
+        __syncwarp();
+        int32_t lmax = INT32_MIN;
+        for (int j = lane; j <= i; j += 32) {
+            int64_t acc = 0;
+            const uint32_t* kr = Ks + j * 33;
+#pragma unroll 8
+            for (int w = 0; w < 32; ++w) acc += dot_pair(qrow[w], kr[w]);
+            const int32_t s = static_cast<int32_t>(sat64(rs64(acc, ap.shift_s), 16));
+            sc[j] = s;
+            lmax = max(lmax, s);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+        int64_t lz = 0;
+        for (int j = lane; j <= i; j += 32) {
+            const int32_t d = lmax - sc[j];
+            const int32_t e = d <= DMAX ? E[d] : 0;
+            sc[j] = e;
+            lz += e;
+        }
+        const int64_t Z = warp_sum64(lz);
+        const int64_t half = Z / 2;
+        const double rz = 1.0 / static_cast<double>(Z);
+        for (int j = lane; j <= i; j += 32) {
+            const int64_t n = static_cast<int64_t>(sc[j]) * 65536 + half;
+            int64_t p = static_cast<int64_t>(static_cast<double>(n) * rz);
+            int64_t r = n - p * Z;
+            if (r < 0) { --p; r += Z; }
+            if (r < 0) { --p; r += Z; }
+            if (r >= Z) { ++p; r -= Z; }
+            if (r >= Z) { ++p; }
+            sc[j] = static_cast<int32_t>(p);
+        }
+        __syncwarp();
+        int64_t a0 = 0, a1 = 0;
+        for (int j = 0; j <= i; ++j) {
+            const int64_t p = sc[j];
+            const uint32_t vv = Vs[j * 33 + lane];
+            a0 += p * static_cast<int16_t>(vv & 0xFFFF);
+            a1 += p * static_cast<int16_t>(vv >> 16);
+        }
+        const int64_t c0 = sat64(rs64(a0, ap.shift_c), ap.bits_c), c1 = sat64(rs64(a1, ap.shift_c), ap.bits_c);
+        const int64_t r = row0 + i;
+        const int col = hh * 64 + 2 * lane;
+        for (int p = 0; p < ap.P; ++p) {
+            const uint16_t pair = static_cast<uint16_t>(plane_byte(c0, p)) | (static_cast<uint16_t>(plane_byte(c1, p)) << 8);
+            *reinterpret_cast<uint16_t*>(ap.ctx_planes + (static_cast<int64_t>(p) * ap.M + r) * D_MODEL + col) = pair;
+        }
+        __syncwarp();
+    }
+}
+
+// --------------------------------------------------------------------------- plane split
+// int64 activations [M,K] (values within b = 8P bits) -> P byte planes [P][M][K].
+__global__ void k_split_planes(const int64_t* __restrict__ a, int64_t count, int P, int64_t plane_stride,
+                               uint8_t* __restrict__ planes) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t v = a[i];
+        for (int p = 0; p < P; ++p) planes[p * plane_stride + i] = plane_byte(v, p);
+    }
+}
+
+__global__ void k_i64_to_i32(const int64_t* __restrict__ a, int64_t n, int32_t* __restrict__ o) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        o[i] = static_cast<int32_t>(a[i]);
+}
+
+// --------------------------------------------------------------------------- digest
+// Per-sequence 64-bit digest of int32 logits [n_seq*T, V] (row stride ld):
+//   digest = sum over (t, v) of uint32(logit) * mix(t * V + v)  (mod 2^64),
+// mix = the splitmix64 finaliser, forced odd.  Order-independent, so blocks combine it with
+// 64-bit atomic adds; digests must be zeroed before the launch.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return (z ^ (z >> 31)) | 1ull;
+}
+
+__global__ void k_digest(const int32_t* __restrict__ logits, int64_t ld, int T, int n_rows,
+                         unsigned long long* __restrict__ digests) {
+    const int row = blockIdx.x;
+    if (row >= n_rows) return;
+    const int t = row % T;
+    const int4* src = reinterpret_cast<const int4*>(logits + row * ld);
+    uint64_t h = 0;
+    for (int c4 = threadIdx.x; c4 < VOCAB / 4; c4 += blockDim.x) {
+        const int4 v = __ldg(src + c4);
+        const uint64_t base = static_cast<uint64_t>(t) * VOCAB + 4ull * c4;
+        h += static_cast<uint64_t>(static_cast<uint32_t>(v.x)) * mix64(base);
+        h += static_cast<uint64_t>(static_cast<uint32_t>(v.y)) * mix64(base + 1);
+        h += static_cast<uint64_t>(static_cast<uint32_t>(v.z)) * mix64(base + 2);
+        h += static_cast<uint64_t>(static_cast<uint32_t>(v.w)) * mix64(base + 3);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) h += __shfl_xor_sync(0xffffffffu, h, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(digests + row / T, static_cast<unsigned long long>(h));
+}
+
+}  // namespace eii

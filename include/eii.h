@@ -1,0 +1,98 @@
+/*
+ * eii.h -- C ABI of the B200 engine for the integer-only SmolLM2-135M forward pass
+ * (standardgalactic/exact-integer-inference, python/intref.py is the definition).
+ *
+ * Plain C types only.  Every call returns an EII_* status; on failure eii_last_error() gives a
+ * message (thread local).  Nothing in the library calls exit().  A handle is bound to one CUDA
+ * device and owns the device copy of the weights and its workspaces; calls on one handle must be
+ * serialised by the caller, different handles may be used from different host threads.
+ *
+ * Integer results are bit-identical to python/intref.py: int64-valued states are returned as the
+ * int32/int64 the reference exports (exp_embed.i32, exp_resid_out.i32, exp_logits.i32).
+ */
+#ifndef EII_H
+#define EII_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  1..3 mirror the reference programs' exit codes where they overlap:
+ * c/intref.c and cuda/intref.cu exit 2 on I/O errors and 3 on CUDA errors. */
+#define EII_OK 0
+#define EII_ERR_ARG 1      /* bad argument: null pointer, shape, T > 512, token id out of range */
+#define EII_ERR_IO 2       /* model file missing, unreadable or of the wrong size */
+#define EII_ERR_CUDA 3     /* CUDA runtime/driver error, or no usable sm_100 device */
+#define EII_ERR_DEVICE 4   /* a kernel reported an error (bounded wait timed out, bad token) */
+#define EII_ERR_FORMAT 5   /* model.bin holds a format this engine does not implement */
+
+typedef struct eii_engine eii_engine;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* eii_last_error(void);
+
+/* Library ABI version (major * 10000 + minor * 100 + patch). */
+int eii_version(void);
+
+/* Load model.bin (layout of c/intref.c:8-13, writer python/export_vectors.py:24-45) onto
+ * `device`.  Replaces load_model() of c/intref.c:70-91 and cuda/intref.cu:184-206. */
+int eii_open(const char* model_bin_path, int device, eii_engine** out);
+
+/* Same, from a caller-owned buffer holding the model.bin bytes (copied; may be freed after). */
+int eii_open_memory(const void* data, size_t nbytes, int device, eii_engine** out);
+
+void eii_close(eii_engine* e);
+
+/* Forward pass of n_seq independent sequences of T tokens each (1 <= T <= 512), host buffers.
+ * Replaces Model.forward (python/intref.py:288-301) applied to each sequence, plus the state
+ * export of python/export_vectors.py:47-57.
+ *   ids        [n_seq][T] int64 token ids in [0, 49152)
+ *   embed_out  nullable, [n_seq][T][576] int32 embedding output (exp_embed.i32 per sequence)
+ *   resid_out  nullable, [n_seq][30][T][576] int32 residual after each block (exp_resid_out.i32)
+ *   logits_out nullable, [n_seq][T][49152] int32 logits, f = 16 (exp_logits.i32)
+ *   digests    nullable, [n_seq] uint64 order-independent digest of each sequence's logits:
+ *              sum over (t, v) of uint32(logit[t][v]) * mix64(t * 49152 + v) mod 2^64, mix64 the
+ *              splitmix64 finaliser with the low bit forced to 1. */
+int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* embed_out,
+                int32_t* resid_out, int32_t* logits_out, uint64_t* digests);
+
+/* Device-resident variant: ids_dev, logits_dev (row stride ld_logits elements, 16-byte aligned
+ * rows) and digests_dev are device pointers on the handle's device; either output may be null.
+ * `stream` is a cudaStream_t (null = the handle's own stream).  Returns after the work is
+ * enqueued and completed. */
+int eii_forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int32_t* logits_dev,
+                       int64_t ld_logits, uint64_t* digests_dev, void* stream);
+
+/* Single steps for the drop-in Python Model (host int64 buffers, python/intref.py names). */
+
+/* Model.embed (python/intref.py:163-166): ids [n] -> x [n][576]. */
+int eii_embed(eii_engine* e, const int64_t* ids, int n, int64_t* x_out);
+
+/* Model.block (python/intref.py:192-286) for layer `layer` on n_seq sequences of T rows:
+ * x_in, x_out [n_seq*T][576] (may alias). */
+int eii_block(eii_engine* e, int layer, const int64_t* x_in, int n_seq, int T, int64_t* x_out);
+
+/* Model.rmsnorm (python/intref.py:168-184) with an explicit gain (q int16-valued [576], f):
+ * x [rows][576] int32-valued -> out [rows][576]; bits_out 16 or 32. */
+int eii_rmsnorm(eii_engine* e, const int64_t* x, int rows, const int64_t* gain_q, int gain_f, int f_out,
+                int bits_out, int64_t* out);
+
+/* Final norm + tied logits (python/intref.py:296-300): x [rows][576] -> logits [rows][49152]
+ * int64 (f = 16, no saturation). */
+int eii_logits(eii_engine* e, const int64_t* x, int rows, int64_t* logits);
+
+/* Model.linear (python/intref.py:186-190): out = SAT(RS(acc * m, n + f_in - f_out), bits_out),
+ * acc = a W^T exact.  a [M][K] with values in signed bits_in (16 or 32), W int8 [N][K], m/n [N].
+ * bits_out 64 means no saturation.  out and acc are int64 [M][N]; acc may be null.
+ * K must be a multiple of 32 and <= 1536 (the proven int32 plane-accumulator range);
+ * N a multiple of 16.  Works on any handle (the weights are uploaded per call). */
+int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const int8_t* W, const int64_t* m,
+               const int64_t* n, int N, int f_in, int f_out, int bits_out, int64_t* out, int64_t* acc);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EII_H */

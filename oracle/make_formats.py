@@ -1,0 +1,38 @@
+"""Derive oracle/formats.json from the reference's format proposal (TEST INFRASTRUCTURE).
+
+Runs only where the reference checkout is present (default /root/reference, or the
+EII_REFERENCE environment variable).  It restates Model.fmt (python/intref.py:154-160):
+a site-layer whose class starts with "flagged" is INT32 with f = 31 - k in wide mode,
+every other site is INT16 with f = 15 - k; the final norm output uses f = 15 - k(final_out|30)
+(python/intref.py:296).  The 12 sites are written in model.bin's fmt[24] order
+(python/export_vectors.py:34).  Narrow mode (wide=False) and the residual grid exponents of
+Model._grid (python/intref.py:303-308) are kept too.
+"""
+import json, os, sys
+
+SITES = ("norm1_out", "q_proj", "k_proj", "v_proj", "q_rope", "k_rope", "attn_ctx",
+         "norm2_out", "gate_proj", "up_proj", "silu_gate", "mlp_gated")
+
+
+def main():
+    ref = os.environ.get("EII_REFERENCE", "/root/reference")
+    prop = json.load(open(os.path.join(ref, "results", "scaling_proposal.json")))["sites"]
+    out = {"source": "results/scaling_proposal.json of the reference", "wide": [], "narrow": []}
+    for l in range(30):
+        for mode in ("wide", "narrow"):
+            fm = []
+            for s in SITES:
+                e = prop[f"{s}|{l}"]
+                flagged = e["class"].startswith("flagged")
+                fm += [32, 31 - e["k"]] if (flagged and mode == "wide") else [16, 15 - e["k"]]
+            out[mode].append(fm)
+    out["f_y"] = 15 - prop["final_out|30"]["k"]
+    out["resid_k"] = {s: [prop[f"{s}|{l}"]["k"] for l in range(30)] for s in ("resid_in", "resid_out")}
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "formats.json")
+    with open(path, "w") as f:
+        json.dump(out, f, indent=0)
+    print("wrote", path)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,198 @@
+"""Generate the golden fixtures in tests/golden/ by running the REFERENCE itself.
+
+Runs only in a container that has the reference checkout (default /root/reference, or
+$EII_REFERENCE); the fixtures it writes are committed so the tests never need the reference.
+
+What it does, for the seeded synthetic model of oracle/synth.py:
+  1. imports the reference's python/intref.py and python/common.py, and patches the two loader
+     names intref.load_config / intref.load_weights (imported at python/intref.py:31) and
+     common.load_token_windows (python/common.py:71) so they return the seeded synthetic
+     weights and token table instead of the HF checkpoint and wikitext;
+  2. runs the reference's own python/export_vectors.py (runpy) for the three vector sets of the
+     reference (t24: window 64, 24 tokens; t128: window 64, 128 tokens; t160: window 100,
+     160 tokens, here on the outlier-gain model) and records the size and sha256 of model.bin and
+     of every exported state, like vectors/*/manifest.json;
+  3. runs the reference's scalar C program (oracle/_ref/intref, built by oracle/build_ref.sh)
+     on each set and records its verdict line;
+  4. runs intref.Model.forward on the 64-sequence check subset of the 4096-sequence batch
+     (T=128) and records per-sequence sha256 digests of the int32 logits and last residual;
+  5. runs intref.Model.linear / matmul_exact + rs on seeded activations spanning the full
+     INT16 / INT32 ranges for the four contraction shapes and records digests of acc and out.
+
+    python tests/golden/make_golden.py [--keep DIR] [--skip-subset]
+"""
+import argparse
+import hashlib
+import json
+import os
+import runpy
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, REPO)
+from oracle import synth  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("EII_REFERENCE", "/root/reference")
+SETS = (("t24", 64, 24, False), ("t128", 64, 128, False), ("t160", 100, 160, True))
+SUBSET_SEED = 2
+SUBSET_N = 64
+
+
+def sha256_bytes(b):
+    return hashlib.sha256(b).hexdigest()
+
+
+def sha256_file(p):
+    h = hashlib.sha256()
+    with open(p, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 20), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def import_reference():
+    import torch
+    sys.path.insert(0, os.path.join(REF, "python"))
+    import common
+    import intref
+    return torch, common, intref
+
+
+def patch(torch, common, intref, outlier):
+    W = synth.float_weights(synth.WEIGHT_SEED, outlier)
+    tW = {"embed": torch.from_numpy(W["embed"]), "norm": torch.from_numpy(W["norm"]), "layers": []}
+    for Ly in W["layers"]:
+        tW["layers"].append({k: torch.from_numpy(v) for k, v in Ly.items()})
+    intref.load_config = lambda: {"num_hidden_layers": 30}
+    intref.load_weights = lambda: tW
+    table = synth.token_table()
+    common.load_token_windows = lambda: (table, {})
+
+
+def subset_rows():
+    return sorted(np.random.default_rng(SUBSET_SEED).choice(synth.IDS_ROWS, SUBSET_N, replace=False).tolist())
+
+
+def gemm_cases():
+    """(name, weight source, site-layer for (f_in, bits_in), out format, M) for the sweep."""
+    return [
+        ("q_576x576", ("q", 0), "norm1_out|0", ("q_proj", 0), 512),
+        ("gate_1536x576", ("gate", 11), "norm2_out|11", ("gate_proj", 11), 1000),
+        ("down_576x1536", ("down", 0), "mlp_gated|0", ("resid", 15), 700),
+        ("down16_576x1536", ("down", 3), "mlp_gated|3", ("resid", 15), 512),
+        ("logits_49152x576", ("embed", None), "final_out|30", ("logits", 16), 160),
+    ]
+
+
+def gemm_activations(bits, M, K, seed):
+    rng = np.random.default_rng(seed)
+    lo, hi = -(1 << (bits - 1)), (1 << (bits - 1))
+    a = rng.integers(lo, hi, size=(M, K), dtype=np.int64)
+    a[0, :] = lo          # extreme rows exercise the full range exactly
+    a[1, :] = hi - 1
+    return a
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--keep", default=None, help="directory to keep the exported vector sets in")
+    ap.add_argument("--skip-subset", action="store_true")
+    args = ap.parse_args()
+    torch, common, intref = import_reference()
+    out_root = args.keep or tempfile.mkdtemp(prefix="eii_golden_")
+    refbin = os.path.join(REPO, "oracle", "_ref", "intref")
+    if not os.path.exists(refbin):
+        subprocess.check_call(["sh", os.path.join(REPO, "oracle", "build_ref.sh"), REF])
+    export = os.path.join(REF, "python", "export_vectors.py")
+
+    for name, win, T, outlier in SETS:
+        patch(torch, common, intref, outlier)
+        d = os.path.join(out_root, name)
+        t0 = time.time()
+        argv = sys.argv
+        sys.argv = [export, d, str(win), str(T)]
+        try:
+            runpy.run_path(export, run_name="__main__")
+        finally:
+            sys.argv = argv
+        man = {"window": win, "tokens": T, "model": "outlier" if outlier else "base",
+               "weight_seed": synth.WEIGHT_SEED, "ids_seed": synth.IDS_SEED, "files": {}}
+        for fn in ("model.bin", "ids.i64", "exp_embed.i32", "exp_resid_out.i32", "exp_logits.i32"):
+            p = os.path.join(d, fn)
+            man["files"][fn] = {"bytes": os.path.getsize(p), "sha256": sha256_file(p)}
+        lg = np.fromfile(os.path.join(d, "exp_logits.i32"), dtype=np.int32).reshape(T, -1)
+        rz = np.fromfile(os.path.join(d, "exp_resid_out.i32"), dtype=np.int32).reshape(30, T, -1)
+        man["samples"] = {"logits_row0_first8": lg[0, :8].tolist(), "logits_last_first8": lg[-1, :8].tolist(),
+                          "logits_absmax": int(np.abs(lg.astype(np.int64)).max()),
+                          "resid29_last_first8": rz[29, -1, :8].tolist()}
+        r = subprocess.run([refbin, d], capture_output=True, text=True)
+        man["reference_c"] = {"returncode": r.returncode, "last_line": r.stdout.strip().splitlines()[-1]}
+        man["export_seconds"] = round(time.time() - t0, 1)
+        with open(os.path.join(HERE, f"vectors_{name}.json"), "w") as f:
+            json.dump(man, f, indent=1)
+        print(name, man["reference_c"], man["export_seconds"], "s", flush=True)
+
+    # GEMM sweep fixtures (base model)
+    patch(torch, common, intref, False)
+    M_ = intref.Model(wide=True)
+    cases = []
+    for i, (name, (wname, wl), site_in, (site_out, lo), Mrows) in enumerate(gemm_cases()):
+        if wname == "embed":
+            W = (M_.emb_q, M_.emb_m, M_.emb_n)
+            bits_in, f_in = 16, 15 - M_.prop["final_out|30"]["k"]
+        else:
+            W = M_.layers[wl][wname]
+            s, l = site_in.split("|")
+            bits_in, f_in = M_.fmt(s, int(l))
+        K = W[0].shape[1]
+        a = gemm_activations(bits_in, Mrows, K, seed=100 + i)
+        if site_out in ("resid", "logits"):
+            f_out, bits_out = lo, 64
+            acc = intref.matmul_exact(a, W[0], 1 << (bits_in - 1))
+            out = intref.rs(acc * W[1][None, :], W[2] + f_in - f_out)
+        else:
+            bits_out, f_out = M_.fmt(site_out, lo)
+            out, acc = M_.linear(a, 1 << (bits_in - 1), W, f_in, f_out, bits_out)
+        cases.append({"name": name, "weight": [wname, wl], "bits_in": bits_in, "f_in": f_in,
+                      "f_out": f_out, "bits_out": bits_out, "M": Mrows, "N": int(W[0].shape[0]), "K": int(K),
+                      "act_seed": 100 + i,
+                      "acc_sha256": sha256_bytes(np.ascontiguousarray(acc, dtype=np.int64).tobytes()),
+                      "out_sha256": sha256_bytes(np.ascontiguousarray(out, dtype=np.int64).tobytes()),
+                      "out_first8": np.asarray(out[2, :8]).tolist()})
+        print(name, "done", flush=True)
+    with open(os.path.join(HERE, "gemm_sweep.json"), "w") as f:
+        json.dump({"note": "acc/out digests are over little-endian int64 arrays [M,N]", "cases": cases}, f, indent=1)
+
+    if not args.skip_subset:
+        rows = subset_rows()
+        table = synth.token_table()
+        T = 128
+        seqs = []
+        t0 = time.time()
+        for r in rows:
+            ids = table[r, :T]
+            x = M_.embed(ids)
+            for l in range(M_.L):
+                x = M_.block(l, x)
+            bits_y, f_y = 16, 15 - M_.prop["final_out|30"]["k"]
+            y = M_.rmsnorm(x, M_.final_gain, f_y, bits_y)
+            acc = intref.matmul_exact(y, M_.emb_q, 1 << 15)
+            lg = intref.rs(acc * M_.emb_m[None, :], M_.emb_n + f_y - 16)
+            seqs.append({"row": r, "logits_i32_sha256": sha256_bytes(lg.astype(np.int32).tobytes()),
+                         "resid29_i32_sha256": sha256_bytes(x.astype(np.int32).tobytes()),
+                         "argmax_last": int(lg[-1].argmax())})
+        with open(os.path.join(HERE, "config4_subset.json"), "w") as f:
+            json.dump({"T": T, "subset_seed": SUBSET_SEED, "rows": rows, "sequences": seqs,
+                       "seconds": round(time.time() - t0, 1)}, f, indent=1)
+        print("subset done", round(time.time() - t0, 1), "s")
+    print("vector sets in", out_root)
+
+
+if __name__ == "__main__":
+    main()
