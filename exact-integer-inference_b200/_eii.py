@@ -16,6 +16,7 @@ STATUS_NAMES = {0: "EII_OK", 1: "EII_ERR_ARG", 2: "EII_ERR_IO", 3: "EII_ERR_CUDA
                 5: "EII_ERR_FORMAT"}
 
 VOCAB, D_MODEL, N_LAYERS = 49152, 576, 30
+NUM_KERNEL_KINDS = 10
 
 
 class EiiError(RuntimeError):
@@ -39,6 +40,10 @@ _SIGS = {
     "eii_block": ([_P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
     "eii_rmsnorm": ([_P, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
     "eii_logits": ([_P, _P, ctypes.c_int, _P], ctypes.c_int),
+    "eii_kernel_name": ([ctypes.c_int], ctypes.c_char_p),
+    "eii_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
+    "eii_profile_read": ([_P, ctypes.c_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)],
+                         ctypes.c_int),
     "eii_linear": ([_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
                     ctypes.c_int, ctypes.c_int, _P, _P], ctypes.c_int),
 }
@@ -118,6 +123,18 @@ class Engine:
                                        ctypes.c_void_p(logits_ptr) if logits_ptr else None, ld,
                                        ctypes.c_void_p(digests_ptr) if digests_ptr else None,
                                        ctypes.c_void_p(stream) if stream else None))
+
+    def profile_enable(self, on=True):
+        check(lib().eii_profile_enable(self.h, 1 if on else 0))
+
+    def profile_read(self):
+        """{kernel name: (total ms, launches)} since the last profile_enable."""
+        out = {}
+        for k in range(NUM_KERNEL_KINDS):
+            ms, n = ctypes.c_double(), ctypes.c_int64()
+            check(lib().eii_profile_read(self.h, k, ctypes.byref(ms), ctypes.byref(n)))
+            out[lib().eii_kernel_name(k).decode()] = (ms.value, n.value)
+        return out
 
     def embed(self, ids):
         ids = _c(ids, np.int64).reshape(-1)

@@ -164,6 +164,12 @@ struct eii_engine {
     std::map<int, ActMaps> maps;
     std::vector<void*> weights;
     std::vector<void*> workspace;
+    // optional per-kernel timing (eii_profile_enable): event pairs around each launch
+    bool prof_on = false;
+    std::vector<cudaEvent_t> prof_pool;
+    std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_pending;
+    double prof_ms[EII_NUM_KERNEL_KINDS] = {};
+    int64_t prof_n[EII_NUM_KERNEL_KINDS] = {};
 };
 
 namespace {
@@ -182,6 +188,52 @@ void free_list(std::vector<void*>& v) {
     v.clear();
 }
 
+cudaEvent_t prof_event(eii_engine* e) {
+    if (!e->prof_pool.empty()) {
+        cudaEvent_t ev = e->prof_pool.back();
+        e->prof_pool.pop_back();
+        return ev;
+    }
+    cudaEvent_t ev = nullptr;
+    cudaEventCreate(&ev);
+    return ev;
+}
+
+// Records an event pair around one launch when profiling is on.
+struct ProfScope {
+    eii_engine* e;
+    int kind;
+    cudaStream_t st;
+    cudaEvent_t a = nullptr;
+    ProfScope(eii_engine* e_, int kind_, cudaStream_t st_) : e(e_), kind(kind_), st(st_) {
+        if (e->prof_on) {
+            a = prof_event(e);
+            cudaEventRecord(a, st);
+        }
+    }
+    ~ProfScope() {
+        if (a) {
+            cudaEvent_t b = prof_event(e);
+            cudaEventRecord(b, st);
+            e->prof_pending.push_back({kind, {a, b}});
+        }
+    }
+};
+
+void prof_resolve(eii_engine* e) {
+    for (auto& p : e->prof_pending) {
+        float ms = 0.f;
+        if (cudaEventSynchronize(p.second.second) == cudaSuccess &&
+            cudaEventElapsedTime(&ms, p.second.first, p.second.second) == cudaSuccess) {
+            e->prof_ms[p.first] += ms;
+            e->prof_n[p.first] += 1;
+        }
+        e->prof_pool.push_back(p.second.first);
+        e->prof_pool.push_back(p.second.second);
+    }
+    e->prof_pending.clear();
+}
+
 int free_workspace(eii_engine* e) {
     free_list(e->workspace);
     e->cap_rows = 0;
@@ -190,6 +242,8 @@ int free_workspace(eii_engine* e) {
     e->q = e->k = e->v = nullptr;
     e->logits_ws = nullptr;
     e->logits_ws_rows = 0;
+    e->ids_dev = nullptr;
+    e->ids_cap = 0;
     e->maps.clear();
     return EII_OK;
 }
@@ -249,7 +303,8 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
 }
 
 template <int P, int KIND>
-int launch_gemm(eii_engine* e, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep, cudaStream_t st) {
+int launch_gemm(eii_engine* e, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep, cudaStream_t st,
+                int prof_kind) {
     using C = GemmCfg<P>;
     static int attr_done_device = -1;
     if (attr_done_device != e->device) {
@@ -258,6 +313,7 @@ int launch_gemm(eii_engine* e, const CUtensorMap& A, const CUtensorMap& B, const
     }
     const int tiles = ((ep.M + 127) / 128) * ((ep.N + 127) / 128);
     const int grid = tiles < e->num_sms ? tiles : e->num_sms;
+    ProfScope ps(e, prof_kind, st);
     k_plane_gemm<P, KIND><<<grid, C::THREADS, C::SMEM, st>>>(A, B, ep);
     CK(cudaGetLastError());
     return EII_OK;
@@ -265,15 +321,16 @@ int launch_gemm(eii_engine* e, const CUtensorMap& A, const CUtensorMap& B, const
 
 template <int KIND>
 int launch_gemm_p(eii_engine* e, int P, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep,
-                  cudaStream_t st) {
-    if (P == 2) return launch_gemm<2, KIND>(e, A, B, ep, st);
-    if (P == 4) return launch_gemm<4, KIND>(e, A, B, ep, st);
+                  cudaStream_t st, int prof_kind) {
+    if (P == 2) return launch_gemm<2, KIND>(e, A, B, ep, st, prof_kind);
+    if (P == 4) return launch_gemm<4, KIND>(e, A, B, ep, st, prof_kind);
     return fail(EII_ERR_FORMAT, "unsupported plane count %d", P);
 }
 
 int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, int shift, int bits,
                 uint8_t* planes, int P, int64_t* out64, cudaStream_t st) {
     const int rows_per_block = 8;
+    ProfScope ps(e, EII_K_NORM, st);
     k_rmsnorm<<<(rows + rows_per_block - 1) / rows_per_block, 32 * rows_per_block, 0, st>>>(x, rows, gain, shift, bits,
                                                                                            planes, P, out64);
     CK(cudaGetLastError());
@@ -282,6 +339,7 @@ int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, 
 
 int launch_embed(eii_engine* e, const int64_t* ids, int rows, cudaStream_t st) {
     const int rows_per_block = 8;
+    ProfScope ps(e, EII_K_EMBED, st);
     k_embed<<<(rows + rows_per_block - 1) / rows_per_block, 32 * rows_per_block, 0, st>>>(ids, rows, e->emb_q, e->emb_m,
                                                                                          e->emb_n, e->x, e->err_dev);
     CK(cudaGetLastError());
@@ -300,18 +358,21 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     ep.T = T; ep.q_out = e->q; ep.k_out = e->k; ep.v_out = e->v; ep.rope_c = e->rope_c; ep.rope_s = e->rope_s;
     ep.bits_q = L.q.bits; ep.bits_k = L.k.bits; ep.bits_v = L.v.bits; ep.bits_qr = L.qr.bits; ep.bits_kr = L.kr.bits;
     ep.rope_shift_q = L.rope_shift_q; ep.rope_shift_k = L.rope_shift_k;
-    TRY(launch_gemm<2, EPI_QKV>(e, am->h, L.tm_qkv, ep, st));
+    TRY(launch_gemm<2, EPI_QKV>(e, am->h, L.tm_qkv, ep, st, EII_K_GEMM_QKV));
 
     AttnParams ap{};
     ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;
     ap.M = rows; ap.T = T; ap.shift_s = L.shift_s; ap.shift_c = L.shift_c; ap.bits_c = L.c.bits;
     const int asmem = attn_smem_bytes(T);
-    k_attention<<<nseq * N_KV, ATTN_WARPS * 32, asmem, st>>>(ap);
+    {
+        ProfScope ps(e, EII_K_ATTENTION, st);
+        k_attention<<<nseq * N_KV, ATTN_WARPS * 32, asmem, st>>>(ap);
+    }
     CK(cudaGetLastError());
 
     ep = EpiParams{};
     ep.M = rows; ep.N = D_MODEL; ep.K = D_MODEL; ep.msh = L.msh_o; ep.err = e->err_dev; ep.x = e->x;
-    TRY(launch_gemm_p<EPI_RESID>(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, L.tm_o, ep, st));
+    TRY(launch_gemm_p<EPI_RESID>(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, L.tm_o, ep, st, EII_K_GEMM_O));
 
     TRY(launch_norm(e, e->x, rows, L.ln2, L.norm2_shift, L.h2.bits, e->h_planes, 2, nullptr, st));
 
@@ -319,11 +380,11 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     ep.M = rows; ep.N = 2 * D_FF; ep.K = D_MODEL; ep.msh = L.msh_gu; ep.err = e->err_dev;
     ep.silu = L.silu; ep.bits_g = L.g.bits; ep.bits_u = L.u.bits; ep.gated_shift = L.gated_shift;
     ep.bits_m = L.m.bits; ep.gated_P = L.Pm; ep.gated_planes = e->gated_planes;
-    TRY(launch_gemm<2, EPI_GATEUP>(e, am->h, L.tm_gu, ep, st));
+    TRY(launch_gemm<2, EPI_GATEUP>(e, am->h, L.tm_gu, ep, st, EII_K_GEMM_GATEUP));
 
     ep = EpiParams{};
     ep.M = rows; ep.N = D_MODEL; ep.K = D_FF; ep.msh = L.msh_d; ep.err = e->err_dev; ep.x = e->x;
-    TRY(launch_gemm_p<EPI_RESID>(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, L.tm_d, ep, st));
+    TRY(launch_gemm_p<EPI_RESID>(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, L.tm_d, ep, st, EII_K_GEMM_DOWN));
     return EII_OK;
 }
 
@@ -334,11 +395,12 @@ int run_logits(eii_engine* e, int rows, int32_t* logits, int64_t ld, cudaStream_
     EpiParams ep{};
     ep.M = rows; ep.N = VOCAB; ep.K = D_MODEL; ep.msh = e->msh_logits; ep.err = e->err_dev;
     ep.logits = logits; ep.ld_logits = ld;
-    return launch_gemm<2, EPI_LOGITS>(e, am->h, e->tm_emb, ep, st);
+    return launch_gemm<2, EPI_LOGITS>(e, am->h, e->tm_emb, ep, st, EII_K_GEMM_LOGITS);
 }
 
 int check_device_error(eii_engine* e, cudaStream_t st) {
     CK(cudaStreamSynchronize(st));
+    prof_resolve(e);
     int code = 0;
     CK(cudaMemcpy(&code, e->err_dev, sizeof(int), cudaMemcpyDeviceToHost));
     if (code) {
@@ -585,6 +647,37 @@ const char* eii_last_error(void) { return g_err.c_str(); }
 
 int eii_version(void) { return 100; }
 
+const char* eii_kernel_name(int kind) {
+    static const char* names[EII_NUM_KERNEL_KINDS] = {"embed", "rmsnorm", "gemm_qkv_rope", "attention", "gemm_o_resid",
+                                                     "gemm_gateup_silu", "gemm_down_resid", "gemm_logits", "digest",
+                                                     "gemm_linear"};
+    return (kind >= 0 && kind < EII_NUM_KERNEL_KINDS) ? names[kind] : "";
+}
+
+int eii_profile_enable(eii_engine* e, int on) {
+    if (!e) return fail(EII_ERR_ARG, "engine is null");
+    CK(cudaSetDevice(e->device));
+    if (!e->prof_pending.empty()) {
+        CK(cudaDeviceSynchronize());
+        prof_resolve(e);
+    }
+    e->prof_on = on != 0;
+    for (int i = 0; i < EII_NUM_KERNEL_KINDS; ++i) { e->prof_ms[i] = 0; e->prof_n[i] = 0; }
+    return EII_OK;
+}
+
+int eii_profile_read(eii_engine* e, int kind, double* total_ms, int64_t* launches) {
+    if (!e || kind < 0 || kind >= EII_NUM_KERNEL_KINDS || !total_ms || !launches) return fail(EII_ERR_ARG, "bad arguments");
+    CK(cudaSetDevice(e->device));
+    if (!e->prof_pending.empty()) {
+        CK(cudaDeviceSynchronize());
+        prof_resolve(e);
+    }
+    *total_ms = e->prof_ms[kind];
+    *launches = e->prof_n[kind];
+    return EII_OK;
+}
+
 int eii_open_memory(const void* data, size_t nbytes, int device, eii_engine** out) {
     if (!data) return fail(EII_ERR_ARG, "data is null");
     return open_common(data, nbytes, device, out);
@@ -609,6 +702,8 @@ void eii_close(eii_engine* e) {
     if (!e) return;
     cudaSetDevice(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
+    prof_resolve(e);
+    for (cudaEvent_t ev : e->prof_pool) cudaEventDestroy(ev);
     free_list(e->workspace);
     free_list(e->weights);
     if (e->stream) cudaStreamDestroy(e->stream);
@@ -637,6 +732,7 @@ int eii_forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, 
             const int64_t lld = logits_dev ? ld : VOCAB;
             TRY(run_logits(e, rows, lg, lld, st));
             if (digests_dev) {
+                ProfScope ps(e, EII_K_DIGEST, st);
                 k_digest<<<rows, 256, 0, st>>>(lg, lld, T, rows, reinterpret_cast<unsigned long long*>(digests_dev + s0));
                 CK(cudaGetLastError());
             }
@@ -690,6 +786,7 @@ int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* em
                 rc = fail(EII_ERR_CUDA, "logits download failed");
             if (rc == EII_OK && digests) {
                 cudaMemsetAsync(dig_dev, 0, sizeof(uint64_t) * ns, st);
+                ProfScope ps(e, EII_K_DIGEST, st);
                 k_digest<<<rows, 256, 0, st>>>(e->logits_ws, VOCAB, T, rows, reinterpret_cast<unsigned long long*>(dig_dev));
                 if (cudaGetLastError() != cudaSuccess ||
                     cudaMemcpyAsync(digests + s0, dig_dev, sizeof(uint64_t) * ns, cudaMemcpyDeviceToHost, st) != cudaSuccess)
@@ -783,7 +880,7 @@ static int linear_device(eii_engine* e, const int64_t* a_dev, int M, int K, int 
     EpiParams ep{};
     ep.M = M; ep.N = N; ep.K = K; ep.msh = msh_dev; ep.err = e->err_dev; ep.out64 = out_dev; ep.acc64 = acc_dev;
     ep.bits_out = bits_out;
-    return launch_gemm_p<EPI_LINEAR>(e, P, tmA, tmB, ep, e->stream);
+    return launch_gemm_p<EPI_LINEAR>(e, P, tmA, tmB, ep, e->stream, EII_K_GEMM_LINEAR);
 }
 
 int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const int8_t* W, const int64_t* m,

@@ -92,6 +92,26 @@ int eii_logits(eii_engine* e, const int64_t* x, int rows, int64_t* logits);
 int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const int8_t* W, const int64_t* m,
                const int64_t* n, int N, int f_in, int f_out, int bits_out, int64_t* out, int64_t* acc);
 
+/* Per-kernel timing.  While enabled, every launch of the engine is bracketed by CUDA events on
+ * its stream (this adds a few microseconds per launch, so time whole runs with it off).
+ * eii_profile_enable resets the counters; eii_profile_read returns the summed device time (ms)
+ * and the launch count of one kernel kind.  No reference counterpart: the reference times only
+ * whole runs (c/intref.c:225,256, cuda/intref.cu:283,302-304). */
+#define EII_K_EMBED 0
+#define EII_K_NORM 1
+#define EII_K_GEMM_QKV 2
+#define EII_K_ATTENTION 3
+#define EII_K_GEMM_O 4
+#define EII_K_GEMM_GATEUP 5
+#define EII_K_GEMM_DOWN 6
+#define EII_K_GEMM_LOGITS 7
+#define EII_K_DIGEST 8
+#define EII_K_GEMM_LINEAR 9
+#define EII_NUM_KERNEL_KINDS 10
+const char* eii_kernel_name(int kind);
+int eii_profile_enable(eii_engine* e, int on);
+int eii_profile_read(eii_engine* e, int kind, double* total_ms, int64_t* launches);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,10 +28,13 @@ def main():
             out[mode].append(fm)
     out["f_y"] = 15 - prop["final_out|30"]["k"]
     out["resid_k"] = {s: [prop[f"{s}|{l}"]["k"] for l in range(30)] for s in ("resid_in", "resid_out")}
-    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "formats.json")
-    with open(path, "w") as f:
-        json.dump(out, f, indent=0)
-    print("wrote", path)
+    here = os.path.dirname(os.path.abspath(__file__))
+    # one copy for the oracle, one for the engine package's synthetic-model writer
+    for path in (os.path.join(here, "formats.json"),
+                 os.path.join(os.path.dirname(here), "exact-integer-inference_b200", "formats.json")):
+        with open(path, "w") as f:
+            json.dump(out, f, indent=0)
+        print("wrote", path)
 
 
 if __name__ == "__main__":

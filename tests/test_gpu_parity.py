@@ -1,0 +1,185 @@
+"""Bit-exact parity of the sm_100a engine (through the C ABI) with the reference.
+
+Compared against the committed digests of the reference's own exports (tests/golden) and,
+for finer-grained checks and random cases, against the pinned CPU oracle (oracle/)."""
+import numpy as np
+import pytest
+
+from conftest import golden, sha256_arr
+from oracle import forward as ofw
+from oracle import synth
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def eng(base_model_path):
+    import _eii
+    e = _eii.Engine(base_model_path, 0)
+    yield e
+    e.close()
+
+
+@pytest.fixture(scope="module")
+def eng_outlier(outlier_model_path):
+    import _eii
+    e = _eii.Engine(outlier_model_path, 0)
+    yield e
+    e.close()
+
+
+def oracle_linear(a, bits_in, W, m, n, f_in, f_out, bits_out):
+    acc = ofw.matmul_exact(a, W, 1 << (bits_in - 1))
+    return ofw.sat(ofw.rs(acc * m[None, :], n + f_in - f_out), bits_out), acc
+
+
+def first_diff(got, want):
+    d = np.argwhere(np.asarray(got) != np.asarray(want))
+    return None if d.size == 0 else (tuple(d[0]), int(np.asarray(got)[tuple(d[0])]), int(np.asarray(want)[tuple(d[0])]),
+                                     len(d))
+
+
+# ------------------------------------------------------------------------------ contraction
+def test_linear_single_tile(eng, base_model):
+    """One 128 x 128 output tile, K = 576, INT16 activations over the full range."""
+    q, m, n = base_model["layers"][0]["q"]
+    rng = np.random.default_rng(5)
+    a = rng.integers(-32768, 32768, size=(128, 576), dtype=np.int64)
+    out, acc = eng.linear(a, 16, q[:128], m[:128], n[:128], 13, 10, 16)
+    want_out, want_acc = oracle_linear(a, 16, q[:128], m[:128], n[:128], 13, 10, 16)
+    assert first_diff(acc, want_acc) is None, first_diff(acc, want_acc)
+    assert first_diff(out, want_out) is None
+
+
+def test_linear_sweep_golden(eng, base_model):
+    """Config-5 shapes against the reference's Model.linear digests (tests/golden/gemm_sweep.json)."""
+    from test_oracle_golden import sweep_activations
+    for c in golden("gemm_sweep.json")["cases"]:
+        wname, wl = c["weight"]
+        W = (base_model["emb_q"], base_model["emb_m"], base_model["emb_n"]) if wname == "embed" \
+            else base_model["layers"][wl][wname]
+        a = sweep_activations(c)
+        out, acc = eng.linear(a, c["bits_in"], W[0], W[1], W[2], c["f_in"], c["f_out"], c["bits_out"])
+        assert sha256_arr(acc, np.int64) == c["acc_sha256"], c["name"]
+        assert sha256_arr(out, np.int64) == c["out_sha256"], c["name"]
+
+
+@pytest.mark.parametrize("M,K,N,bits", [(1, 576, 64, 16), (7, 1536, 192, 32), (129, 576, 576, 16),
+                                        (300, 1536, 576, 32), (256, 32, 16, 16), (640, 160, 960, 32)])
+def test_linear_ragged_extremes(eng, M, K, N, bits):
+    """Ragged M/N/K, extreme activations (all -2^(b-1), all 2^(b-1)-1) and weights (+-127, -128)."""
+    rng = np.random.default_rng(M * 7 + K + N + bits)
+    lo, hi = -(1 << (bits - 1)), (1 << (bits - 1))
+    a = rng.integers(lo, hi, size=(M, K), dtype=np.int64)
+    a[0] = lo
+    if M > 1:
+        a[1] = hi - 1
+    W = rng.integers(-128, 128, size=(N, K), dtype=np.int64).astype(np.int8)
+    W[0] = -128
+    if N > 1:
+        W[1] = 127
+    m = rng.integers(1 << 13, (1 << 14) + 1, size=N, dtype=np.int64)
+    n = rng.integers(18, 30, size=N, dtype=np.int64)
+    for bits_out in (16, 32, 64):
+        out, acc = eng.linear(a, bits, W, m, n, 12, 10, bits_out)
+        want_out, want_acc = oracle_linear(a, bits, W, m, n, 12, 10, bits_out)
+        assert first_diff(acc, want_acc) is None, first_diff(acc, want_acc)
+        assert first_diff(out, want_out) is None, (bits_out, first_diff(out, want_out))
+
+
+# ------------------------------------------------------------------------------ steps
+def test_embed_and_rmsnorm(eng, base_model):
+    ids = synth.window_ids(64, 24)
+    x = eng.embed(ids)
+    want = ofw.embed(base_model, ids)
+    assert first_diff(x, want) is None
+    L0 = base_model["layers"][0]
+    F = ofw.fm_unpack(L0["fm"])
+    rng = np.random.default_rng(9)
+    xr = rng.integers(-(1 << 31), 1 << 31, size=(37, 576), dtype=np.int64)
+    xr[0] = 0                      # all-zero row: S = 0, only epsilon
+    xr[1] = -(1 << 31)             # saturated row
+    for x_in in (x, xr):
+        got = eng.rmsnorm(x_in, L0["ln1_q"], L0["ln1_f"], F["h"][1], 16)
+        exp = ofw.rmsnorm(x_in, L0["ln1_q"], L0["ln1_f"], F["h"][1], 16)
+        assert first_diff(got, exp) is None, first_diff(got, exp)
+
+
+@pytest.mark.parametrize("layer", [0, 4, 11, 13, 28])
+def test_block_matches_oracle(eng, base_model, layer):
+    """One decoder block (python/intref.py:192-286) on two sequences; layers chosen for their
+    formats: INT32 attn_ctx (0, 4), INT32 silu_gate (11, 28), INT16 mlp_gated (13)."""
+    T = 24
+    ids = np.stack([synth.window_ids(64, T), synth.window_ids(65, T)])
+    x = ofw.embed(base_model, ids)
+    for l in range(layer):
+        x = ofw.block_batch(base_model, l, x, T)
+    want = ofw.block_batch(base_model, layer, x, T)
+    got = eng.block(layer, x, T)
+    assert first_diff(got, want) is None, first_diff(got, want)
+
+
+# ------------------------------------------------------------------------------ full forward
+def _check_set(e, mdl, name):
+    g = golden(f"vectors_{name}.json")
+    ids = synth.window_ids(g["window"], g["tokens"])
+    out = e.forward(ids, embed=True, resid=True, logits=True, digests=True)
+    files = g["files"]
+    ok_embed = sha256_arr(out["embed"][0], np.int32) == files["exp_embed.i32"]["sha256"]
+    ok_resid = sha256_arr(out["resid"][0], np.int32) == files["exp_resid_out.i32"]["sha256"]
+    ok_logits = sha256_arr(out["logits"][0], np.int32) == files["exp_logits.i32"]["sha256"]
+    if not (ok_embed and ok_resid and ok_logits):
+        ref = ofw.forward(mdl, ids)
+        msg = [f"embed: {first_diff(out['embed'][0], ref['embed'][0])}"]
+        for l in range(30):
+            d = first_diff(out["resid"][0, l], ref["resid"][l, 0])
+            if d is not None:
+                msg.append(f"layer {l}: {d}")
+                break
+        msg.append(f"logits: {first_diff(out['logits'][0], ref['logits'][0].astype(np.int32))}")
+        pytest.fail("; ".join(msg))
+    import _eii
+    assert out["digests"][0] == _eii.digest_logits(out["logits"])[0]
+
+
+def test_forward_t24(eng, base_model):
+    _check_set(eng, base_model, "t24")
+
+
+def test_forward_t128(eng, base_model):
+    _check_set(eng, base_model, "t128")
+
+
+def test_forward_t160_outlier(eng_outlier, outlier_model):
+    _check_set(eng_outlier, outlier_model, "t160")
+
+
+def test_batch_subset_against_reference(eng):
+    """Config 4 in miniature: golden subset sequences embedded in a larger batch of the same
+    4096 x 128 table (other rows in between) must reproduce the reference's per-sequence logits."""
+    g = golden("config4_subset.json")
+    table = synth.token_table()
+    seqs = g["sequences"][:16]
+    rows = sorted(set([s["row"] for s in seqs] + list(range(40))))
+    ids = table[rows, :g["T"]]
+    out = eng.forward(ids, logits=True, digests=True)
+    import _eii
+    dig = _eii.digest_logits(out["logits"])
+    assert np.array_equal(dig, out["digests"])
+    for s in seqs:
+        i = rows.index(s["row"])
+        assert sha256_arr(out["logits"][i], np.int32) == s["logits_i32_sha256"], s["row"]
+        assert int(out["logits"][i, -1].argmax()) == s["argmax_last"]
+
+
+def test_errors_are_reported(eng):
+    import _eii
+    with pytest.raises(_eii.EiiError) as ei:
+        eng.forward(np.array([[0, 49152]], np.int64))
+    assert ei.value.code == _eii.EII_ERR_ARG
+    with pytest.raises(_eii.EiiError) as ei:
+        eng.forward(np.zeros((1, 513), np.int64))
+    assert ei.value.code == _eii.EII_ERR_ARG
+    # the handle stays usable after a rejected call
+    out = eng.forward(synth.window_ids(64, 3), logits=True)
+    assert out["logits"].shape == (1, 3, 49152)
