@@ -18,6 +18,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cerrno>
 #include <cstdarg>
 #include <cstdio>
@@ -303,20 +304,27 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
 }
 
 template <int P, int KIND>
-int launch_gemm(eii_engine* e, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep, cudaStream_t st,
-                int prof_kind) {
+int launch_gemm_raw(int device, int num_sms, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep,
+                    cudaStream_t st) {
     using C = GemmCfg<P>;
-    static int attr_done_device = -1;
-    if (attr_done_device != e->device) {
+    static std::atomic<unsigned long long> attr_done{0};  // one bit per device
+    const unsigned long long bit = (device >= 0 && device < 64) ? (1ull << device) : 0ull;
+    if (!bit || !(attr_done.load() & bit)) {
         CK(cudaFuncSetAttribute(k_plane_gemm<P, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        attr_done_device = e->device;
+        attr_done.fetch_or(bit);
     }
     const int tiles = ((ep.M + 127) / 128) * ((ep.N + 127) / 128);
-    const int grid = tiles < e->num_sms ? tiles : e->num_sms;
-    ProfScope ps(e, prof_kind, st);
+    const int grid = tiles < num_sms ? tiles : num_sms;
     k_plane_gemm<P, KIND><<<grid, C::THREADS, C::SMEM, st>>>(A, B, ep);
     CK(cudaGetLastError());
     return EII_OK;
+}
+
+template <int P, int KIND>
+int launch_gemm(eii_engine* e, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep, cudaStream_t st,
+                int prof_kind) {
+    ProfScope ps(e, prof_kind, st);
+    return launch_gemm_raw<P, KIND>(e->device, e->num_sms, A, B, ep, st);
 }
 
 template <int KIND>
