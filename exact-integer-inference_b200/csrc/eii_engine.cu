@@ -25,6 +25,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -949,3 +950,96 @@ int eii_logits(eii_engine* e, const int64_t* x, int rows, int64_t* logits) {
 }
 
 }  // extern "C"
+
+// =========================================================================== allocation-free linear
+// eii_linear_noalloc: the byte-plane linear of eii_linear for callers that must not allocate device
+// memory.  Its scratch (the activation byte planes, the per-column (m, shift) table and the error
+// word) lives in the file-scope __device__ arrays below, which every GPU that loads this library
+// holds until the process exits.  Host code cannot use these names as device addresses; the
+// addresses come from cudaGetSymbolAddress, once per device, on the first call made on that device.
+namespace {
+
+constexpr size_t kNoAllocPlaneBytes = EII_NOALLOC_PLANE_BYTES;
+constexpr int kNoAllocMaxN = EII_NOALLOC_MAX_N;
+
+__device__ __align__(256) uint8_t g_noalloc_planes[kNoAllocPlaneBytes];
+__device__ __align__(256) int2 g_noalloc_msh[kNoAllocMaxN];
+__device__ __align__(256) int g_noalloc_err[64];
+
+struct NoAllocDevice {
+    bool ready = false;
+    uint8_t* planes = nullptr;
+    int2* msh = nullptr;
+    int* err = nullptr;
+    int num_sms = 0;
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc[64];
+
+// Per-device set-up: resolve the device addresses of the scratch arrays with that device current.
+int noalloc_setup(int dev, NoAllocDevice** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocDevice& d = g_noalloc[dev];
+    if (!d.ready) {
+        int major = 0;
+        CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+        if (major != 10) return fail(EII_ERR_CUDA, "device %d is not sm_100", dev);
+        CK(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.planes), g_noalloc_planes));
+        CK(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.msh), g_noalloc_msh));
+        CK(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err), g_noalloc_err));
+        CK(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev));
+        d.ready = true;
+    }
+    *out = &d;
+    return EII_OK;
+}
+
+__global__ void k_msh_from_mn(const int64_t* __restrict__ m, const int64_t* __restrict__ n, int N, int dshift,
+                              int2* __restrict__ msh) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < N; j += gridDim.x * blockDim.x)
+        msh[j] = make_int2(static_cast<int>(m[j]), static_cast<int>(n[j] + dshift));
+}
+
+}  // namespace
+
+extern "C" int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_in, const int8_t* w_dev,
+                                  const int64_t* m_dev, const int64_t* n_dev, int N, int f_in, int f_out,
+                                  int bits_out, int64_t* out_dev, int64_t* acc_dev, void* stream) {
+    if (!a_dev || !w_dev || !m_dev || !n_dev || !out_dev) return fail(EII_ERR_ARG, "null argument to eii_linear_noalloc");
+    if (M < 1 || K < 32 || K > 1536 || K % 32 != 0) return fail(EII_ERR_ARG, "K must be a multiple of 32 in [32, 1536] (got %d)", K);
+    if (N < 16 || N % 16 != 0) return fail(EII_ERR_ARG, "N must be a positive multiple of 16 (got %d)", N);
+    if (bits_in != 16 && bits_in != 32) return fail(EII_ERR_ARG, "bits_in must be 16 or 32 (got %d)", bits_in);
+    if (bits_out < 2 || bits_out > 64) return fail(EII_ERR_ARG, "bits_out %d out of range", bits_out);
+    const int P = bits_in / 8;
+    if ((size_t)P * M * K > kNoAllocPlaneBytes)
+        return fail(EII_ERR_ARG, "eii_linear_noalloc: %d planes x M=%d x K=%d = %zu bytes exceeds the static scratch of %zu bytes",
+                    P, M, K, (size_t)P * M * K, kNoAllocPlaneBytes);
+    if (N > kNoAllocMaxN) return fail(EII_ERR_ARG, "eii_linear_noalloc: N=%d exceeds the maximum of %d", N, kNoAllocMaxN);
+    if (reinterpret_cast<uintptr_t>(w_dev) & 15) return fail(EII_ERR_ARG, "w_dev must be 16-byte aligned");
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(EII_ERR_ARG, "device %d out of range", dev);
+    NoAllocDevice* d;
+    TRY(noalloc_setup(dev, &d));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    CK(cudaMemsetAsync(d->err, 0, sizeof(int), st));
+    k_msh_from_mn<<<(N + 255) / 256, 256, 0, st>>>(m_dev, n_dev, N, f_in - f_out, d->msh);
+    CK(cudaGetLastError());
+    const int64_t count = (int64_t)M * K;
+    k_split_planes<<<(unsigned)((count + 255) / 256 < 4096 ? (count + 255) / 256 : 4096), 256, 0, st>>>(a_dev, count, P,
+                                                                                                        count, d->planes);
+    CK(cudaGetLastError());
+    CUtensorMap tmA, tmB;
+    TRY(map_planes(&tmA, d->planes, K, M, P));
+    TRY(map_2d(&tmB, w_dev, K, N));
+    EpiParams ep{};
+    ep.M = M; ep.N = N; ep.K = K; ep.msh = d->msh; ep.err = d->err; ep.out64 = out_dev; ep.acc64 = acc_dev;
+    ep.bits_out = bits_out;
+    if (P == 2) TRY(launch_gemm_raw<2, EPI_LINEAR>(dev, d->num_sms, tmA, tmB, ep, st));
+    else TRY(launch_gemm_raw<4, EPI_LINEAR>(dev, d->num_sms, tmA, tmB, ep, st));
+    int code = 0;
+    CK(cudaMemcpyAsync(&code, d->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (code) return fail(EII_ERR_DEVICE, "kernel reported error %d (bounded wait timed out)", code);
+    return EII_OK;
+}

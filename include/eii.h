@@ -92,6 +92,31 @@ int eii_logits(eii_engine* e, const int64_t* x, int rows, int64_t* logits);
 int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const int8_t* W, const int64_t* m,
                const int64_t* n, int N, int f_in, int f_out, int bits_out, int64_t* out, int64_t* acc);
 
+/* Allocation-free linear: the same contraction and requantisation as eii_linear, for callers that
+ * must not allocate device memory -- code whose device memory is owned by another allocator (a
+ * framework or serving runtime that reserved the GPU up front) or that cannot afford the implicit
+ * synchronisation of cudaMalloc/cudaFree in a latency-critical loop.  It calls no cudaMalloc,
+ * cudaFree or other allocating routine and needs no engine handle.  No counterpart in the
+ * reference.
+ *   All pointers are device pointers on the CURRENT device: a_dev int64 [M][K] (values within
+ *   signed bits_in, 16 or 32), w_dev int8 [N][K] (16-byte aligned), m_dev and n_dev int64 [N],
+ *   out_dev int64 [M][N], acc_dev int64 [M][N] or null.  `stream` is a cudaStream_t (null = the
+ *   legacy default stream); the call returns after the work on it has finished.
+ *   Scratch: the activation byte planes, the per-column multiplier/shift table and an error word
+ *   live in fixed __device__ arrays of this library (about 16.4 MB that every GPU loading the
+ *   library holds until the process exits).  Limits: (bits_in / 8) * M * K <= EII_NOALLOC_PLANE_BYTES,
+ *   N <= EII_NOALLOC_MAX_N, K a multiple of 32 up to 1536, N a multiple of 16; larger sizes are
+ *   rejected with EII_ERR_ARG.
+ *   The first call on a device resolves the scratch addresses for that device (cudaGetSymbolAddress),
+ *   so make that first call before any stream capture.  Every call shares the same scratch: calls
+ *   that overlap on the GPU (different streams or threads at the same time) race and must be
+ *   serialised by the caller. */
+#define EII_NOALLOC_PLANE_BYTES (16u * 1024u * 1024u)
+#define EII_NOALLOC_MAX_N 49152
+int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_in, const int8_t* w_dev, const int64_t* m_dev,
+                       const int64_t* n_dev, int N, int f_in, int f_out, int bits_out, int64_t* out_dev,
+                       int64_t* acc_dev, void* stream);
+
 /* Per-kernel timing.  While enabled, every launch of the engine is bracketed by CUDA events on
  * its stream (this adds a few microseconds per launch, so time whole runs with it off).
  * eii_profile_enable resets the counters; eii_profile_read returns the summed device time (ms)
