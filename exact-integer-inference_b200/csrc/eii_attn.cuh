@@ -1,0 +1,292 @@
+// Integer causal attention on tcgen05 kind::i8 for sequences of T <= 128 tokens.
+//
+// One CTA per (sequence, KV group): the group's K and V and its three query heads are split into
+// byte planes in shared memory (128-byte swizzled K-major tiles, the layout TMA would write), and
+// for each head:
+//   S  = Q K^T  as three int32 TMEM accumulators over the 64-dim head:
+//        D0 = q0.k0, D1 = q1.k0 + q0.k1, D2 = q1.k1      (q0,k0 u8 low bytes, q1,k1 s8 top bytes)
+//        S = 65536 D2 + 256 D1 + D0 exactly (|partial sums| <= 64 * 255 * 255 < 2^31).
+//   softmax per query row (one thread per row), exactly as python/intref.py:239-246:
+//        s = SAT16(RS(S, shift_s)) for j <= i, rowmax, e = E[rowmax - s] (0 beyond DMAX),
+//        Z = sum e, P = floor((e 65536 + floor(Z/2)) / Z) in [0, 65536]; the division by the
+//        row-invariant Z is a double estimate corrected with integer remainders.
+//        P = 65536 * [P == 65536] + 256 p1 + p0; the two low bytes are written as u8 planes and
+//        the (at most one) P == 65536 key of a row is added back in the epilogue.
+//   ctx = P V   as three TMEM accumulators over the T keys (V transposed, K-major):
+//        C0 = p0.v0, C1 = p1.v0 + p0.v1, C2 = p1.v1 (|partial sums| <= 128 * 255 * 255 < 2^31)
+//        ctx = SAT(RS(65536 C2 + 256 C1 + C0 + 65536 v[j*], shift_c), bits_c) -> byte planes.
+// (python/intref.py:227-254, c/intref.c:160-187.)
+#pragma once
+#include <cstdint>
+
+#include "eii_gemm.cuh"
+#include "eii_int.cuh"
+#include "eii_kernels.cuh"
+#include "eii_ptx.cuh"
+
+namespace eii {
+
+constexpr int ATTN_TC_THREADS = 512;   // 16 warps: warp w owns TMEM lane quadrant w % 4 and key/dim block w / 4
+constexpr int ATTN_TC_TILE = 128 * 128;  // one 128 x 128-byte swizzled tile
+// smem: Q (3 tiles) | K (1) | V^T planes (2 x 64 rows x 128 B = 1 tile) | P planes (2 tiles) | E |
+//       row max [4][128] int32 | row sum [4][128] int64 | j* [128] int32 | barrier, TMEM slot, abort
+constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + (DMAX + 1 + 3) * 4 + 4 * 128 * 4 + 4 * 128 * 8 + 128 * 4 + 64;
+
+// Byte offset of byte b of row r inside a 128-byte-row tile with the 128-byte swizzle.
+__device__ __forceinline__ int sw128(int r, int b) { return r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15); }
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// floor((e * 65536 + floor(Z/2)) / Z) for 0 <= e <= 2^30, 2^30 <= Z < 2^40: double estimate, then
+// integer-remainder correction (the estimate is within one of the quotient, which is < 2^17 + 1).
+__device__ __forceinline__ int64_t prob_q16(int64_t e, int64_t Z, int64_t halfZ, double rz) {
+    const int64_t n = e * 65536 + halfZ;
+    int64_t p = static_cast<int64_t>(static_cast<double>(n) * rz);
+    int64_t r = n - p * Z;
+    if (r < 0) { --p; r += Z; }
+    if (r < 0) { --p; r += Z; }
+    if (r >= Z) { ++p; r -= Z; }
+    if (r >= Z) { ++p; }
+    return p;
+}
+
+__global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams ap, int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* Qs = sm;                       // 3 tiles: row i = [q0 bytes 0..63 | q1 bytes 64..127]
+    uint8_t* Ks = sm + 3 * ATTN_TC_TILE;    // row j = [k0 | k1]
+    uint8_t* VT = sm + 4 * ATTN_TC_TILE;    // plane p at VT + p * 8192: row d, byte j
+    uint8_t* Ps = sm + 5 * ATTN_TC_TILE;    // plane p at Ps + p * ATTN_TC_TILE: row i, byte j
+    int32_t* E = reinterpret_cast<int32_t*>(sm + 7 * ATTN_TC_TILE);
+    int32_t* red_max = E + DMAX + 1 + 3;                                  // [4][128]
+    int64_t* red_z = reinterpret_cast<int64_t*>(red_max + 4 * 128);      // [4][128]
+    int32_t* jstar_s = reinterpret_cast<int32_t*>(red_z + 4 * 128);      // [128]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(jstar_s + 128);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int T = ap.T;
+    const int seq = blockIdx.x / N_KV, g = blockIdx.x % N_KV;
+    const int64_t row0 = static_cast<int64_t>(seq) * T;
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    const int quad = warp & 3, kb = warp >> 2;  // rows 32 quad .. +31, key block / dim block kb
+    const int i = quad * 32 + lane;             // query row of this thread (TMEM lane)
+
+    if (warp == 0) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+    if (tid == 0) { mbar_init(bar, 1); *abort = 0; fence_mbar_init(); }
+
+    // ---- stage K, Q (3 heads) and V^T as byte planes; rows/keys >= T are zero
+    for (int idx = tid; idx < 128 * 4 * 4; idx += ATTN_TC_THREADS) {
+        const int r = idx / 16, c = (idx / 4) % 4, which = idx % 4;  // which: 0..2 = q head, 3 = k
+        uint8_t lo[16], hi[16];
+        if (r < T) {
+            const int16_t* src = which < 3 ? ap.q + (row0 + r) * D_MODEL + (g * 3 + which) * 64 + c * 16
+                                           : ap.k + (row0 + r) * 192 + g * 64 + c * 16;
+            const int4 a = reinterpret_cast<const int4*>(src)[0], b = reinterpret_cast<const int4*>(src)[1];
+            const int16_t* v = reinterpret_cast<const int16_t*>(&a);
+            const int16_t* w = reinterpret_cast<const int16_t*>(&b);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                lo[u] = static_cast<uint8_t>(v[u] & 0xFF); hi[u] = static_cast<uint8_t>((v[u] >> 8) & 0xFF);
+                lo[8 + u] = static_cast<uint8_t>(w[u] & 0xFF); hi[8 + u] = static_cast<uint8_t>((w[u] >> 8) & 0xFF);
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < 16; ++u) lo[u] = hi[u] = 0;
+        }
+        uint8_t* tile = which < 3 ? Qs + which * ATTN_TC_TILE : Ks;
+        *reinterpret_cast<uint4*>(tile + sw128(r, c * 16)) = *reinterpret_cast<uint4*>(lo);
+        *reinterpret_cast<uint4*>(tile + sw128(r, 64 + c * 16)) = *reinterpret_cast<uint4*>(hi);
+    }
+    {   // V^T: thread (j, dim quarter) scatters key j's 16 values into column j of both planes
+        const int j = tid & 127, dq = tid >> 7;
+        int16_t v[16];
+        if (j < T) {
+            const int4* src = reinterpret_cast<const int4*>(ap.v + (row0 + j) * 192 + g * 64 + dq * 16);
+            *reinterpret_cast<int4*>(&v[0]) = src[0];
+            *reinterpret_cast<int4*>(&v[8]) = src[1];
+        } else {
+#pragma unroll
+            for (int d = 0; d < 16; ++d) v[d] = 0;
+        }
+#pragma unroll
+        for (int d = 0; d < 16; ++d) {
+            VT[sw128(dq * 16 + d, j)] = static_cast<uint8_t>(v[d] & 0xFF);
+            VT[8192 + sw128(dq * 16 + d, j)] = static_cast<uint8_t>((v[d] >> 8) & 0xFF);
+        }
+    }
+    for (int u = tid; u <= DMAX; u += ATTN_TC_THREADS) E[u] = ap.exp_tab[u];
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    uint32_t phase = 0;
+    const uint32_t sK = smem_u32(Ks), sV0 = smem_u32(VT), sV1 = smem_u32(VT + 8192);
+    const uint32_t sP0 = smem_u32(Ps), sP1 = smem_u32(Ps + ATTN_TC_TILE);
+    // key block kb holds keys 32 kb .. 32 kb + 31; it has unmasked keys for this quadrant iff kb <= quad
+    const bool active = kb <= quad;
+
+    for (int h = 0; h < 3; ++h) {
+        // ---- S = Q_h K^T (M = 128 queries, N = 128 keys, K = 64 dims per plane pair)
+        if (tid == 0) {
+            const uint32_t sQ = smem_u32(Qs + h * ATTN_TC_TILE);
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks) {
+                const uint32_t qlo = sQ + ks * 32, qhi = sQ + 64 + ks * 32, klo = sK + ks * 32, khi = sK + 64 + ks * 32;
+                const uint32_t acc = ks > 0 ? 1u : 0u;
+                mma_i8(tmem + 0, smem_desc_sw128(qlo), smem_desc_sw128(klo), idesc_i8(false, false, 128), acc);
+                mma_i8(tmem + 128, smem_desc_sw128(qhi), smem_desc_sw128(klo), idesc_i8(true, false, 128), acc);
+                mma_i8(tmem + 128, smem_desc_sw128(qlo), smem_desc_sw128(khi), idesc_i8(false, true, 128), 1u);
+                mma_i8(tmem + 256, smem_desc_sw128(qhi), smem_desc_sw128(khi), idesc_i8(true, true, 128), acc);
+            }
+            tc_commit(bar);
+        }
+        if (tid < 128) jstar_s[tid] = -1;
+        if (!__syncthreads_and(mbar_wait(bar, phase, abort, err, ERR_TIMEOUT_ATTN))) break;
+        phase ^= 1;
+        tc_fence_after();
+
+        // ---- pass 1: scores of my 32 keys, partial row max
+        uint32_t sp[16];  // s_j as int16 pairs, j = 32 kb + 0..31
+        int32_t lmax = INT32_MIN;
+        if (active) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int col = kb * 32 + c * 16;
+                uint32_t d0[16], d1[16], d2[16];
+                tmem_ld16(tq + col, d0);
+                tmem_ld16(tq + 128 + col, d1);
+                tmem_ld16(tq + 256 + col, d2);
+                tmem_wait_ld();
+                tmem_launder(d0); tmem_launder(d1); tmem_launder(d2);
+#pragma unroll
+                for (int q = 0; q < 16; q += 2) {
+                    int32_t s2[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int64_t S = static_cast<int64_t>(static_cast<int32_t>(d2[q + u])) * 65536 +
+                                          static_cast<int64_t>(static_cast<int32_t>(d1[q + u])) * 256 +
+                                          static_cast<int64_t>(static_cast<int32_t>(d0[q + u]));
+                        s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
+                        if (col + q + u <= i) lmax = max(lmax, s2[u]);
+                    }
+                    sp[(c * 16 + q) / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
+                }
+            }
+        }
+        red_max[kb * 128 + i] = lmax;
+        __syncthreads();
+        int32_t rowmax = red_max[i];
+#pragma unroll
+        for (int b = 1; b < 4; ++b) rowmax = max(rowmax, red_max[b * 128 + i]);
+
+        // ---- pass 2: partial Z
+        int64_t lz = 0;
+        if (active) {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) {
+                const int j = kb * 32 + q;
+                const int32_t s = static_cast<int16_t>((q & 1) ? (sp[q / 2] >> 16) : (sp[q / 2] & 0xFFFF));
+                const int32_t dd = rowmax - s;
+                if (j <= i && dd <= DMAX) lz += E[dd];
+            }
+        }
+        red_z[kb * 128 + i] = lz;
+        __syncthreads();
+        const int64_t Z = red_z[i] + red_z[128 + i] + red_z[256 + i] + red_z[384 + i];
+
+        // ---- pass 3: probabilities of my keys -> u8 planes of P mod 65536 (+ the P == 65536 key)
+        {
+            const int64_t halfZ = Z / 2;
+            const double rz = Z > 0 ? 1.0 / static_cast<double>(Z) : 0.0;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint8_t b0[16], b1[16];
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    const int qq = c * 16 + q;
+                    const int j = kb * 32 + qq;
+                    int64_t p = 0;
+                    if (active && i < T) {
+                        const int32_t s = static_cast<int16_t>((qq & 1) ? (sp[qq / 2] >> 16) : (sp[qq / 2] & 0xFFFF));
+                        const int32_t dd = rowmax - s;
+                        if (j <= i && dd <= DMAX) p = prob_q16(E[dd], Z, halfZ, rz);
+                    }
+                    if (p == 65536) jstar_s[i] = j;
+                    b0[q] = static_cast<uint8_t>(p & 0xFF);
+                    b1[q] = static_cast<uint8_t>((p >> 8) & 0xFF);
+                }
+                const int byte = kb * 32 + c * 16;
+                *reinterpret_cast<uint4*>(Ps + sw128(i, byte)) = *reinterpret_cast<uint4*>(b0);
+                *reinterpret_cast<uint4*>(Ps + ATTN_TC_TILE + sw128(i, byte)) = *reinterpret_cast<uint4*>(b1);
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+
+        // ---- ctx = P V (M = 128 queries, N = 64 dims, K = 128 keys); reuses the S columns
+        if (tid == 0) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                const uint32_t acc = ks > 0 ? 1u : 0u;
+                const uint64_t p0 = smem_desc_sw128(sP0 + ks * 32), p1 = smem_desc_sw128(sP1 + ks * 32);
+                const uint64_t v0 = smem_desc_sw128(sV0 + ks * 32), v1 = smem_desc_sw128(sV1 + ks * 32);
+                mma_i8(tmem + 0, p0, v0, idesc_i8(false, false, 64), acc);
+                mma_i8(tmem + 64, p1, v0, idesc_i8(false, false, 64), acc);
+                mma_i8(tmem + 64, p0, v1, idesc_i8(false, true, 64), 1u);
+                mma_i8(tmem + 128, p1, v1, idesc_i8(false, true, 64), acc);
+            }
+            tc_commit(bar);
+        }
+        if (!__syncthreads_and(mbar_wait(bar, phase, abort, err, ERR_TIMEOUT_ATTN))) break;
+        phase ^= 1;
+        tc_fence_after();
+        {   // epilogue: rows of my quadrant, dims 16 kb .. 16 kb + 15
+            const int hh = g * 3 + h;
+            const int col = kb * 16;
+            uint32_t c0[16], c1[16], c2[16];
+            tmem_ld16(tq + col, c0);
+            tmem_ld16(tq + 64 + col, c1);
+            tmem_ld16(tq + 128 + col, c2);
+            tmem_wait_ld();
+            tmem_launder(c0); tmem_launder(c1); tmem_launder(c2);
+            if (i < T) {
+                const int js = jstar_s[i];
+                int32_t out[16];
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    const int d = col + q;
+                    int64_t a = static_cast<int64_t>(static_cast<int32_t>(c2[q])) * 65536 +
+                                static_cast<int64_t>(static_cast<int32_t>(c1[q])) * 256 +
+                                static_cast<int64_t>(static_cast<int32_t>(c0[q]));
+                    if (js >= 0) {
+                        const int32_t vj = static_cast<int32_t>(VT[sw128(d, js)]) |
+                                           (static_cast<int32_t>(static_cast<int8_t>(VT[8192 + sw128(d, js)])) << 8);
+                        a += static_cast<int64_t>(vj) * 65536;
+                    }
+                    out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
+                }
+                for (int p = 0; p < ap.P; ++p) {
+                    uint8_t b[16];
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) b[q] = plane_byte(out[q], p);
+                    *reinterpret_cast<uint4*>(ap.ctx_planes + (static_cast<int64_t>(p) * ap.M + row0 + i) * D_MODEL +
+                                              hh * 64 + col) = *reinterpret_cast<uint4*>(b);
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(*tmem_slot, 512);
+}
+
+}  // namespace eii

@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "eii.h"
+#include "eii_attn.cuh"
 #include "eii_gemm.cuh"
 #include "eii_kernels.cuh"
 
@@ -167,6 +168,7 @@ struct eii_engine {
     std::vector<void*> weights;
     std::vector<void*> workspace;
     // optional per-kernel timing (eii_profile_enable): event pairs around each launch
+    bool force_cuda_core_attention = false;  // EII_ATTENTION=cuda_core selects the CUDA-core kernel for T <= 128
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_pool;
     std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_pending;
@@ -372,10 +374,12 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     AttnParams ap{};
     ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;
     ap.M = rows; ap.T = T; ap.shift_s = L.shift_s; ap.shift_c = L.shift_c; ap.bits_c = L.c.bits;
-    const int asmem = attn_smem_bytes(T);
     {
         ProfScope ps(e, EII_K_ATTENTION, st);
-        k_attention<<<nseq * N_KV, ATTN_WARPS * 32, asmem, st>>>(ap);
+        if (T <= 128 && !e->force_cuda_core_attention)
+            k_attention_tc<<<nseq * N_KV, ATTN_TC_THREADS, ATTN_TC_SMEM, st>>>(ap, e->err_dev);
+        else
+            k_attention<<<nseq * N_KV, ATTN_WARPS * 32, attn_smem_bytes(T), st>>>(ap);
     }
     CK(cudaGetLastError());
 
@@ -623,9 +627,12 @@ int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
     if (rc == EII_OK) rc = dalloc(e->weights, &e->err_dev, 1);
     if (rc == EII_OK && cudaMemset(e->err_dev, 0, sizeof(int)) != cudaSuccess) rc = fail(EII_ERR_CUDA, "memset failed");
     if (rc == EII_OK) rc = load_model(e, static_cast<const uint8_t*>(data), nbytes);
-    if (rc == EII_OK && cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             attn_smem_bytes(ROPE_POS)) != cudaSuccess)
+    if (rc == EII_OK && (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              attn_smem_bytes(ROPE_POS)) != cudaSuccess ||
+                         cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              ATTN_TC_SMEM) != cudaSuccess))
         rc = fail(EII_ERR_CUDA, "attention smem attribute failed");
+    if (const char* a = getenv("EII_ATTENTION")) e->force_cuda_core_attention = strcmp(a, "cuda_core") == 0;
     if (rc != EII_OK) {
         eii_close(e);
         return rc;

@@ -36,6 +36,7 @@ enum : int {
     ERR_TIMEOUT_MMA_ACC = 103,
     ERR_TIMEOUT_EPI = 104,
     ERR_TIMEOUT_DRAIN = 105,
+    ERR_TIMEOUT_ATTN = 106,
 };
 
 struct EpiParams {

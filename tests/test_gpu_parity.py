@@ -183,3 +183,14 @@ def test_errors_are_reported(eng):
     # the handle stays usable after a rejected call
     out = eng.forward(synth.window_ids(64, 3), logits=True)
     assert out["logits"].shape == (1, 3, 49152)
+
+
+def test_forward_t128_cuda_core_attention(base_model, base_model_path, monkeypatch):
+    """The CUDA-core attention kernel (used for T > 128) is also exact for T <= 128."""
+    import _eii
+    monkeypatch.setenv("EII_ATTENTION", "cuda_core")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        _check_set(e, base_model, "t128")
+    finally:
+        e.close()
