@@ -35,7 +35,6 @@ constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + (DMAX + 1 + 3) * 4 + 4 * 
 // Byte offset of byte b of row r inside a 128-byte-row tile with the 128-byte swizzle.
 __device__ __forceinline__ int sw128(int r, int b) { return r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15); }
 
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // floor((e * 65536 + floor(Z/2)) / Z) for 0 <= e <= 2^30, 2^30 <= Z < 2^40: double estimate, then
 // integer-remainder correction (the estimate is within one of the quotient, which is < 2^17 + 1).

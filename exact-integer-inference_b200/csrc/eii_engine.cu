@@ -81,13 +81,18 @@ struct LayerDev {
     int f_m, Pc, Pm;
     int norm1_shift, norm2_shift, rope_shift_q, rope_shift_k, shift_s, shift_c, gated_shift;
     int32_t *ln1, *ln2, *silu;
+    void* silu_neg;  // compact SiLU table (negative half, dense range) or null
+    int silu_lo, silu_count, silu_wide, silu_d;
+    int fast_qkv, fast_o, fast_gu, fast_d;  // fast requantisation path applies (see EpiParams::fast)
     int8_t *w_qkv, *w_o, *w_gu, *w_d;
     int2 *msh_qkv, *msh_o, *msh_gu, *msh_d;
-    CUtensorMap tm_qkv, tm_o, tm_gu, tm_d;
+    CUtensorMap tm_qkv, tm_o, tm_gu, tm_d, tm_o64, tm_d64;  // *64: 64-row boxes for 4-plane GEMMs
 };
 
 struct ActMaps {
     CUtensorMap h, ctx2, ctx4, gated2, gated4;
+    CUtensorMap x32, x16;  // residual tiles for the O/down epilogues (32 or 16 columns x 32 rows)
+    CUtensorMap q, k, v;   // RoPE'd q/k and v stores of the QKV epilogue (16 int16 x 32 rows)
 };
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -108,13 +113,14 @@ int get_encode(EncodeTiledFn* fn) {
     return EII_OK;
 }
 
-// K-major uint8 tile maps with 128-byte swizzle, 128 x 128-byte boxes.
-int map_2d(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows) {
+// K-major uint8 tile maps with 128-byte swizzle: boxes of 128 bytes x box_rows rows (the GEMM's
+// N tile: 128 for two activation planes, 64 for four).
+int map_2d(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows = 128) {
     EncodeTiledFn enc;
     TRY(get_encode(&enc));
     cuuint64_t dims[2] = {K, rows};
     cuuint64_t strides[1] = {K};
-    cuuint32_t box[2] = {128, 128};
+    cuuint32_t box[2] = {128, box_rows};
     cuuint32_t es[2] = {1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -123,6 +129,27 @@ int map_2d(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows) {
                                        (unsigned long long)K, (unsigned long long)rows, (int)r);
     return EII_OK;
 }
+// Row-major 2-D maps for the epilogue's TMA tile stores/loads: elements of elem_bytes, `cols` per row,
+// row pitch `pitch_bytes`, box of box_cols x box_rows with the swizzle matching box_cols * elem_bytes.
+int map_out(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes, uint64_t cols,
+            uint64_t rows, uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows) {
+    EncodeTiledFn enc;
+    TRY(get_encode(&enc));
+    const uint32_t span = box_cols * elem_bytes;
+    const CUtensorMapSwizzle sw = span == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : span == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                  : span == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {pitch_bytes};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(EII_ERR_CUDA, "cuTensorMapEncodeTiled(out cols=%llu rows=%llu) failed: %d",
+                                       (unsigned long long)cols, (unsigned long long)rows, (int)r);
+    return EII_OK;
+}
+
 int map_planes(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint64_t planes) {
     EncodeTiledFn enc;
     TRY(get_encode(&enc));
@@ -150,6 +177,7 @@ struct eii_engine {
     CUtensorMap tm_emb;
     int32_t* final_q = nullptr;
     int final_f = 0, f_y = 0, final_shift = 0;
+    int fast_logits = 0;
     int32_t *exp_tab = nullptr, *rope_c = nullptr, *rope_s = nullptr;
     LayerDev L[N_LAYERS];
     // chunk workspace
@@ -300,6 +328,11 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
         TRY(map_planes(&am.ctx4, e->ctx_planes, D_MODEL, rows, 4));
         TRY(map_planes(&am.gated2, e->gated_planes, D_FF, rows, 2));
         TRY(map_planes(&am.gated4, e->gated_planes, D_FF, rows, 4));
+        TRY(map_out(&am.x32, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 32, 32));
+        TRY(map_out(&am.x16, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 16, 32));
+        TRY(map_out(&am.q, e->q, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, D_MODEL, rows, D_MODEL * 2, 16, 32));
+        TRY(map_out(&am.k, e->k, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, 192, rows, 192 * 2, 16, 32));
+        TRY(map_out(&am.v, e->v, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, 192, rows, 192 * 2, 16, 32));
         it = e->maps.emplace(rows, am).first;
     }
     *out = &it->second;
@@ -307,34 +340,35 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
 }
 
 template <int P, int KIND>
-int launch_gemm_raw(int device, int num_sms, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep,
-                    cudaStream_t st) {
-    using C = GemmCfg<P>;
+int launch_gemm_raw(int device, int num_sms, const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& C0,
+                    const CUtensorMap& C1, const CUtensorMap& C2, const EpiParams& ep, cudaStream_t st) {
+    using C = GemmCfg<P, KIND>;
     static std::atomic<unsigned long long> attr_done{0};  // one bit per device
     const unsigned long long bit = (device >= 0 && device < 64) ? (1ull << device) : 0ull;
     if (!bit || !(attr_done.load() & bit)) {
         CK(cudaFuncSetAttribute(k_plane_gemm<P, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_done.fetch_or(bit);
     }
-    const int tiles = ((ep.M + 127) / 128) * ((ep.N + 127) / 128);
+    const int tiles = ((ep.M + 127) / 128) * ((ep.N + C::BN - 1) / C::BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    k_plane_gemm<P, KIND><<<grid, C::THREADS, C::SMEM, st>>>(A, B, ep);
+    k_plane_gemm<P, KIND><<<grid, C::THREADS, C::SMEM, st>>>(A, B, C0, C1, C2, ep);
     CK(cudaGetLastError());
     return EII_OK;
 }
 
 template <int P, int KIND>
 int launch_gemm(eii_engine* e, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep, cudaStream_t st,
-                int prof_kind) {
+                int prof_kind, const CUtensorMap* C0 = nullptr, const CUtensorMap* C1 = nullptr,
+                const CUtensorMap* C2 = nullptr) {
     ProfScope ps(e, prof_kind, st);
-    return launch_gemm_raw<P, KIND>(e->device, e->num_sms, A, B, ep, st);
+    return launch_gemm_raw<P, KIND>(e->device, e->num_sms, A, B, C0 ? *C0 : A, C1 ? *C1 : A, C2 ? *C2 : A, ep, st);
 }
 
 template <int KIND>
 int launch_gemm_p(eii_engine* e, int P, const CUtensorMap& A, const CUtensorMap& B, const EpiParams& ep,
-                  cudaStream_t st, int prof_kind) {
-    if (P == 2) return launch_gemm<2, KIND>(e, A, B, ep, st, prof_kind);
-    if (P == 4) return launch_gemm<4, KIND>(e, A, B, ep, st, prof_kind);
+                  cudaStream_t st, int prof_kind, const CUtensorMap* C0_p2 = nullptr, const CUtensorMap* C0_p4 = nullptr) {
+    if (P == 2) return launch_gemm<2, KIND>(e, A, B, ep, st, prof_kind, C0_p2);
+    if (P == 4) return launch_gemm<4, KIND>(e, A, B, ep, st, prof_kind, C0_p4);
     return fail(EII_ERR_FORMAT, "unsupported plane count %d", P);
 }
 
@@ -368,8 +402,8 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     ep.M = rows; ep.N = 960; ep.K = D_MODEL; ep.msh = L.msh_qkv; ep.err = e->err_dev;
     ep.T = T; ep.q_out = e->q; ep.k_out = e->k; ep.v_out = e->v; ep.rope_c = e->rope_c; ep.rope_s = e->rope_s;
     ep.bits_q = L.q.bits; ep.bits_k = L.k.bits; ep.bits_v = L.v.bits; ep.bits_qr = L.qr.bits; ep.bits_kr = L.kr.bits;
-    ep.rope_shift_q = L.rope_shift_q; ep.rope_shift_k = L.rope_shift_k;
-    TRY(launch_gemm<2, EPI_QKV>(e, am->h, L.tm_qkv, ep, st, EII_K_GEMM_QKV));
+    ep.rope_shift_q = L.rope_shift_q; ep.rope_shift_k = L.rope_shift_k; ep.fast = L.fast_qkv;
+    TRY(launch_gemm<2, EPI_QKV>(e, am->h, L.tm_qkv, ep, st, EII_K_GEMM_QKV, &am->q, &am->k, &am->v));
 
     AttnParams ap{};
     ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;
@@ -384,20 +418,25 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     CK(cudaGetLastError());
 
     ep = EpiParams{};
-    ep.M = rows; ep.N = D_MODEL; ep.K = D_MODEL; ep.msh = L.msh_o; ep.err = e->err_dev; ep.x = e->x;
-    TRY(launch_gemm_p<EPI_RESID>(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, L.tm_o, ep, st, EII_K_GEMM_O));
+    ep.M = rows; ep.N = D_MODEL; ep.K = D_MODEL; ep.msh = L.msh_o; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_o;
+    TRY(launch_gemm_p<EPI_RESID>(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, L.Pc == 2 ? L.tm_o : L.tm_o64, ep, st,
+                                 EII_K_GEMM_O, &am->x32, &am->x16));
 
     TRY(launch_norm(e, e->x, rows, L.ln2, L.norm2_shift, L.h2.bits, e->h_planes, 2, nullptr, st));
 
     ep = EpiParams{};
     ep.M = rows; ep.N = 2 * D_FF; ep.K = D_MODEL; ep.msh = L.msh_gu; ep.err = e->err_dev;
     ep.silu = L.silu; ep.bits_g = L.g.bits; ep.bits_u = L.u.bits; ep.gated_shift = L.gated_shift;
+    ep.silu_neg = L.silu_neg; ep.silu_smem = L.silu_neg != nullptr; ep.silu_lo = L.silu_lo;
+    ep.silu_count = L.silu_count; ep.silu_wide = L.silu_wide; ep.silu_d = L.silu_d; ep.bits_s = L.s.bits;
+    ep.fast = L.fast_gu;
     ep.bits_m = L.m.bits; ep.gated_P = L.Pm; ep.gated_planes = e->gated_planes;
     TRY(launch_gemm<2, EPI_GATEUP>(e, am->h, L.tm_gu, ep, st, EII_K_GEMM_GATEUP));
 
     ep = EpiParams{};
-    ep.M = rows; ep.N = D_MODEL; ep.K = D_FF; ep.msh = L.msh_d; ep.err = e->err_dev; ep.x = e->x;
-    TRY(launch_gemm_p<EPI_RESID>(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, L.tm_d, ep, st, EII_K_GEMM_DOWN));
+    ep.M = rows; ep.N = D_MODEL; ep.K = D_FF; ep.msh = L.msh_d; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_d;
+    TRY(launch_gemm_p<EPI_RESID>(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, L.Pm == 2 ? L.tm_d : L.tm_d64, ep, st,
+                                 EII_K_GEMM_DOWN, &am->x32, &am->x16));
     return EII_OK;
 }
 
@@ -407,8 +446,10 @@ int run_logits(eii_engine* e, int rows, int32_t* logits, int64_t ld, cudaStream_
     TRY(launch_norm(e, e->x, rows, e->final_q, e->final_shift, 16, e->h_planes, 2, nullptr, st));
     EpiParams ep{};
     ep.M = rows; ep.N = VOCAB; ep.K = D_MODEL; ep.msh = e->msh_logits; ep.err = e->err_dev;
-    ep.logits = logits; ep.ld_logits = ld;
-    return launch_gemm<2, EPI_LOGITS>(e, am->h, e->tm_emb, ep, st, EII_K_GEMM_LOGITS);
+    ep.logits = logits; ep.ld_logits = ld; ep.fast = e->fast_logits;
+    CUtensorMap lm;
+    TRY(map_out(&lm, logits, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, VOCAB, rows, (uint64_t)ld * 4, 32, 32));
+    return launch_gemm<2, EPI_LOGITS>(e, am->h, e->tm_emb, ep, st, EII_K_GEMM_LOGITS, &lm);
 }
 
 int check_device_error(eii_engine* e, cudaStream_t st) {
@@ -469,6 +510,67 @@ int upload(eii_engine* e, T** dst, const T* src, size_t count) {
     return EII_OK;
 }
 
+// Compact SiLU table for shared memory.  Since silu(x) - silu(-x) = x, the half-up rounded table
+// satisfies tab[g] = SAT_bits_s(tab[-g] + g * 2^(f_s - f_g)) for g > 0 whenever f_s >= f_g; below
+// some lo <= 0 the table is 0.  The identity is checked for all 65536 inputs; if it fails, or the
+// dense range does not fit SILU_SMEM_BYTES, the kernel gathers from the full table instead.
+int compact_silu(eii_engine* e, LayerDev& L, const int64_t* tab) {
+    L.silu_neg = nullptr;
+    if (const char* mode = getenv("EII_SILU"))  // EII_SILU=global: always gather from the full table
+        if (strcmp(mode, "global") == 0) return EII_OK;
+    const int d = L.s.f - L.g.f;
+    if (d < 0 || d > 30) return EII_OK;
+    int lo = 0;
+    for (int g = -32768; g <= 0; ++g)
+        if (tab[g + 32768] != 0) { lo = g; break; }
+    bool wide = false;
+    for (int g = lo; g <= 0; ++g)
+        if (tab[g + 32768] < INT16_MIN || tab[g + 32768] > INT16_MAX) wide = true;
+    const int count = 1 - lo;
+    if ((size_t)count * (wide ? 4 : 2) > (size_t)SILU_SMEM_BYTES) return EII_OK;
+    const int64_t smax = (int64_t(1) << (L.s.bits - 1)) - 1, smin = -smax - 1;
+    for (int g = -32768; g <= 32767; ++g) {
+        const int a = g < 0 ? g : -g;
+        int64_t t = a >= lo ? tab[a + 32768] : 0;
+        if (g > 0) {
+            t += static_cast<int64_t>(g) << d;
+            t = t < smin ? smin : (t > smax ? smax : t);
+        }
+        if (t != tab[g + 32768]) return EII_OK;
+    }
+    std::vector<uint8_t> buf((size_t)count * (wide ? 4 : 2) + 16, 0);
+    for (int k = 0; k < count; ++k) {
+        const int64_t v = tab[lo + k + 32768];
+        if (wide) reinterpret_cast<int32_t*>(buf.data())[k] = static_cast<int32_t>(v);
+        else reinterpret_cast<int16_t*>(buf.data())[k] = static_cast<int16_t>(v);
+    }
+    uint8_t* dev;
+    TRY(upload(e, &dev, buf.data(), buf.size()));
+    L.silu_neg = dev;
+    L.silu_lo = lo;
+    L.silu_count = count;
+    L.silu_wide = wide ? 1 : 0;
+    L.silu_d = d;
+    return EII_OK;
+}
+
+// The fast epilogue path needs every column shift in [1, 31] and every multiplier in [0, 2^15).
+bool cols_fast(const std::vector<int2>& msh) {
+    for (const int2& c : msh)
+        if (c.y < 1 || c.y > 31 || c.x < 0 || c.x >= (1 << 15)) return false;
+    return true;
+}
+
+// Per-column requantisation shifts are array shifts of the reference, which it requires to be >= 1
+// (python/intref.py:49); the GEMM epilogues rely on that.
+int check_col_shifts(const std::vector<int2>& msh, const char* what, int layer) {
+    for (size_t j = 0; j < msh.size(); ++j)
+        if (msh[j].y < 1 || msh[j].y > 62)
+            return fail(EII_ERR_FORMAT, "%s shift %d at layer %d column %zu: per-element shift must be >= 1 "
+                        "(python/intref.py:49)", what, msh[j].y, layer, j);
+    return EII_OK;
+}
+
 int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
     if (nbytes != model_bin_bytes())
         return fail(EII_ERR_IO, "model.bin has %zu bytes, expected %zu (layout of c/intref.c:8-13)", nbytes, model_bin_bytes());
@@ -502,6 +604,8 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
     {
         std::vector<int2> msh(VOCAB);
         for (int i = 0; i < VOCAB; ++i) msh[i] = make_int2((int)emb_m[i], (int)(emb_n[i] + e->f_y - 16));
+        TRY(check_col_shifts(msh, "logits", -1));
+        e->fast_logits = cols_fast(msh);
         TRY(upload(e, &e->msh_logits, msh.data(), VOCAB));
     }
     TRY(map_2d(&e->tm_emb, e->emb_q, D_MODEL, VOCAB));
@@ -551,6 +655,7 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
         TRY(upload(e, &L.ln2, tmp.data(), D_MODEL));
         TRY(narrow32(silu, 65536, tmp, "silu"));
         TRY(upload(e, &L.silu, tmp.data(), 65536));
+        TRY(compact_silu(e, L, silu));
 
         // q | k | v
         {
@@ -566,6 +671,9 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
                 for (int j = 0; j < MODEL_LIN_N[i]; ++j, ++col)
                     msh[col] = make_int2((int)wm[i][j], (int)(wn[i][j] + L.h.f - outf[i].f));
             }
+            TRY(check_col_shifts(msh, "q/k/v", l));
+            L.fast_qkv = cols_fast(msh) && L.rope_shift_q >= 1 && L.rope_shift_q <= 31 && L.rope_shift_k >= 1 &&
+                         L.rope_shift_k <= 31;
             TRY(upload(e, &L.w_qkv, w.data(), w.size()));
             TRY(upload(e, &L.msh_qkv, msh.data(), 960));
             TRY(map_2d(&L.tm_qkv, L.w_qkv, D_MODEL, 960));
@@ -574,9 +682,12 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
         {
             std::vector<int2> msh(D_MODEL);
             for (int j = 0; j < D_MODEL; ++j) msh[j] = make_int2((int)wm[3][j], (int)(wn[3][j] + L.c.f - F_RES));
+            TRY(check_col_shifts(msh, "o_proj", l));
+            L.fast_o = cols_fast(msh);
             TRY(upload(e, &L.w_o, wq[3], (size_t)D_MODEL * D_MODEL));
             TRY(upload(e, &L.msh_o, msh.data(), D_MODEL));
             TRY(map_2d(&L.tm_o, L.w_o, D_MODEL, D_MODEL));
+            TRY(map_2d(&L.tm_o64, L.w_o, D_MODEL, D_MODEL, 64));
         }
         // gate / up interleaved per 128-row tile
         {
@@ -591,6 +702,8 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
                     msh[128 * t + 64 + r2] = make_int2((int)wm[5][j], (int)(wn[5][j] + L.h2.f - L.u.f));
                 }
             }
+            TRY(check_col_shifts(msh, "gate/up", l));
+            L.fast_gu = cols_fast(msh) && L.gated_shift >= 0 && L.gated_shift <= 31;
             TRY(upload(e, &L.w_gu, w.data(), w.size()));
             TRY(upload(e, &L.msh_gu, msh.data(), 2 * D_FF));
             TRY(map_2d(&L.tm_gu, L.w_gu, D_MODEL, 2 * D_FF));
@@ -599,9 +712,12 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
         {
             std::vector<int2> msh(D_MODEL);
             for (int j = 0; j < D_MODEL; ++j) msh[j] = make_int2((int)wm[6][j], (int)(wn[6][j] + L.f_m - F_RES));
+            TRY(check_col_shifts(msh, "down", l));
+            L.fast_d = cols_fast(msh);
             TRY(upload(e, &L.w_d, wq[6], (size_t)D_MODEL * D_FF));
             TRY(upload(e, &L.msh_d, msh.data(), D_MODEL));
             TRY(map_2d(&L.tm_d, L.w_d, D_FF, D_MODEL));
+            TRY(map_2d(&L.tm_d64, L.w_d, D_FF, D_MODEL, 64));
         }
     }
     if (r.left != 0) return fail(EII_ERR_IO, "model.bin has %zu trailing bytes", r.left);
@@ -627,6 +743,10 @@ int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
     if (rc == EII_OK) rc = dalloc(e->weights, &e->err_dev, 1);
     if (rc == EII_OK && cudaMemset(e->err_dev, 0, sizeof(int)) != cudaSuccess) rc = fail(EII_ERR_CUDA, "memset failed");
     if (rc == EII_OK) rc = load_model(e, static_cast<const uint8_t*>(data), nbytes);
+    if (rc == EII_OK && getenv("EII_GENERIC_REQUANT")) {  // test switch: always take the int64 epilogue path
+        e->fast_logits = 0;
+        for (LayerDev& L : e->L) L.fast_qkv = L.fast_o = L.fast_gu = L.fast_d = 0;
+    }
     if (rc == EII_OK && (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               attn_smem_bytes(ROPE_POS)) != cudaSuccess ||
                          cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -912,6 +1032,7 @@ int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const
     CK(cudaSetDevice(e->device));
     std::vector<int2> msh(N);
     for (int j = 0; j < N; ++j) msh[j] = make_int2((int)m[j], (int)(n[j] + f_in - f_out));
+    TRY(check_col_shifts(msh, "linear", -1));
     std::vector<void*> tmp;
     int64_t *a_dev, *out_dev, *acc_dev = nullptr;
     int8_t* w_dev;
@@ -927,7 +1048,7 @@ int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const
                          cudaMemcpy(msh_dev, msh.data(), (size_t)N * sizeof(int2), cudaMemcpyHostToDevice) != cudaSuccess))
         rc = fail(EII_ERR_CUDA, "upload failed");
     CUtensorMap tmB;
-    if (rc == EII_OK) rc = map_2d(&tmB, w_dev, K, N);
+    if (rc == EII_OK) rc = map_2d(&tmB, w_dev, K, N, bits_in == 32 ? 64 : 128);
     if (rc == EII_OK) rc = linear_device(e, a_dev, M, K, bits_in, tmB, msh_dev, N, bits_out, out_dev, acc_dev, tmp);
     if (rc == EII_OK && cudaMemcpyAsync(out, out_dev, (size_t)M * N * 8, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
         rc = fail(EII_ERR_CUDA, "download failed");
@@ -1001,10 +1122,19 @@ int noalloc_setup(int dev, NoAllocDevice** out) {
     return EII_OK;
 }
 
+// Per-column (m, n + f_in - f_out).  A shift outside [1, 62] violates the reference's array-shift
+// rule (python/intref.py:49); it is reported through the error word and clamped so the GEMM stays
+// well defined.
 __global__ void k_msh_from_mn(const int64_t* __restrict__ m, const int64_t* __restrict__ n, int N, int dshift,
-                              int2* __restrict__ msh) {
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < N; j += gridDim.x * blockDim.x)
-        msh[j] = make_int2(static_cast<int>(m[j]), static_cast<int>(n[j] + dshift));
+                              int2* __restrict__ msh, int* err) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < N; j += gridDim.x * blockDim.x) {
+        int64_t sh = n[j] + dshift;
+        if (sh < 1 || sh > 62) {
+            atomicCAS(err, 0, ERR_BAD_SHIFT);
+            sh = 1;
+        }
+        msh[j] = make_int2(static_cast<int>(m[j]), static_cast<int>(sh));
+    }
 }
 
 }  // namespace
@@ -1030,7 +1160,7 @@ extern "C" int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_i
     TRY(noalloc_setup(dev, &d));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     CK(cudaMemsetAsync(d->err, 0, sizeof(int), st));
-    k_msh_from_mn<<<(N + 255) / 256, 256, 0, st>>>(m_dev, n_dev, N, f_in - f_out, d->msh);
+    k_msh_from_mn<<<(N + 255) / 256, 256, 0, st>>>(m_dev, n_dev, N, f_in - f_out, d->msh, d->err);
     CK(cudaGetLastError());
     const int64_t count = (int64_t)M * K;
     k_split_planes<<<(unsigned)((count + 255) / 256 < 4096 ? (count + 255) / 256 : 4096), 256, 0, st>>>(a_dev, count, P,
@@ -1038,15 +1168,16 @@ extern "C" int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_i
     CK(cudaGetLastError());
     CUtensorMap tmA, tmB;
     TRY(map_planes(&tmA, d->planes, K, M, P));
-    TRY(map_2d(&tmB, w_dev, K, N));
+    TRY(map_2d(&tmB, w_dev, K, N, bits_in == 32 ? 64 : 128));
     EpiParams ep{};
     ep.M = M; ep.N = N; ep.K = K; ep.msh = d->msh; ep.err = d->err; ep.out64 = out_dev; ep.acc64 = acc_dev;
     ep.bits_out = bits_out;
-    if (P == 2) TRY(launch_gemm_raw<2, EPI_LINEAR>(dev, d->num_sms, tmA, tmB, ep, st));
-    else TRY(launch_gemm_raw<4, EPI_LINEAR>(dev, d->num_sms, tmA, tmB, ep, st));
+    if (P == 2) TRY(launch_gemm_raw<2, EPI_LINEAR>(dev, d->num_sms, tmA, tmB, tmA, tmA, tmA, ep, st));
+    else TRY(launch_gemm_raw<4, EPI_LINEAR>(dev, d->num_sms, tmA, tmB, tmA, tmA, tmA, ep, st));
     int code = 0;
     CK(cudaMemcpyAsync(&code, d->err, sizeof(int), cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
+    if (code == ERR_BAD_SHIFT) return fail(EII_ERR_ARG, "n + f_in - f_out outside [1, 62] (python/intref.py:49)");
     if (code) return fail(EII_ERR_DEVICE, "kernel reported error %d (bounded wait timed out)", code);
     return EII_OK;
 }

@@ -53,8 +53,18 @@ struct EpiParams {
     int bits_q, bits_k, bits_v, bits_qr, bits_kr, rope_shift_q, rope_shift_k;
     // EPI_RESID: x [M,N] int32, x = SAT32(x + RS(acc m, shift))
     int32_t* x;
-    // EPI_GATEUP: gate/up interleaved by tile (cols 0-63 gate j, 64-127 up j), gated -> planes
+    // EPI_GATEUP: gate/up interleaved by tile (cols 0-63 gate j, 64-127 up j), gated -> planes.
+    // SiLU: the full 65536-entry table (global), or, when silu_smem is set, its compact form
+    //   tab[g] = neg[-|g| - lo] (0 below lo) for g <= 0,  SAT_bits_s(neg[-g - lo] + g * 2^silu_d) for g > 0
+    // (silu(x) - silu(-x) = x exactly, so with f_s >= f_g the rounded table obeys it; the engine
+    // verifies it for all 65536 inputs before enabling it), staged once per CTA in shared memory.
     const int32_t* silu;
+    const void* silu_neg;
+    int silu_smem, silu_lo, silu_count, silu_wide, silu_d, bits_s;
+    // fast = every column shift is in [1, 31] and every m in [0, 2^15), the RoPE shifts are in
+    // [1, 31] and the gated-product shift in [0, 31]: requantisation then runs on 32x32->64
+    // multiply-adds and 32-bit funnel shifts; otherwise the generic int64 path is taken.
+    int fast;
     int bits_g, bits_u, gated_shift, bits_m, gated_P;
     uint8_t* gated_planes;  // [gated_P][M][N/2]
     // EPI_LOGITS: int32 out[row * ld + col] = RS(acc m, shift) (low 32 bits, no SAT)
@@ -66,53 +76,229 @@ struct EpiParams {
     int bits_out;
 };
 
-template <int P>
+constexpr int SILU_SMEM_BYTES = 48 * 1024;  // compact SiLU table capacity (int16 x 24576 or int32 x 12288)
+constexpr int SMEM_LIMIT = 227 * 1024;
+
+template <int P, int KIND>
 struct GemmCfg {
-    static constexpr int BM = 128, BN = 128, BK = 128;
+    // P = 4 uses 64-wide N tiles so that two accumulator sets (2 x 4 x 64 columns) fit in TMEM and the
+    // epilogue of one tile overlaps the MMAs of the next.
+    static constexpr int BM = 128, BN = (P == 4) ? 64 : 128, BK = 128;
     static constexpr int ACC_COLS = P * BN;
     static constexpr int NB = 512 / ACC_COLS;  // accumulator sets in TMEM
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = P * A_BYTES + B_BYTES;
-    static constexpr int STAGES = (P == 2) ? 4 : 2;
-    static constexpr int EPI_WARPS = 8;
-    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-    static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+    // Per-warp staging buffer for TMA tile stores (and the residual tile load): 32 rows x the warp's
+    // columns.  LOGITS/RESID: int32, BN/4 columns; QKV: two 32-row x 16 int16 boxes.
+    static constexpr int STG_BYTES = (KIND == EPI_LOGITS || KIND == EPI_RESID) ? (BN / 4) * 4 * 32
+                                     : (KIND == EPI_QKV ? 2048 : 0);
+    static constexpr int STAGES = (P == 2) ? (KIND == EPI_LINEAR ? 4 : 3) : (KIND == EPI_LINEAR ? 3 : 2);
+    static constexpr int EPI_WARPS = 16;  // 4 per TMEM lane quadrant, each owns 32 tile columns
+    static constexpr int EPI_THREADS = 32 * EPI_WARPS;
+    static constexpr int THREADS = 64 + EPI_THREADS;
+    static constexpr int BAR_BYTES = 512;
+    static constexpr int COLP_BYTES = 2 * BN * 16;  // per-tile column (m, shift, 2^(shift-1), m << 8), x2
+    static constexpr int SILU_BYTES = KIND == EPI_GATEUP ? SILU_SMEM_BYTES : 0;
+    static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;  // 1024-aligned
+    static constexpr int BAR_OFFSET = STG_OFFSET + EPI_WARPS * STG_BYTES;
+    static constexpr int SMEM = BAR_OFFSET + 1024 + BAR_BYTES + COLP_BYTES + SILU_BYTES;
     static_assert(NB >= 1, "accumulators must fit in TMEM");
+    static_assert(STG_BYTES % 1024 == 0, "staging buffers are 1024-byte aligned");
+    static_assert(SMEM <= SMEM_LIMIT, "shared memory budget");
 };
 
-// Load 16 consecutive accumulator columns of all P planes for this thread's row and combine.
-template <int P>
-__device__ __forceinline__ void load_acc16(uint32_t taddr, int64_t (&acc)[16]) {
-    uint32_t v[P][16];
+// Barrier of the 512 epilogue threads (named barrier 1) that also ANDs a flag across them, so that a
+// timed-out wait in one warp makes every epilogue warp leave together.
+__device__ __forceinline__ bool epi_barrier_and(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.and.pred po, 1, 512, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}\n"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v))
+        : "memory");
+    return r != 0;
+}
+
+// ------------------------------------------------------------------------------ epilogue math
+// Raw int32 plane accumulators of 16 consecutive columns of this thread's row.
+// Plane p of an accumulator set starts at column p * BN (BN = 128 for P = 2, 64 for P = 4).
+template <int P, int N>
+__device__ __forceinline__ void load_planes(uint32_t taddr, uint32_t (&v)[P][N]) {
+    static_assert(N == 8 || N == 16, "8 or 16 columns");
+    constexpr int PS = (P == 4) ? 64 : 128;
 #pragma unroll
-    for (int p = 0; p < P; ++p) tmem_ld16(taddr + p * 128, v[p]);
+    for (int p = 0; p < P; ++p) {
+        if constexpr (N == 16) tmem_ld16(taddr + p * PS, v[p]);
+        else tmem_ld8(taddr + p * PS, v[p]);
+    }
     tmem_wait_ld();
 #pragma unroll
     for (int p = 0; p < P; ++p) tmem_launder(v[p]);
+}
+
+template <int P, int N>
+__device__ __forceinline__ int64_t combine(const uint32_t (&v)[P][N], int i) {
+    int64_t a = 0;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        int64_t a = 0;
+    for (int p = 0; p < P; ++p) a += static_cast<int64_t>(static_cast<int32_t>(v[p][i])) * (int64_t(1) << (8 * p));
+    return a;
+}
+
+// Generic path: RS with a per-column shift >= 1 (an array shift of the reference, which
+// python/intref.py:49 requires to be >= 1; the engine rejects models and arguments that violate it).
+__device__ __forceinline__ int64_t rs_col(int64_t x, int n) {
+    return static_cast<int64_t>(static_cast<uint64_t>(x) + (static_cast<uint64_t>(1) << (n - 1))) >> n;
+}
+
+// Fast path: acc * m + 2^(sh-1) built directly from the int32 plane accumulators,
+// sum_p d_p (m 2^(8p)) + rnd, with 32x32 -> 64 multiply-adds (exact: the total is < 2^63).
+template <int P, int N>
+__device__ __forceinline__ int64_t mulround(const uint32_t (&v)[P][N], int i, int4 cp) {
+    int64_t t = static_cast<int64_t>(static_cast<int32_t>(v[0][i])) * cp.x + static_cast<int64_t>(static_cast<uint32_t>(cp.z));
+    t += static_cast<int64_t>(static_cast<int32_t>(v[1][i])) * cp.w;
+    if constexpr (P == 4) {
+        t += static_cast<int64_t>(static_cast<int32_t>(v[2][i])) * (cp.x << 16);
+        t += (static_cast<int64_t>(static_cast<int32_t>(v[3][i])) * cp.x) * (int64_t(1) << 24);
+    }
+    return t;
+}
+
+// t >> sh for 1 <= sh <= 31 as (hi, lo) words, by funnel shift.
+__device__ __forceinline__ void shr31(int64_t t, int sh, int32_t& hi, uint32_t& lo) {
+    const uint32_t tl = static_cast<uint32_t>(t), th = static_cast<uint32_t>(static_cast<uint64_t>(t) >> 32);
+    lo = __funnelshift_r(tl, th, sh);
+    hi = static_cast<int32_t>(th) >> sh;
+}
+
+// SAT to `bits` (<= 32) of the 64-bit value (hi, lo).
+__device__ __forceinline__ int32_t sat_hl(int32_t hi, uint32_t lo, int bits) {
+    const bool fits = hi == (static_cast<int32_t>(lo) >> 31);
+    int32_t v = fits ? static_cast<int32_t>(lo) : (hi < 0 ? INT32_MIN : INT32_MAX);
+    if (bits < 32) {
+        const int32_t lim = 1 << (bits - 1);
+        v = min(max(v, -lim), lim - 1);
+    }
+    return v;
+}
+
+// Fast requantisation of one element: SAT_bits(RS(acc m, sh)).
+template <int P, int N>
+__device__ __forceinline__ int32_t requant_fast(const uint32_t (&v)[P][N], int i, int4 cp, int bits) {
+    int32_t hi;
+    uint32_t lo;
+    shr31(mulround<P, N>(v, i, cp), cp.y, hi, lo);
+    return sat_hl(hi, lo, bits);
+}
+
+// Generic requantisation (any shift in [1, 62]); bits may be up to 64.
+template <int P, int N>
+__device__ __forceinline__ int64_t requant_gen(const uint32_t (&v)[P][N], int i, int4 cp, int bits) {
+    return sat64(rs_col(combine<P, N>(v, i) * static_cast<int64_t>(cp.x), cp.y), bits);
+}
+
+__device__ __forceinline__ int64_t silu_lookup(const EpiParams& ep, const void* tab_smem, int g) {
+    if (!ep.silu_smem) return __ldg(ep.silu + (g + 32768));
+    const int a = g < 0 ? g : -g;
+    int64_t t = 0;
+    if (a >= ep.silu_lo) {
+        t = ep.silu_wide ? static_cast<const int32_t*>(tab_smem)[a - ep.silu_lo]
+                         : static_cast<const int16_t*>(tab_smem)[a - ep.silu_lo];
+    }
+    if (g > 0) t = sat64(t + (static_cast<int64_t>(g) << ep.silu_d), ep.bits_s);
+    return t;
+}
+
+// Byte plane p of 16 values -> one 16-byte vector (three byte permutes per 4 values).
+template <int PL, int N>
+__device__ __forceinline__ void pack_plane(const int32_t (&x)[N], uint32_t (&w)[N / 4]) {
+    constexpr uint32_t sel = PL | ((4 + PL) << 4);
 #pragma unroll
-        for (int p = 0; p < P; ++p) a += static_cast<int64_t>(static_cast<int32_t>(v[p][i])) * (int64_t(1) << (8 * p));
-        acc[i] = a;
+    for (int q = 0; q < N / 4; ++q) {
+        const uint32_t t01 = __byte_perm(static_cast<uint32_t>(x[4 * q]), static_cast<uint32_t>(x[4 * q + 1]), sel);
+        const uint32_t t23 = __byte_perm(static_cast<uint32_t>(x[4 * q + 2]), static_cast<uint32_t>(x[4 * q + 3]), sel);
+        w[q] = __byte_perm(t01, t23, 0x5410);
     }
 }
 
-__device__ __forceinline__ int64_t requant(int64_t acc, int2 ms, int bits) {
-    return sat64(rs64(acc * static_cast<int64_t>(ms.x), ms.y), bits);
+template <int PL, int N>
+__device__ __forceinline__ void store_plane(uint8_t* dst, const int32_t (&x)[N]) {
+    uint32_t w[N / 4];
+    pack_plane<PL, N>(x, w);
+    if constexpr (N == 16) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+}
+
+// The byte planes of N values (N = 8 or 16) to plane_stride-separated destinations.
+template <int N>
+__device__ __forceinline__ void store_planes(uint8_t* base, int64_t plane_stride, int nplanes, const int32_t (&x)[N]) {
+    store_plane<0, N>(base, x);
+    store_plane<1, N>(base + plane_stride, x);
+    if (nplanes == 4) {
+        store_plane<2, N>(base + 2 * plane_stride, x);
+        store_plane<3, N>(base + 3 * plane_stride, x);
+    }
+}
+
+// Gate/up/SiLU/gated product for 16 features, all-32-bit path: INT16 gate and up, compact INT16
+// SiLU table with shift d <= 15 (so g * 2^d < 2^31), gated shift in [0, 31].
+template <int P, int N, int BITS_M>
+__device__ __forceinline__ void gateup_lean(const uint32_t (&vg)[P][N], const uint32_t (&vu)[P][N], const int4* cpg,
+                                            const int4* cpu, const int16_t* tab, int lo_g, int d, int gs, int64_t grnd,
+                                            int32_t (&gm)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const int32_t g = requant_fast<P, N>(vg, i, cpg[i], 16);
+        const int32_t u = requant_fast<P, N>(vu, i, cpu[i], 16);
+        const int32_t a = min(g, -g);
+        int32_t sg = a >= lo_g ? static_cast<int32_t>(tab[a - lo_g]) : 0;
+        if (g > 0) sg = min(max(sg + (g << d), -32768), 32767);
+        const int64_t prod = static_cast<int64_t>(sg) * u + grnd;
+        int32_t hi;
+        uint32_t lo;
+        if (gs == 0) {
+            hi = static_cast<int32_t>(static_cast<uint64_t>(prod) >> 32);
+            lo = static_cast<uint32_t>(prod);
+        } else {
+            shr31(prod, gs, hi, lo);
+        }
+        gm[i] = sat_hl(hi, lo, BITS_M);
+    }
 }
 
 // ---------------------------------------------------------------------------------------------
+// One epilogue warp's share of a 128 x 128 tile: rows quad*32 + lane, column group cg (0..3).
+// Byte offset of 16-byte chunk c of row r in a TMA box whose rows are S bytes (S = 32, 64 or 128)
+// stored with the matching S-byte swizzle (chunk index XOR address bits 7.., as TMA lays it out).
+template <int S>
+__device__ __forceinline__ int stg_off(int r, int c) {
+    return r * S + (((c ^ ((r * S) >> 7)) & (S / 16 - 1)) << 4);
+}
+
+// Output maps of the epilogue (TMA stores; RESID also loads its residual tile through map 0):
+// LOGITS 0 = logits; RESID 0 = x; QKV 0/1/2 = q/k/v.
+struct EpiMaps {
+    const CUtensorMap* c0;
+    const CUtensorMap* c1;
+    const CUtensorMap* c2;
+};
+
+
 template <int P, int KIND>
-__device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc, int m_blk, int n_blk, int half,
-                                              int quad, int lane) {
+__device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc, int m_blk, int n_blk, int cg,
+                                              int quad, int lane, const int4* colp, const void* silu_tab,
+                                              uint8_t* stg, const EpiMaps& maps) {
+    constexpr int BN = (P == 4) ? 64 : 128;
     const int row = m_blk * 128 + quad * 32 + lane;
     const bool row_ok = row < ep.M;
-    const int n0 = n_blk * 128;
+    const int n0 = n_blk * BN;
     if constexpr (KIND == EPI_QKV) {
-        const int c0 = n0 + 64 * half;  // one head per warp half
+        // cg -> head (cg >> 1) of the tile, dims d in [sub, sub + 16) paired with d + 32 for RoPE
+        const int hl = cg >> 1, sub = (cg & 1) * 16;
+        const int c0 = n0 + 64 * hl;
         if (c0 >= ep.N) return;
         int region, head;  // 0 = q, 1 = k, 2 = v
         if (c0 < 576) { region = 0; head = c0 / 64; }
@@ -121,107 +307,193 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
         const int bits_in = region == 0 ? ep.bits_q : (region == 1 ? ep.bits_k : ep.bits_v);
         const int bits_r = region == 0 ? ep.bits_qr : ep.bits_kr;
         const int rshift = region == 0 ? ep.rope_shift_q : ep.rope_shift_k;
-        int16_t* out = region == 0 ? ep.q_out : (region == 1 ? ep.k_out : ep.v_out);
-        const int width = region == 0 ? 576 : 192;
+        const CUtensorMap* omap = region == 0 ? maps.c0 : (region == 1 ? maps.c1 : maps.c2);
         const int pos = row_ok ? row % ep.T : 0;
+        const int64_t rrnd = rshift >= 1 ? (int64_t(1) << (rshift - 1)) : 0;
+        // staging: dims [sub, sub + 16) and [32 + sub, 32 + sub + 16) of the head, 32 rows each (SW32)
+        uint8_t* sa = stg;
+        uint8_t* sb = stg + 1024;
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
 #pragma unroll 1
-        for (int sub = 0; sub < 32; sub += 16) {
-            int64_t aa[16], bb[16];
-            load_acc16<P>(tacc + 64 * half + sub, aa);
-            load_acc16<P>(tacc + 64 * half + 32 + sub, bb);
+        for (int h8 = 0; h8 < 16; h8 += 8) {  // 8 dims at a time keeps the pass free of spills
+            const int d0 = sub + h8;
+            uint32_t va[P][8], vb[P][8];
+            load_planes<P, 8>(tacc + 64 * hl + d0, va);
+            load_planes<P, 8>(tacc + 64 * hl + 32 + d0, vb);
             if (!row_ok) continue;
-            int16_t oa[16], ob[16];
+            int32_t rc[8], rsn[8];
+            if (region < 2) {
+                const int4* cpp = reinterpret_cast<const int4*>(ep.rope_c + pos * 32 + d0);
+                const int4* spp = reinterpret_cast<const int4*>(ep.rope_s + pos * 32 + d0);
+                reinterpret_cast<int4*>(rc)[0] = __ldg(cpp);
+                reinterpret_cast<int4*>(rc)[1] = __ldg(cpp + 1);
+                reinterpret_cast<int4*>(rsn)[0] = __ldg(spp);
+                reinterpret_cast<int4*>(rsn)[1] = __ldg(spp + 1);
+            }
+            int16_t oa[8], ob[8];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int d = sub + i;
-                const int64_t a = requant(aa[i], __ldg(ep.msh + c0 + d), bits_in);
-                const int64_t b = requant(bb[i], __ldg(ep.msh + c0 + 32 + d), bits_in);
+            for (int i = 0; i < 8; ++i) {
+                const int4 ca = colp[64 * hl + d0 + i], cb = colp[64 * hl + 32 + d0 + i];
+                int32_t a, b;
+                if (ep.fast) {
+                    a = requant_fast<P, 8>(va, i, ca, bits_in);
+                    b = requant_fast<P, 8>(vb, i, cb, bits_in);
+                } else {
+                    a = static_cast<int32_t>(requant_gen<P, 8>(va, i, ca, bits_in));
+                    b = static_cast<int32_t>(requant_gen<P, 8>(vb, i, cb, bits_in));
+                }
                 if (region < 2) {
-                    const int64_t c = __ldg(ep.rope_c + pos * 32 + d), s = __ldg(ep.rope_s + pos * 32 + d);
-                    oa[i] = static_cast<int16_t>(sat64(rs64(a * c - b * s, rshift), bits_r));
-                    ob[i] = static_cast<int16_t>(sat64(rs64(b * c + a * s, rshift), bits_r));
+                    const int64_t t1 = static_cast<int64_t>(a) * rc[i] - static_cast<int64_t>(b) * rsn[i];
+                    const int64_t t2 = static_cast<int64_t>(b) * rc[i] + static_cast<int64_t>(a) * rsn[i];
+                    if (ep.fast) {
+                        int32_t hi;
+                        uint32_t lo;
+                        shr31(t1 + rrnd, rshift, hi, lo);
+                        oa[i] = static_cast<int16_t>(sat_hl(hi, lo, bits_r));
+                        shr31(t2 + rrnd, rshift, hi, lo);
+                        ob[i] = static_cast<int16_t>(sat_hl(hi, lo, bits_r));
+                    } else {
+                        oa[i] = static_cast<int16_t>(sat64(rs64(t1, rshift), bits_r));
+                        ob[i] = static_cast<int16_t>(sat64(rs64(t2, rshift), bits_r));
+                    }
                 } else {
                     oa[i] = static_cast<int16_t>(a);
                     ob[i] = static_cast<int16_t>(b);
                 }
             }
-            int16_t* dst = out + static_cast<int64_t>(row) * width + head * 64 + sub;
-            reinterpret_cast<uint4*>(dst)[0] = *reinterpret_cast<uint4*>(&oa[0]);
-            reinterpret_cast<uint4*>(dst)[1] = *reinterpret_cast<uint4*>(&oa[8]);
-            reinterpret_cast<uint4*>(dst + 32)[0] = *reinterpret_cast<uint4*>(&ob[0]);
-            reinterpret_cast<uint4*>(dst + 32)[1] = *reinterpret_cast<uint4*>(&ob[8]);
+            *reinterpret_cast<uint4*>(sa + stg_off<32>(lane, h8 / 8)) = *reinterpret_cast<uint4*>(oa);
+            *reinterpret_cast<uint4*>(sb + stg_off<32>(lane, h8 / 8)) = *reinterpret_cast<uint4*>(ob);
+        }
+        fence_async_smem();
+        __syncwarp();
+        const int row0 = m_blk * 128 + quad * 32;
+        if (lane == 0 && row0 < ep.M) {
+            tma_store_2d(omap, sa, head * 64 + sub, row0);
+            tma_store_2d(omap, sb, head * 64 + 32 + sub, row0);
+            bulk_commit();
         }
     } else if constexpr (KIND == EPI_GATEUP) {
-        const int j0 = n_blk * 64 + 32 * half;  // gated feature index of this half
+        // cg -> gated features 16 cg .. 16 cg + 15 of the tile: gate cols 16 cg.., up cols 64 + 16 cg..
         if (n0 >= ep.N) return;
         const int Nh = ep.N / 2;
+        const int j0 = n_blk * 64 + 16 * cg;
+        const int gs = ep.gated_shift;
+        const int64_t grnd = gs >= 1 ? (int64_t(1) << (gs - 1)) : 0;
+        const bool lean = ep.fast && ep.silu_smem && !ep.silu_wide && ep.bits_s == 16 && ep.silu_d <= 15 &&
+                          ep.bits_g == 16 && ep.bits_u == 16;
 #pragma unroll 1
-        for (int sub = 0; sub < 32; sub += 16) {
-            int64_t ga[16], ua[16];
-            load_acc16<P>(tacc + 32 * half + sub, ga);
-            load_acc16<P>(tacc + 64 + 32 * half + sub, ua);
+        for (int h8 = 0; h8 < 16; h8 += 8) {  // 8 features at a time keeps the pass free of spills
+            const int f0 = 16 * cg + h8;
+            uint32_t vg[P][8], vu[P][8];
+            load_planes<P, 8>(tacc + f0, vg);
+            load_planes<P, 8>(tacc + 64 + f0, vu);
             if (!row_ok) continue;
-            int32_t gm[16];
+            int32_t gm[8];
+            if (lean && ep.bits_m == 32) {
+                gateup_lean<P, 8, 32>(vg, vu, colp + f0, colp + 64 + f0, static_cast<const int16_t*>(silu_tab), ep.silu_lo,
+                                      ep.silu_d, gs, grnd, gm);
+            } else if (lean && ep.bits_m == 16) {
+                gateup_lean<P, 8, 16>(vg, vu, colp + f0, colp + 64 + f0, static_cast<const int16_t*>(silu_tab), ep.silu_lo,
+                                      ep.silu_d, gs, grnd, gm);
+            } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int tc = 32 * half + sub + i;
-                const int64_t g = requant(ga[i], __ldg(ep.msh + n0 + tc), ep.bits_g);
-                const int64_t u = requant(ua[i], __ldg(ep.msh + n0 + 64 + tc), ep.bits_u);
-                const int64_t sg = __ldg(ep.silu + (g + 32768));
-                gm[i] = static_cast<int32_t>(sat64(rs64(sg * u, ep.gated_shift), ep.bits_m));
+                for (int i = 0; i < 8; ++i) {
+                    const int4 cgp = colp[f0 + i], cup = colp[64 + f0 + i];
+                    if (ep.fast) {
+                        const int32_t g = requant_fast<P, 8>(vg, i, cgp, ep.bits_g);
+                        const int32_t u = requant_fast<P, 8>(vu, i, cup, ep.bits_u);
+                        const int32_t sg = static_cast<int32_t>(silu_lookup(ep, silu_tab, g));
+                        const int64_t prod = static_cast<int64_t>(sg) * u + grnd;
+                        int32_t hi;
+                        uint32_t lo;
+                        if (gs == 0) { hi = static_cast<int32_t>(static_cast<uint64_t>(prod) >> 32); lo = static_cast<uint32_t>(prod); }
+                        else shr31(prod, gs, hi, lo);
+                        gm[i] = sat_hl(hi, lo, ep.bits_m);
+                    } else {
+                        const int64_t g = requant_gen<P, 8>(vg, i, cgp, ep.bits_g);
+                        const int64_t u = requant_gen<P, 8>(vu, i, cup, ep.bits_u);
+                        const int64_t sg = silu_lookup(ep, silu_tab, static_cast<int>(g));
+                        gm[i] = static_cast<int32_t>(sat64(rs64(sg * u, gs), ep.bits_m));
+                    }
+                }
             }
-            const int64_t base = static_cast<int64_t>(row) * Nh + j0 + sub;
-            for (int p = 0; p < ep.gated_P; ++p) {
-                uint8_t b[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) b[i] = plane_byte(gm[i], p);
-                *reinterpret_cast<uint4*>(ep.gated_planes + static_cast<int64_t>(p) * ep.M * Nh + base) =
-                    *reinterpret_cast<uint4*>(b);
-            }
+            store_planes<8>(ep.gated_planes + static_cast<int64_t>(row) * Nh + j0 + h8, static_cast<int64_t>(ep.M) * Nh,
+                            ep.gated_P, gm);
         }
     } else {
+        constexpr int NCOL = BN / 4;  // columns of this warp: 32 (P = 2) or 16 (P = 4)
+        if constexpr (KIND == EPI_LOGITS) {
+            if (lane == 0) bulk_wait_read0();  // the previous tile's store has read the staging buffer
+            __syncwarp();
+        }
 #pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
-            const int tc = 64 * half + 16 * ch;
+        for (int ch = 0; ch < NCOL / 16; ++ch) {
+            const int tc = NCOL * cg + 16 * ch;
             const int gc = n0 + tc;
             if (gc >= ep.N) break;
-            int64_t acc[16];
-            load_acc16<P>(tacc + tc, acc);
+            uint32_t v[P][16];
+            load_planes<P, 16>(tacc + tc, v);
             if (!row_ok) continue;
             if constexpr (KIND == EPI_RESID) {
-                int32_t* xp = ep.x + static_cast<int64_t>(row) * ep.N + gc;
-                int4 xv[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) xv[q] = reinterpret_cast<const int4*>(xp)[q];
-                const int32_t* xs = reinterpret_cast<const int32_t*>(xv);
+                // the residual tile was loaded into the staging buffer (TMA) before the accumulator wait
                 int32_t xo[16];
 #pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<int4*>(&xo[4 * q]) = *reinterpret_cast<const int4*>(stg + stg_off<NCOL * 4>(lane, 4 * ch + q));
+#pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int2 ms = __ldg(ep.msh + gc + i);
-                    const int64_t r = rs64(acc[i] * static_cast<int64_t>(ms.x), ms.y);
-                    xo[i] = static_cast<int32_t>(sat64(static_cast<int64_t>(xs[i]) + r, 32));
+                    const int4 cp = colp[tc + i];
+                    if (ep.fast) {
+                        int32_t hi;
+                        uint32_t lo;
+                        shr31(mulround<P, 16>(v, i, cp), cp.y, hi, lo);
+                        const int64_t r = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(hi)) << 32) | lo);
+                        const int64_t y = r + xo[i];
+                        xo[i] = sat_hl(static_cast<int32_t>(static_cast<uint64_t>(y) >> 32), static_cast<uint32_t>(y), 32);
+                    } else {
+                        const int64_t r = rs_col(combine<P, 16>(v, i) * static_cast<int64_t>(cp.x), cp.y);
+                        xo[i] = static_cast<int32_t>(sat64(static_cast<int64_t>(xo[i]) + r, 32));
+                    }
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) reinterpret_cast<int4*>(xp)[q] = reinterpret_cast<int4*>(xo)[q];
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<int4*>(stg + stg_off<NCOL * 4>(lane, 4 * ch + q)) = *reinterpret_cast<int4*>(&xo[4 * q]);
             } else if constexpr (KIND == EPI_LOGITS) {
                 int32_t o[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int2 ms = __ldg(ep.msh + gc + i);
-                    o[i] = static_cast<int32_t>(rs64(acc[i] * static_cast<int64_t>(ms.x), ms.y));
+                    const int4 cp = colp[tc + i];
+                    if (ep.fast) {
+                        int32_t hi;
+                        uint32_t lo;
+                        shr31(mulround<P, 16>(v, i, cp), cp.y, hi, lo);
+                        o[i] = static_cast<int32_t>(lo);
+                    } else {
+                        o[i] = static_cast<int32_t>(rs_col(combine<P, 16>(v, i) * static_cast<int64_t>(cp.x), cp.y));
+                    }
                 }
-                int32_t* op = ep.logits + static_cast<int64_t>(row) * ep.ld_logits + gc;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) reinterpret_cast<int4*>(op)[q] = reinterpret_cast<int4*>(o)[q];
-            } else {  // EPI_LINEAR
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<int4*>(stg + stg_off<128>(lane, 4 * ch + q)) = *reinterpret_cast<int4*>(&o[4 * q]);
+            } else {  // EPI_LINEAR (generic path only)
                 int64_t* op = ep.out64 + static_cast<int64_t>(row) * ep.N + gc;
 #pragma unroll
-                for (int i = 0; i < 16; ++i) op[i] = requant(acc[i], __ldg(ep.msh + gc + i), ep.bits_out);
+                for (int i = 0; i < 16; ++i) op[i] = requant_gen<P, 16>(v, i, colp[tc + i], ep.bits_out);
                 if (ep.acc64) {
                     int64_t* ap = ep.acc64 + static_cast<int64_t>(row) * ep.N + gc;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) ap[i] = acc[i];
+                    for (int i = 0; i < 16; ++i) ap[i] = combine<P, 16>(v, i);
                 }
+            }
+        }
+        if constexpr (KIND == EPI_LOGITS || KIND == EPI_RESID) {
+            fence_async_smem();
+            __syncwarp();
+            const int row0 = m_blk * 128 + quad * 32, gc0 = n0 + NCOL * cg;
+            if (lane == 0 && row0 < ep.M && gc0 < ep.N) {
+                tma_store_2d(maps.c0, stg, gc0, row0);
+                bulk_commit();
             }
         }
     }
@@ -229,22 +501,28 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
 
 // ---------------------------------------------------------------------------------------------
 template <int P, int KIND>
-__global__ void __launch_bounds__(GemmCfg<P>::THREADS, 1)
-    k_plane_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep) {
-    using C = GemmCfg<P>;
+__global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
+    k_plane_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmC0, const __grid_constant__ CUtensorMap tmC1,
+                 const __grid_constant__ CUtensorMap tmC2, EpiParams ep) {
+    using C = GemmCfg<P, KIND>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint8_t* staging = smem + C::STG_OFFSET;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFFSET);
     uint64_t* full = bars;
     uint64_t* empty = bars + C::STAGES;
     uint64_t* acc_full = bars + 2 * C::STAGES;
     uint64_t* acc_empty = acc_full + C::NB;
     uint64_t* drain = acc_empty + C::NB;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* xbar = drain + 1;  // per epilogue warp: residual tile load (RESID)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + C::EPI_WARPS);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int4* colp_all = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
+    void* silu_tab = reinterpret_cast<uint8_t*>(colp_all) + C::COLP_BYTES;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int num_m = (ep.M + 127) / 128, num_n = (ep.N + 127) / 128;
+    const int num_m = (ep.M + 127) / 128, num_n = (ep.N + C::BN - 1) / C::BN;
     const int tiles = num_m * num_n;
     const int KB = (ep.K + 127) / 128;
 
@@ -252,6 +530,7 @@ __global__ void __launch_bounds__(GemmCfg<P>::THREADS, 1)
         for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int b = 0; b < C::NB; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], C::EPI_WARPS); }
         mbar_init(drain, 1);
+        for (int w = 0; w < C::EPI_WARPS; ++w) mbar_init(&xbar[w], 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -278,7 +557,7 @@ __global__ void __launch_bounds__(GemmCfg<P>::THREADS, 1)
                     mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
 #pragma unroll
                     for (int p = 0; p < P; ++p) tma_load_3d(sA + p * C::A_BYTES, &tmA, &full[stage], kb * 128, m_blk * 128, p);
-                    tma_load_2d(sB, &tmB, &full[stage], kb * 128, n_blk * 128);
+                    tma_load_2d(sB, &tmB, &full[stage], kb * 128, n_blk * C::BN);
                     ++fills;
                     if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
                 }
@@ -307,7 +586,7 @@ __global__ void __launch_bounds__(GemmCfg<P>::THREADS, 1)
                 const uint32_t acc_phase = (acc_iter / C::NB) & 1;
                 if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort, ep.err, ERR_TIMEOUT_MMA_ACC)) { ok = false; break; }
                 tc_fence_after();
-                const int n_valid = min(128, ep.N - n_blk * 128);
+                const int n_valid = min(C::BN, ep.N - n_blk * C::BN);
                 const uint32_t id_lo = idesc_i8(false, true, n_valid);
                 const uint32_t id_hi = idesc_i8(true, true, n_valid);
                 const uint32_t dbase = tmem_base + buf * C::ACC_COLS;
@@ -322,7 +601,7 @@ __global__ void __launch_bounds__(GemmCfg<P>::THREADS, 1)
 #pragma unroll
                         for (int p = 0; p < P; ++p) {
                             const uint64_t adesc = smem_desc_sw128(sA + p * C::A_BYTES + ks * 32);
-                            mma_i8(dbase + p * 128, adesc, bdesc, p == P - 1 ? id_hi : id_lo,
+                            mma_i8(dbase + p * C::BN, adesc, bdesc, p == P - 1 ? id_hi : id_lo,
                                    (kb > 0 || ks > 0) ? 1u : 0u);
                         }
                     }
@@ -342,21 +621,61 @@ __global__ void __launch_bounds__(GemmCfg<P>::THREADS, 1)
         }
     } else {
         const int e = warp - 2;
+        const int et = threadIdx.x - 64;  // 0 .. 511
         const int quad = warp & 3;
-        const int half = e >> 2;
+        const int cg = e >> 2;
+        uint8_t* stg = staging + e * C::STG_BYTES;
+        const EpiMaps maps{&tmC0, &tmC1, &tmC2};
+        uint32_t xphase = 0;
+        if constexpr (KIND == EPI_GATEUP) {
+            if (ep.silu_smem) {  // stage the compact SiLU table once per CTA
+                const int nbytes = ep.silu_count * (ep.silu_wide ? 4 : 2);
+                const int n16 = (nbytes + 15) / 16;
+                for (int q = et; q < n16; q += C::EPI_THREADS)
+                    reinterpret_cast<int4*>(silu_tab)[q] = __ldg(reinterpret_cast<const int4*>(ep.silu_neg) + q);
+            }
+        }
         int acc_iter = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++acc_iter) {
             const int m_blk = t / num_n, n_blk = t % num_n;
             const int buf = acc_iter % C::NB;
             const uint32_t acc_phase = (acc_iter / C::NB) & 1;
-            if (!mbar_wait(&acc_full[buf], acc_phase, abort, ep.err, ERR_TIMEOUT_EPI)) break;
+            // Per-tile column parameters, double buffered: a warp that writes buffer b for this tile
+            // has passed the previous tile's barrier, so every warp is done with tile - 2.  The
+            // barrier below also publishes the staged SiLU table before the first tile.
+            int4* colp = colp_all + (acc_iter & 1) * C::BN;
+            if (et < C::BN) {
+                const int c = n_blk * C::BN + et;
+                const int2 ms = c < ep.N ? __ldg(ep.msh + c) : make_int2(0, 1);
+                const int rnd = (ms.y >= 1 && ms.y <= 31) ? (1 << (ms.y - 1)) : 0;
+                colp[et] = make_int4(ms.x, ms.y, rnd, ms.x << 8);
+            }
+            // RESID: the residual tile of this warp (32 rows x BN/4 int32) goes into its staging buffer by
+            // TMA while the accumulators are being computed.
+            bool xload = false;
+            if constexpr (KIND == EPI_RESID) {
+                const int row0 = m_blk * 128 + quad * 32, gc0 = n_blk * C::BN + (C::BN / 4) * cg;
+                xload = row0 < ep.M && gc0 < ep.N;
+                if (xload && lane == 0) {
+                    bulk_wait_read0();
+                    mbar_arrive_expect_tx(&xbar[e], C::STG_BYTES);
+                    tma_load_2d(stg, &tmC0, &xbar[e], gc0, row0);
+                }
+            }
+            bool ok = mbar_wait(&acc_full[buf], acc_phase, abort, ep.err, ERR_TIMEOUT_EPI);
+            if (xload) {
+                ok = ok && mbar_wait(&xbar[e], xphase, abort, ep.err, ERR_TIMEOUT_EPI);
+                xphase ^= 1;
+            }
+            if (!epi_barrier_and(ok)) break;
             tc_fence_after();
             const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
-            epilogue_tile<P, KIND>(ep, tacc, m_blk, n_blk, half, quad, lane);
+            epilogue_tile<P, KIND>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
+        if (lane == 0) bulk_wait0();  // this warp's tile stores are complete before the CTA exits
     }
     tc_fence_before();
     __syncthreads();

@@ -13,7 +13,7 @@ constexpr int N_HEADS = 9, N_KV = 3, HEAD_DIM = 64, ROPE_POS = 512, DMAX = 12 * 
 constexpr int F_RES = 15, F_SCORE = 7;
 constexpr int64_t EPS_S = 6184753;  // round(1e-5 * 576 * 2^30), python/intref.py:37
 
-enum : int { ERR_BAD_TOKEN = 201 };
+enum : int { ERR_BAD_TOKEN = 201, ERR_BAD_SHIFT = 202 };
 
 // --------------------------------------------------------------------------- embedding
 // x[t,c] = RS(emb_q[id,c] * emb_m[id], emb_n[id] - 15)   (python/intref.py:163-166)
@@ -47,18 +47,29 @@ __global__ void k_embed(const int64_t* __restrict__ ids, int M, const int8_t* __
 
 // --------------------------------------------------------------------------- RMSNorm
 // Exact reciprocal root of python/intref.py:170-177 / c/intref.c:96-104:
-//   S = A 2^32 + B 2^17 + C = sum x^2 (exact, 128-bit), U = isqrt(floor(2^80 / (S + EPS_S))).
-// The quotient is < 2^58 (S + EPS_S >= 2^22); the root is seeded from a double square root and
-// then corrected with exact integer comparisons, so U is the exact integer square root.
-__device__ __forceinline__ int64_t norm_recip_root(int64_t A, int64_t B, int64_t C) {
+//   S = A 2^32 + B 2^17 + C = sum x^2 (exact, 128-bit), U = isqrt(floor(2^80 / Tt)), Tt = S + EPS_S.
+// For an integer u, u^2 <= floor(2^80 / Tt) iff u^2 Tt <= 2^80, so U is the largest u with
+// u^2 Tt <= 2^80.  It is seeded from 2^40 / sqrt(Tt) in double precision (within one of U, since
+// U < 2^29) and then corrected with exact 128-bit products, which avoids a 128-bit division.
+__host__ __device__ __forceinline__ bool sq_times_le_2p80(uint64_t u, unsigned __int128 Tt) {
+    const uint64_t u2 = u * u;  // u < 2^31 here, so u^2 < 2^62
+    const uint64_t th = static_cast<uint64_t>(Tt >> 64), tl = static_cast<uint64_t>(Tt);
+    const unsigned __int128 hi = static_cast<unsigned __int128>(u2) * th;
+    if (hi > (static_cast<unsigned __int128>(1) << 16)) return false;  // (hi << 64) > 2^80
+    const unsigned __int128 prod = (hi << 64) + static_cast<unsigned __int128>(u2) * tl;
+    return prod <= (static_cast<unsigned __int128>(1) << 80);
+}
+
+__host__ __device__ __forceinline__ int64_t norm_recip_root(int64_t A, int64_t B, int64_t C) {
     const __int128 S = static_cast<__int128>(A) * (static_cast<__int128>(1) << 32) +
                        static_cast<__int128>(B) * (static_cast<__int128>(1) << 17) + static_cast<__int128>(C);
     const unsigned __int128 Tt = static_cast<unsigned __int128>(S) + static_cast<unsigned __int128>(EPS_S);
-    const uint64_t q = static_cast<uint64_t>((static_cast<unsigned __int128>(1) << 80) / Tt);
-    uint64_t s = static_cast<uint64_t>(sqrt(static_cast<double>(q)));
-    while (s > 0 && s * s > q) --s;
-    while ((s + 1) * (s + 1) <= q) ++s;
-    return static_cast<int64_t>(s);
+    double est = 1099511627776.0 / sqrt(static_cast<double>(Tt));  // 2^40 / sqrt(Tt)
+    if (est > 2147483647.0) est = 2147483647.0;
+    uint64_t u = static_cast<uint64_t>(est);
+    while (u > 0 && !sq_times_le_2p80(u, Tt)) --u;
+    while (u < 2147483647u && sq_times_le_2p80(u + 1, Tt)) ++u;
+    return static_cast<int64_t>(u);
 }
 
 __device__ __forceinline__ int64_t warp_sum64(int64_t v) {
@@ -90,10 +101,37 @@ __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* _
     B = warp_sum64(B);
     C = warp_sum64(C);
     const int64_t U = norm_recip_root(A, B, C);
+    // Fast path (planes output, bits_out 16, 1 <= shift_out <= 31): z = RS(x U, 16) fits int32
+    // (|x U| <= 2^40, python/intref.py:178), 3 g fits int32, and RS(z 3 g, shift_out) is a funnel
+    // shift of one 32x32 -> 64 multiply-add.
+    const bool fast = planes && !out64 && P == 2 && bits_out == 16 && shift_out >= 1 && shift_out <= 31;
+    const int64_t rnd_out = (shift_out >= 1 && shift_out <= 62) ? (int64_t(1) << (shift_out - 1)) : 0;
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
         const int c = 64 * i + 2 * lane;
         const int2 g = __ldg(reinterpret_cast<const int2*>(gain) + 32 * i + lane);
+        if (fast) {
+            int32_t o[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int64_t xu = static_cast<int64_t>(u ? v[i].y : v[i].x) * U + 32768;
+                const int32_t z = static_cast<int32_t>(__funnelshift_r(static_cast<uint32_t>(xu),
+                                                                       static_cast<uint32_t>(static_cast<uint64_t>(xu) >> 32), 16));
+                const int64_t t = static_cast<int64_t>(z) * (3 * (u ? g.y : g.x)) + rnd_out;
+                const uint32_t tl = static_cast<uint32_t>(t), th = static_cast<uint32_t>(static_cast<uint64_t>(t) >> 32);
+                const uint32_t lo = __funnelshift_r(tl, th, shift_out);
+                const int32_t hi = static_cast<int32_t>(th) >> shift_out;
+                int32_t w = hi == (static_cast<int32_t>(lo) >> 31) ? static_cast<int32_t>(lo) : (hi < 0 ? INT32_MIN : INT32_MAX);
+                o[u] = min(max(w, -32768), 32767);
+            }
+            const uint32_t both = (static_cast<uint32_t>(o[0]) & 0xFFFFu) | (static_cast<uint32_t>(o[1]) << 16);
+            // bytes: [o0 lo, o0 hi, o1 lo, o1 hi] -> plane 0 gets (o0 lo, o1 lo), plane 1 (o0 hi, o1 hi)
+            *reinterpret_cast<uint16_t*>(planes + static_cast<int64_t>(row) * D_MODEL + c) =
+                static_cast<uint16_t>(__byte_perm(both, 0, 0x0020));
+            *reinterpret_cast<uint16_t*>(planes + (static_cast<int64_t>(M) + row) * D_MODEL + c) =
+                static_cast<uint16_t>(__byte_perm(both, 0, 0x0031));
+            continue;
+        }
         const int64_t z0 = rs64(static_cast<int64_t>(v[i].x) * U, 16), z1 = rs64(static_cast<int64_t>(v[i].y) * U, 16);
         const int64_t o0 = sat64(rs64(z0 * g.x * 3, shift_out), bits_out);
         const int64_t o1 = sat64(rs64(z1 * g.y * 3, shift_out), bits_out);

@@ -194,3 +194,34 @@ def test_forward_t128_cuda_core_attention(base_model, base_model_path, monkeypat
         _check_set(e, base_model, "t128")
     finally:
         e.close()
+
+
+@pytest.mark.parametrize("layer", [0, 11])
+def test_block_full_silu_table(base_model, base_model_path, monkeypatch, layer):
+    """The gate/up epilogue's fallback that gathers from the full 65536-entry SiLU table (used when
+    the compact shared-memory form does not apply) is exact too."""
+    import _eii
+    monkeypatch.setenv("EII_SILU", "global")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        T = 24
+        x = ofw.embed(base_model, synth.window_ids(64, T))
+        for l in range(layer):
+            x = ofw.block_batch(base_model, l, x, T)
+        want = ofw.block_batch(base_model, layer, x, T)
+        got = e.block(layer, x, T)
+        assert first_diff(got, want) is None, first_diff(got, want)
+    finally:
+        e.close()
+
+
+def test_forward_t24_generic_requant(base_model, base_model_path, monkeypatch):
+    """The int64 epilogue path (taken when a column shift is outside [1, 31] or a multiplier is
+    >= 2^15) gives the same integers as the fast 32-bit path."""
+    import _eii
+    monkeypatch.setenv("EII_GENERIC_REQUANT", "1")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        _check_set(e, base_model, "t24")
+    finally:
+        e.close()

@@ -103,3 +103,22 @@ def test_reference_c_program_accepts_oracle_vectors(base_model, base_model_path,
     r = subprocess.run([REF_BIN, str(tmp_path)], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "ALL STATES EXACT" in r.stdout
+
+
+def test_silu_tables_obey_the_odd_part_identity(base_model):
+    """silu(x) - silu(-x) = x, so each rounded table satisfies tab[g] = SAT(tab[-g] + g 2^(f_s-f_g))
+    for g > 0 when f_s >= f_g; the engine keeps only the negative half in shared memory when this
+    holds for every input (and verifies it itself at load)."""
+    checked = 0
+    for Ly in base_model["layers"]:
+        F = ofw.fm_unpack(Ly["fm"])
+        (_, f_g), (bits_s, f_s) = F["g"], F["s"]
+        d = f_s - f_g
+        if d < 0:
+            continue
+        tab = np.asarray(Ly["silu"], dtype=np.int64)
+        g = np.arange(1, 32768, dtype=np.int64)
+        pred = ofw.sat(tab[32768 - g] + (g << d), bits_s)
+        assert np.array_equal(pred, tab[32768 + g])
+        checked += 1
+    assert checked == 30
