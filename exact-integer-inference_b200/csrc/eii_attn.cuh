@@ -36,8 +36,19 @@ constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + (DMAX + 1 + 3) * 4 + 4 * 
 __device__ __forceinline__ int sw128(int r, int b) { return r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15); }
 
 
-// floor((e * 65536 + floor(Z/2)) / Z) for 0 <= e <= 2^30, 2^30 <= Z < 2^40: double estimate, then
-// integer-remainder correction (the estimate is within one of the quotient, which is < 2^17 + 1).
+// floor((e * 65536 + floor(Z/2)) / Z) for 0 <= e <= 2^30, 2^30 <= Z < 2^40.
+// n / Z = e (65536 / Z) + floor(Z/2) / Z, the second term in (0.5 - 1/(2Z), 0.5]; in fp32 the
+// estimate e * (65536 / Z) + 0.5 has absolute error < 0.05 (quotient < 2^17), so its floor is within
+// one of the true quotient, which the integer remainder r = n - q Z then fixes exactly.
+__device__ __forceinline__ int32_t prob_q16_f32(int32_t e, int64_t Z, int64_t halfZ, float scale) {
+    const int64_t n = static_cast<int64_t>(e) * 65536 + halfZ;
+    int32_t q = __float2int_rd(__fmaf_rn(static_cast<float>(e), scale, 0.5f));
+    const int64_t r = n - static_cast<int64_t>(q) * Z;
+    if (r < 0) --q;
+    else if (r >= Z) ++q;
+    return q;
+}
+
 __device__ __forceinline__ int64_t prob_q16(int64_t e, int64_t Z, int64_t halfZ, double rz) {
     const int64_t n = e * 65536 + halfZ;
     int64_t p = static_cast<int64_t>(static_cast<double>(n) * rz);
@@ -126,6 +137,8 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     const uint32_t sP0 = smem_u32(Ps), sP1 = smem_u32(Ps + ATTN_TC_TILE);
     // key block kb holds keys 32 kb .. 32 kb + 31; it has unmasked keys for this quadrant iff kb <= quad
     const bool active = kb <= quad;
+    const bool fast = ap.shift_s >= 1 && ap.shift_s <= 31;
+    const int64_t srnd = fast ? (int64_t(1) << (ap.shift_s - 1)) : 0;
 
     for (int h = 0; h < 3; ++h) {
         // ---- S = Q_h K^T (M = 128 queries, N = 128 keys, K = 64 dims per plane pair)
@@ -165,10 +178,23 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                     int32_t s2[2];
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
-                        const int64_t S = static_cast<int64_t>(static_cast<int32_t>(d2[q + u])) * 65536 +
-                                          static_cast<int64_t>(static_cast<int32_t>(d1[q + u])) * 256 +
-                                          static_cast<int64_t>(static_cast<int32_t>(d0[q + u]));
-                        s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
+                        if (fast) {
+                            // S + 2^(shift-1) from the three plane sums with 32x32 -> 64 multiply-adds
+                            const int64_t t = static_cast<int64_t>(static_cast<int32_t>(d2[q + u])) * 65536 +
+                                              (static_cast<int64_t>(static_cast<int32_t>(d1[q + u])) * 256 +
+                                               (static_cast<int64_t>(static_cast<int32_t>(d0[q + u])) + srnd));
+                            const uint32_t tl = static_cast<uint32_t>(t), th = static_cast<uint32_t>(static_cast<uint64_t>(t) >> 32);
+                            const uint32_t lo = __funnelshift_r(tl, th, ap.shift_s);
+                            const int32_t hi = static_cast<int32_t>(th) >> ap.shift_s;
+                            const int32_t w = hi == (static_cast<int32_t>(lo) >> 31) ? static_cast<int32_t>(lo)
+                                                                                     : (hi < 0 ? INT32_MIN : INT32_MAX);
+                            s2[u] = min(max(w, -32768), 32767);
+                        } else {
+                            const int64_t S = static_cast<int64_t>(static_cast<int32_t>(d2[q + u])) * 65536 +
+                                              static_cast<int64_t>(static_cast<int32_t>(d1[q + u])) * 256 +
+                                              static_cast<int64_t>(static_cast<int32_t>(d0[q + u]));
+                            s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
+                        }
                         if (col + q + u <= i) lmax = max(lmax, s2[u]);
                     }
                     sp[(c * 16 + q) / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
@@ -199,7 +225,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
         // ---- pass 3: probabilities of my keys -> u8 planes of P mod 65536 (+ the P == 65536 key)
         {
             const int64_t halfZ = Z / 2;
-            const double rz = Z > 0 ? 1.0 / static_cast<double>(Z) : 0.0;
+            const float scale = Z > 0 ? static_cast<float>(65536.0 / static_cast<double>(Z)) : 0.f;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint8_t b0[16], b1[16];
@@ -211,7 +237,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                     if (active && i < T) {
                         const int32_t s = static_cast<int16_t>((qq & 1) ? (sp[qq / 2] >> 16) : (sp[qq / 2] & 0xFFFF));
                         const int32_t dd = rowmax - s;
-                        if (j <= i && dd <= DMAX) p = prob_q16(E[dd], Z, halfZ, rz);
+                        if (j <= i && dd <= DMAX) p = prob_q16_f32(E[dd], Z, halfZ, scale);
                     }
                     if (p == 65536) jstar_s[i] = j;
                     b0[q] = static_cast<uint8_t>(p & 0xFF);

@@ -21,7 +21,8 @@ static uint64_t isqrt_ref(unsigned __int128 Tt) {
     return lo;
 }
 
-// Same estimate-and-correct division as the attention kernels (host copy of prob_q16).
+// Same estimate-and-correct divisions as the attention kernels (host copies of prob_q16 and
+// prob_q16_f32: fmaf is correctly rounded on the host as __fmaf_rn is on the device).
 static int64_t prob_ref(int64_t e, int64_t Z) { return (e * 65536 + Z / 2) / Z; }
 static int64_t prob_fast(int64_t e, int64_t Z) {
     const int64_t n = e * 65536 + Z / 2;
@@ -33,6 +34,16 @@ static int64_t prob_fast(int64_t e, int64_t Z) {
     if (r >= Z) { ++p; r -= Z; }
     if (r >= Z) { ++p; }
     return p;
+}
+
+static int64_t prob_fast32(int64_t e, int64_t Z) {
+    const int64_t n = e * 65536 + Z / 2;
+    const float scale = static_cast<float>(65536.0 / static_cast<double>(Z));
+    int64_t q = static_cast<int64_t>(floorf(fmaf(static_cast<float>(e), scale, 0.5f)));
+    const int64_t r = n - q * Z;
+    if (r < 0) --q;
+    else if (r >= Z) ++q;
+    return q;
 }
 
 int main(int argc, char** argv) {
@@ -63,6 +74,15 @@ int main(int argc, char** argv) {
         const int64_t e = static_cast<int64_t>(rng() % ((int64_t(1) << 30) + 1));
         ++n;
         if (prob_fast(e, Z) != prob_ref(e, Z)) ++bad;
+        ++n;
+        if (prob_fast32(e, Z) != prob_ref(e, Z)) ++bad;
+        const int64_t e2 = static_cast<int64_t>(rng() % 1537);  // small e and e = Z exactly (P = 65536)
+        ++n;
+        if (prob_fast32(e2, Z) != prob_ref(e2, Z)) ++bad;
+        const int64_t zs = int64_t(1) << 30;
+        ++n;
+        const int64_t z2 = zs + static_cast<int64_t>(rng() % 4);  // a row whose maximum dominates: P near 65536
+        if (prob_fast32(zs, z2) != prob_ref(zs, z2)) ++bad;
     }
     printf("checked %ld, mismatches %ld\n", n, bad);
     return bad != 0;
