@@ -86,7 +86,7 @@ struct LayerDev {
     int fast_qkv, fast_o, fast_gu, fast_d;  // fast requantisation path applies (see EpiParams::fast)
     int8_t *w_qkv, *w_o, *w_gu, *w_d;
     int2 *msh_qkv, *msh_o, *msh_gu, *msh_d;
-    CUtensorMap tm_qkv, tm_o, tm_gu, tm_d, tm_o64, tm_d64;  // *64: 64-row boxes for 4-plane GEMMs
+    CUtensorMap tm_qkv, tm_o, tm_gu, tm_d, tm_o64, tm_d64;  // *64: boxes of BN_P4 rows for 4-plane GEMMs
 };
 
 struct ActMaps {
@@ -687,7 +687,7 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
             TRY(upload(e, &L.w_o, wq[3], (size_t)D_MODEL * D_MODEL));
             TRY(upload(e, &L.msh_o, msh.data(), D_MODEL));
             TRY(map_2d(&L.tm_o, L.w_o, D_MODEL, D_MODEL));
-            TRY(map_2d(&L.tm_o64, L.w_o, D_MODEL, D_MODEL, 64));
+            TRY(map_2d(&L.tm_o64, L.w_o, D_MODEL, D_MODEL, BN_P4));
         }
         // gate / up interleaved per 128-row tile
         {
@@ -717,7 +717,7 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
             TRY(upload(e, &L.w_d, wq[6], (size_t)D_MODEL * D_FF));
             TRY(upload(e, &L.msh_d, msh.data(), D_MODEL));
             TRY(map_2d(&L.tm_d, L.w_d, D_FF, D_MODEL));
-            TRY(map_2d(&L.tm_d64, L.w_d, D_FF, D_MODEL, 64));
+            TRY(map_2d(&L.tm_d64, L.w_d, D_FF, D_MODEL, BN_P4));
         }
     }
     if (r.left != 0) return fail(EII_ERR_IO, "model.bin has %zu trailing bytes", r.left);
@@ -1048,7 +1048,7 @@ int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const
                          cudaMemcpy(msh_dev, msh.data(), (size_t)N * sizeof(int2), cudaMemcpyHostToDevice) != cudaSuccess))
         rc = fail(EII_ERR_CUDA, "upload failed");
     CUtensorMap tmB;
-    if (rc == EII_OK) rc = map_2d(&tmB, w_dev, K, N, bits_in == 32 ? 64 : 128);
+    if (rc == EII_OK) rc = map_2d(&tmB, w_dev, K, N, bits_in == 32 ? BN_P4 : 128);
     if (rc == EII_OK) rc = linear_device(e, a_dev, M, K, bits_in, tmB, msh_dev, N, bits_out, out_dev, acc_dev, tmp);
     if (rc == EII_OK && cudaMemcpyAsync(out, out_dev, (size_t)M * N * 8, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
         rc = fail(EII_ERR_CUDA, "download failed");
@@ -1168,7 +1168,7 @@ extern "C" int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_i
     CK(cudaGetLastError());
     CUtensorMap tmA, tmB;
     TRY(map_planes(&tmA, d->planes, K, M, P));
-    TRY(map_2d(&tmB, w_dev, K, N, bits_in == 32 ? 64 : 128));
+    TRY(map_2d(&tmB, w_dev, K, N, bits_in == 32 ? BN_P4 : 128));
     EpiParams ep{};
     ep.M = M; ep.N = N; ep.K = K; ep.msh = d->msh; ep.err = d->err; ep.out64 = out_dev; ep.acc64 = acc_dev;
     ep.bits_out = bits_out;

@@ -78,12 +78,16 @@ struct EpiParams {
 
 constexpr int SILU_SMEM_BYTES = 48 * 1024;  // compact SiLU table capacity (int16 x 24576 or int32 x 12288)
 constexpr int SMEM_LIMIT = 227 * 1024;
+// N-tile width of the 4-plane GEMMs (down, and O at INT32 attn_ctx layers).  128 keeps their
+// operand traffic from L2 at the level of the 2-plane GEMMs (the mainloops are L2-bound) at the
+// price of a single TMEM accumulator set; 64 would double-buffer the accumulators.
+constexpr int BN_P4 = 128;
 
 template <int P, int KIND>
 struct GemmCfg {
     // P = 4 uses 64-wide N tiles so that two accumulator sets (2 x 4 x 64 columns) fit in TMEM and the
     // epilogue of one tile overlaps the MMAs of the next.
-    static constexpr int BM = 128, BN = (P == 4) ? 64 : 128, BK = 128;
+    static constexpr int BM = 128, BN = (P == 4) ? BN_P4 : 128, BK = 128;
     static constexpr int ACC_COLS = P * BN;
     static constexpr int NB = 512 / ACC_COLS;  // accumulator sets in TMEM
     static constexpr int A_BYTES = BM * BK;
@@ -91,9 +95,11 @@ struct GemmCfg {
     static constexpr int STAGE_BYTES = P * A_BYTES + B_BYTES;
     // Per-warp staging buffer for TMA tile stores (and the residual tile load): 32 rows x the warp's
     // columns.  LOGITS/RESID: int32, BN/4 columns; QKV: two 32-row x 16 int16 boxes.
-    static constexpr int STG_BYTES = (KIND == EPI_LOGITS || KIND == EPI_RESID) ? (BN / 4) * 4 * 32
+    // RESID with 4 planes and 128-wide tiles keeps one 16-column chunk resident (2 KB) to fit.
+    static constexpr int STG_BYTES = KIND == EPI_LOGITS ? (BN / 4) * 4 * 32
+                                     : KIND == EPI_RESID ? ((P == 4 && BN == 128) ? 2048 : (BN / 4) * 4 * 32)
                                      : (KIND == EPI_QKV ? 2048 : 0);
-    static constexpr int STAGES = (P == 2) ? (KIND == EPI_LINEAR ? 4 : 3) : (KIND == EPI_LINEAR ? 3 : 2);
+    static constexpr int STAGES = (P == 2) ? (KIND == EPI_LINEAR ? 4 : 3) : (BN == 128 ? 2 : 3);
     static constexpr int EPI_WARPS = 16;  // 4 per TMEM lane quadrant, each owns 32 tile columns
     static constexpr int EPI_THREADS = 32 * EPI_WARPS;
     static constexpr int THREADS = 64 + EPI_THREADS;
@@ -129,7 +135,7 @@ __device__ __forceinline__ bool epi_barrier_and(bool v) {
 template <int P, int N>
 __device__ __forceinline__ void load_planes(uint32_t taddr, uint32_t (&v)[P][N]) {
     static_assert(N == 8 || N == 16, "8 or 16 columns");
-    constexpr int PS = (P == 4) ? 64 : 128;
+    constexpr int PS = (P == 4) ? BN_P4 : 128;
 #pragma unroll
     for (int p = 0; p < P; ++p) {
         if constexpr (N == 16) tmem_ld16(taddr + p * PS, v[p]);
@@ -290,8 +296,9 @@ struct EpiMaps {
 template <int P, int KIND>
 __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc, int m_blk, int n_blk, int cg,
                                               int quad, int lane, const int4* colp, const void* silu_tab,
-                                              uint8_t* stg, const EpiMaps& maps) {
-    constexpr int BN = (P == 4) ? 64 : 128;
+                                              uint8_t* stg, const EpiMaps& maps, uint64_t* xbar, uint32_t& xphase,
+                                              volatile int* abort) {
+    constexpr int BN = (P == 4) ? BN_P4 : 128;
     const int row = m_blk * 128 + quad * 32 + lane;
     const bool row_ok = row < ep.M;
     const int n0 = n_blk * BN;
@@ -421,26 +428,37 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
             store_planes<8>(ep.gated_planes + static_cast<int64_t>(row) * Nh + j0 + h8, static_cast<int64_t>(ep.M) * Nh,
                             ep.gated_P, gm);
         }
-    } else {
-        constexpr int NCOL = BN / 4;  // columns of this warp: 32 (P = 2) or 16 (P = 4)
-        if constexpr (KIND == EPI_LOGITS) {
-            if (lane == 0) bulk_wait_read0();  // the previous tile's store has read the staging buffer
-            __syncwarp();
-        }
+    } else if constexpr (KIND == EPI_RESID) {
+        // x = SAT32(x + RS(acc m, shift)) on this warp's 32 rows x NCOL columns.  The residual tile is
+        // in the staging buffer (TMA load issued before the accumulator wait); with one resident
+        // 16-column chunk (XCH == 1) the second chunk is loaded after the first is stored.
+        constexpr int NCOL = BN / 4, NCH = NCOL / 16;
+        constexpr int XCH = GemmCfg<P, KIND>::STG_BYTES / 2048;
+        constexpr int S = XCH * 64;  // staging row bytes
+        const int row0 = m_blk * 128 + quad * 32;
+        const bool live = row0 < ep.M;
 #pragma unroll 1
-        for (int ch = 0; ch < NCOL / 16; ++ch) {
+        for (int ch = 0; ch < NCH; ++ch) {
             const int tc = NCOL * cg + 16 * ch;
             const int gc = n0 + tc;
             if (gc >= ep.N) break;
+            const int slot = XCH == 1 ? 0 : ch;
+            if (XCH == 1 && ch > 0 && live) {
+                if (lane == 0) {
+                    bulk_wait_read0();
+                    mbar_arrive_expect_tx(xbar, 2048);
+                    tma_load_2d(stg, maps.c0, xbar, gc, row0);
+                }
+                if (!mbar_wait(xbar, xphase, abort, ep.err, ERR_TIMEOUT_EPI)) return;
+                xphase ^= 1;
+            }
             uint32_t v[P][16];
             load_planes<P, 16>(tacc + tc, v);
-            if (!row_ok) continue;
-            if constexpr (KIND == EPI_RESID) {
-                // the residual tile was loaded into the staging buffer (TMA) before the accumulator wait
+            if (row_ok) {
                 int32_t xo[16];
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<int4*>(&xo[4 * q]) = *reinterpret_cast<const int4*>(stg + stg_off<NCOL * 4>(lane, 4 * ch + q));
+                    *reinterpret_cast<int4*>(&xo[4 * q]) = *reinterpret_cast<const int4*>(stg + stg_off<S>(lane, 4 * slot + q));
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int4 cp = colp[tc + i];
@@ -458,8 +476,41 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 }
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<int4*>(stg + stg_off<NCOL * 4>(lane, 4 * ch + q)) = *reinterpret_cast<int4*>(&xo[4 * q]);
-            } else if constexpr (KIND == EPI_LOGITS) {
+                    *reinterpret_cast<int4*>(stg + stg_off<S>(lane, 4 * slot + q)) = *reinterpret_cast<int4*>(&xo[4 * q]);
+            }
+            if (XCH == 1) {
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0 && live) {
+                    tma_store_2d(maps.c0, stg, gc, row0);
+                    bulk_commit();
+                }
+            }
+        }
+        if (XCH > 1) {
+            fence_async_smem();
+            __syncwarp();
+            const int gc0 = n0 + NCOL * cg;
+            if (lane == 0 && live && gc0 < ep.N) {
+                tma_store_2d(maps.c0, stg, gc0, row0);
+                bulk_commit();
+            }
+        }
+    } else {
+        constexpr int NCOL = BN / 4;  // columns of this warp: 32 (P = 2) or 16 (P = 4)
+        if constexpr (KIND == EPI_LOGITS) {
+            if (lane == 0) bulk_wait_read0();  // the previous tile's store has read the staging buffer
+            __syncwarp();
+        }
+#pragma unroll 1
+        for (int ch = 0; ch < NCOL / 16; ++ch) {
+            const int tc = NCOL * cg + 16 * ch;
+            const int gc = n0 + tc;
+            if (gc >= ep.N) break;
+            uint32_t v[P][16];
+            load_planes<P, 16>(tacc + tc, v);
+            if (!row_ok) continue;
+            if constexpr (KIND == EPI_LOGITS) {
                 int32_t o[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
@@ -487,7 +538,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 }
             }
         }
-        if constexpr (KIND == EPI_LOGITS || KIND == EPI_RESID) {
+        if constexpr (KIND == EPI_LOGITS) {
             fence_async_smem();
             __syncwarp();
             const int row0 = m_blk * 128 + quad * 32, gc0 = n0 + NCOL * cg;
@@ -670,7 +721,8 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             if (!epi_barrier_and(ok)) break;
             tc_fence_after();
             const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
-            epilogue_tile<P, KIND>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps);
+            epilogue_tile<P, KIND>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e], xphase,
+                                   abort);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
