@@ -18,6 +18,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cerrno>
 #include <cstdarg>
@@ -84,6 +85,7 @@ struct LayerDev {
     void* silu_neg;  // compact SiLU table (negative half, dense range) or null
     int silu_lo, silu_count, silu_wide, silu_d;
     int fast_qkv, fast_o, fast_gu, fast_d;  // fast requantisation path applies (see EpiParams::fast)
+    int narrow_qkv, narrow_gu;              // requantised values provably fit int32 (EpiParams::narrow)
     int8_t *w_qkv, *w_o, *w_gu, *w_d;
     int2 *msh_qkv, *msh_o, *msh_gu, *msh_d;
     CUtensorMap tm_qkv, tm_o, tm_gu, tm_d, tm_o64, tm_d64;  // *64: boxes of BN_P4 rows for 4-plane GEMMs
@@ -402,7 +404,7 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     ep.M = rows; ep.N = 960; ep.K = D_MODEL; ep.msh = L.msh_qkv; ep.err = e->err_dev;
     ep.T = T; ep.q_out = e->q; ep.k_out = e->k; ep.v_out = e->v; ep.rope_c = e->rope_c; ep.rope_s = e->rope_s;
     ep.bits_q = L.q.bits; ep.bits_k = L.k.bits; ep.bits_v = L.v.bits; ep.bits_qr = L.qr.bits; ep.bits_kr = L.kr.bits;
-    ep.rope_shift_q = L.rope_shift_q; ep.rope_shift_k = L.rope_shift_k; ep.fast = L.fast_qkv;
+    ep.rope_shift_q = L.rope_shift_q; ep.rope_shift_k = L.rope_shift_k; ep.fast = L.fast_qkv; ep.narrow = L.narrow_qkv;
     TRY(launch_gemm<2, EPI_QKV>(e, am->h, L.tm_qkv, ep, st, EII_K_GEMM_QKV, &am->q, &am->k, &am->v));
 
     AttnParams ap{};
@@ -429,7 +431,7 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     ep.silu = L.silu; ep.bits_g = L.g.bits; ep.bits_u = L.u.bits; ep.gated_shift = L.gated_shift;
     ep.silu_neg = L.silu_neg; ep.silu_smem = L.silu_neg != nullptr; ep.silu_lo = L.silu_lo;
     ep.silu_count = L.silu_count; ep.silu_wide = L.silu_wide; ep.silu_d = L.silu_d; ep.bits_s = L.s.bits;
-    ep.fast = L.fast_gu;
+    ep.fast = L.fast_gu; ep.narrow = L.narrow_gu;
     ep.bits_m = L.m.bits; ep.gated_P = L.Pm; ep.gated_planes = e->gated_planes;
     TRY(launch_gemm<2, EPI_GATEUP>(e, am->h, L.tm_gu, ep, st, EII_K_GEMM_GATEUP));
 
@@ -554,6 +556,20 @@ int compact_silu(eii_engine* e, LayerDev& L, const int64_t* tab) {
     return EII_OK;
 }
 
+// True when, for every output column j of int8 weight rows w (K per row), an activation of magnitude
+// at most amax gives |acc m_j| + 2^(sh_j - 1) < 2^(31 + sh_j): RS(acc m_j, sh_j) then fits int32.
+bool cols_narrow(const int8_t* w, int N, int K, const std::vector<int2>& msh, int64_t amax) {
+    for (int j = 0; j < N; ++j) {
+        int64_t l1 = 0;
+        for (int k = 0; k < K; ++k) l1 += std::abs(static_cast<int>(w[(size_t)j * K + k]));
+        const int sh = msh[j].y;
+        if (sh < 1 || sh > 31 || msh[j].x < 0) return false;
+        const __int128 bound = static_cast<__int128>(amax) * l1 * msh[j].x + (static_cast<__int128>(1) << (sh - 1));
+        if (bound >= (static_cast<__int128>(1) << (31 + sh))) return false;
+    }
+    return true;
+}
+
 // The fast epilogue path needs every column shift in [1, 31] and every multiplier in [0, 2^15).
 bool cols_fast(const std::vector<int2>& msh) {
     for (const int2& c : msh)
@@ -597,6 +613,8 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
     e->final_shift = 21 + e->final_f - e->f_y;
     TRY(narrow32(expt, DMAX + 1, tmp, "exp_table"));
     TRY(upload(e, &e->exp_tab, tmp.data(), DMAX + 1));
+    int64_t rope_max = 0;
+    for (int i = 0; i < ROPE_POS * 32; ++i) rope_max = std::max(rope_max, std::max(std::abs(rc[i]), std::abs(rsn[i])));
     TRY(narrow32(rc, ROPE_POS * 32, tmp, "rope_cos"));
     TRY(upload(e, &e->rope_c, tmp.data(), ROPE_POS * 32));
     TRY(narrow32(rsn, ROPE_POS * 32, tmp, "rope_sin"));
@@ -674,6 +692,9 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
             TRY(check_col_shifts(msh, "q/k/v", l));
             L.fast_qkv = cols_fast(msh) && L.rope_shift_q >= 1 && L.rope_shift_q <= 31 && L.rope_shift_k >= 1 &&
                          L.rope_shift_k <= 31;
+            // RoPE: |a c - b s| <= 2 * 2^15 * 2^30 (tables are Q30), so shifts >= 16 keep it in int32
+            L.narrow_qkv = L.fast_qkv && cols_narrow(w.data(), 960, D_MODEL, msh, 32768) && L.rope_shift_q >= 16 &&
+                           L.rope_shift_k >= 16 && rope_max <= (int64_t(1) << 30);
             TRY(upload(e, &L.w_qkv, w.data(), w.size()));
             TRY(upload(e, &L.msh_qkv, msh.data(), 960));
             TRY(map_2d(&L.tm_qkv, L.w_qkv, D_MODEL, 960));
@@ -704,6 +725,7 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
             }
             TRY(check_col_shifts(msh, "gate/up", l));
             L.fast_gu = cols_fast(msh) && L.gated_shift >= 0 && L.gated_shift <= 31;
+            L.narrow_gu = L.fast_gu && cols_narrow(w.data(), 2 * D_FF, D_MODEL, msh, 32768);
             TRY(upload(e, &L.w_gu, w.data(), w.size()));
             TRY(upload(e, &L.msh_gu, msh.data(), 2 * D_FF));
             TRY(map_2d(&L.tm_gu, L.w_gu, D_MODEL, 2 * D_FF));
@@ -745,8 +767,10 @@ int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
     if (rc == EII_OK) rc = load_model(e, static_cast<const uint8_t*>(data), nbytes);
     if (rc == EII_OK && getenv("EII_GENERIC_REQUANT")) {  // test switch: always take the int64 epilogue path
         e->fast_logits = 0;
-        for (LayerDev& L : e->L) L.fast_qkv = L.fast_o = L.fast_gu = L.fast_d = 0;
+        for (LayerDev& L : e->L) L.fast_qkv = L.fast_o = L.fast_gu = L.fast_d = L.narrow_qkv = L.narrow_gu = 0;
     }
+    if (rc == EII_OK && getenv("EII_NO_NARROW"))  // test switch: keep the 64-bit saturation tests
+        for (LayerDev& L : e->L) L.narrow_qkv = L.narrow_gu = 0;
     if (rc == EII_OK && (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               attn_smem_bytes(ROPE_POS)) != cudaSuccess ||
                          cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,

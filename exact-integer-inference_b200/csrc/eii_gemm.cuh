@@ -65,6 +65,10 @@ struct EpiParams {
     // [1, 31] and the gated-product shift in [0, 31]: requantisation then runs on 32x32->64
     // multiply-adds and 32-bit funnel shifts; otherwise the generic int64 path is taken.
     int fast;
+    // narrow = for every column, |acc m| + 2^(shift-1) < 2^(31 + shift) (checked on the host from the
+    // L1 norm of each weight row and the activation range), so RS(acc m, shift) fits int32 and
+    // needs no 64-bit saturation test; the RoPE shifts are >= 16 for the same reason.
+    int narrow;
     int bits_g, bits_u, gated_shift, bits_m, gated_P;
     uint8_t* gated_planes;  // [gated_P][M][N/2]
     // EPI_LOGITS: int32 out[row * ld + col] = RS(acc m, shift) (low 32 bits, no SAT)
@@ -191,6 +195,15 @@ __device__ __forceinline__ int32_t sat_hl(int32_t hi, uint32_t lo, int bits) {
     return v;
 }
 
+// Narrow requantisation: RS(acc m, sh) is known to fit int32 (EpiParams::narrow).
+template <int P, int N>
+__device__ __forceinline__ int32_t rs_narrow(const uint32_t (&v)[P][N], int i, int4 cp) {
+    const int64_t t = mulround<P, N>(v, i, cp);
+    return static_cast<int32_t>(
+        __funnelshift_r(static_cast<uint32_t>(t), static_cast<uint32_t>(static_cast<uint64_t>(t) >> 32), cp.y));
+}
+__device__ __forceinline__ int32_t clamp16(int32_t v) { return min(max(v, -32768), 32767); }
+
 // Fast requantisation of one element: SAT_bits(RS(acc m, sh)).
 template <int P, int N>
 __device__ __forceinline__ int32_t requant_fast(const uint32_t (&v)[P][N], int i, int4 cp, int bits) {
@@ -251,14 +264,14 @@ __device__ __forceinline__ void store_planes(uint8_t* base, int64_t plane_stride
 
 // Gate/up/SiLU/gated product for 16 features, all-32-bit path: INT16 gate and up, compact INT16
 // SiLU table with shift d <= 15 (so g * 2^d < 2^31), gated shift in [0, 31].
-template <int P, int N, int BITS_M>
+template <int P, int N, int BITS_M, bool NARROW>
 __device__ __forceinline__ void gateup_lean(const uint32_t (&vg)[P][N], const uint32_t (&vu)[P][N], const int4* cpg,
                                             const int4* cpu, const int16_t* tab, int lo_g, int d, int gs, int64_t grnd,
                                             int32_t (&gm)[N]) {
 #pragma unroll
     for (int i = 0; i < N; ++i) {
-        const int32_t g = requant_fast<P, N>(vg, i, cpg[i], 16);
-        const int32_t u = requant_fast<P, N>(vu, i, cpu[i], 16);
+        const int32_t g = NARROW ? clamp16(rs_narrow<P, N>(vg, i, cpg[i])) : requant_fast<P, N>(vg, i, cpg[i], 16);
+        const int32_t u = NARROW ? clamp16(rs_narrow<P, N>(vu, i, cpu[i])) : requant_fast<P, N>(vu, i, cpu[i], 16);
         const int32_t a = min(g, -g);
         int32_t sg = a >= lo_g ? static_cast<int32_t>(tab[a - lo_g]) : 0;
         if (g > 0) sg = min(max(sg + (g << d), -32768), 32767);
@@ -343,7 +356,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
             for (int i = 0; i < 8; ++i) {
                 const int4 ca = colp[64 * hl + d0 + i], cb = colp[64 * hl + 32 + d0 + i];
                 int32_t a, b;
-                if (ep.fast) {
+                if (ep.narrow) {
+                    a = clamp16(rs_narrow<P, 8>(va, i, ca));
+                    b = clamp16(rs_narrow<P, 8>(vb, i, cb));
+                } else if (ep.fast) {
                     a = requant_fast<P, 8>(va, i, ca, bits_in);
                     b = requant_fast<P, 8>(vb, i, cb, bits_in);
                 } else {
@@ -353,7 +369,13 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 if (region < 2) {
                     const int64_t t1 = static_cast<int64_t>(a) * rc[i] - static_cast<int64_t>(b) * rsn[i];
                     const int64_t t2 = static_cast<int64_t>(b) * rc[i] + static_cast<int64_t>(a) * rsn[i];
-                    if (ep.fast) {
+                    if (ep.narrow) {
+                        const int64_t u1 = t1 + rrnd, u2 = t2 + rrnd;
+                        oa[i] = static_cast<int16_t>(clamp16(static_cast<int32_t>(__funnelshift_r(
+                            static_cast<uint32_t>(u1), static_cast<uint32_t>(static_cast<uint64_t>(u1) >> 32), rshift))));
+                        ob[i] = static_cast<int16_t>(clamp16(static_cast<int32_t>(__funnelshift_r(
+                            static_cast<uint32_t>(u2), static_cast<uint32_t>(static_cast<uint64_t>(u2) >> 32), rshift))));
+                    } else if (ep.fast) {
                         int32_t hi;
                         uint32_t lo;
                         shr31(t1 + rrnd, rshift, hi, lo);
@@ -397,12 +419,15 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
             load_planes<P, 8>(tacc + 64 + f0, vu);
             if (!row_ok) continue;
             int32_t gm[8];
-            if (lean && ep.bits_m == 32) {
-                gateup_lean<P, 8, 32>(vg, vu, colp + f0, colp + 64 + f0, static_cast<const int16_t*>(silu_tab), ep.silu_lo,
-                                      ep.silu_d, gs, grnd, gm);
+            const int16_t* tab16 = static_cast<const int16_t*>(silu_tab);
+            if (lean && ep.narrow && ep.bits_m == 32) {
+                gateup_lean<P, 8, 32, true>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
+            } else if (lean && ep.narrow && ep.bits_m == 16) {
+                gateup_lean<P, 8, 16, true>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
+            } else if (lean && ep.bits_m == 32) {
+                gateup_lean<P, 8, 32, false>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
             } else if (lean && ep.bits_m == 16) {
-                gateup_lean<P, 8, 16>(vg, vu, colp + f0, colp + 64 + f0, static_cast<const int16_t*>(silu_tab), ep.silu_lo,
-                                      ep.silu_d, gs, grnd, gm);
+                gateup_lean<P, 8, 16, false>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
