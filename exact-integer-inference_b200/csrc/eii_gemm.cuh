@@ -575,6 +575,13 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
     }
 }
 
+// Column parameters (m, shift, 2^(shift-1), m << 8) of output column c (zero multiplier past N).
+__device__ __forceinline__ int4 col_params(const EpiParams& ep, int c) {
+    const int2 ms = c < ep.N ? __ldg(ep.msh + c) : make_int2(0, 1);
+    const int rnd = (ms.y >= 1 && ms.y <= 31) ? (1 << (ms.y - 1)) : 0;
+    return make_int4(ms.x, ms.y, rnd, ms.x << 8);
+}
+
 // ---------------------------------------------------------------------------------------------
 template <int P, int KIND>
 __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
@@ -720,12 +727,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             // has passed the previous tile's barrier, so every warp is done with tile - 2.  The
             // barrier below also publishes the staged SiLU table before the first tile.
             int4* colp = colp_all + (acc_iter & 1) * C::BN;
-            if (et < C::BN) {
-                const int c = n_blk * C::BN + et;
-                const int2 ms = c < ep.N ? __ldg(ep.msh + c) : make_int2(0, 1);
-                const int rnd = (ms.y >= 1 && ms.y <= 31) ? (1 << (ms.y - 1)) : 0;
-                colp[et] = make_int4(ms.x, ms.y, rnd, ms.x << 8);
-            }
+            if (acc_iter == 0 && et < C::BN) colp[et] = col_params(ep, n_blk * C::BN + et);
             // RESID: the residual tile of this warp (32 rows x BN/4 int32) goes into its staging buffer by
             // TMA while the accumulators are being computed.
             bool xload = false;
@@ -745,6 +747,10 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             }
             if (!epi_barrier_and(ok)) break;
             tc_fence_after();
+            // parameters of this CTA's next tile go into the other buffer now (published by the next
+            // tile's barrier), so their global-load latency is hidden behind this tile's epilogue
+            if (et < C::BN && t + static_cast<int>(gridDim.x) < tiles)
+                colp_all[((acc_iter + 1) & 1) * C::BN + et] = col_params(ep, ((t + gridDim.x) % num_n) * C::BN + et);
             const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
             epilogue_tile<P, KIND>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e], xphase,
                                    abort);
