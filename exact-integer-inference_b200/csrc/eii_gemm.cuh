@@ -278,12 +278,7 @@ __device__ __forceinline__ void gateup_lean(const uint32_t (&vg)[P][N], const ui
         const int64_t prod = static_cast<int64_t>(sg) * u + grnd;
         int32_t hi;
         uint32_t lo;
-        if (gs == 0) {
-            hi = static_cast<int32_t>(static_cast<uint64_t>(prod) >> 32);
-            lo = static_cast<uint32_t>(prod);
-        } else {
-            shr31(prod, gs, hi, lo);
-        }
+        shr31(prod, gs, hi, lo);  // also right for gs == 0 (a funnel shift by 0 returns the low word)
         gm[i] = sat_hl(hi, lo, BITS_M);
     }
 }
@@ -306,7 +301,10 @@ struct EpiMaps {
 };
 
 
-template <int P, int KIND>
+// MODE selects the requantisation at compile time (0 generic int64, 1 fast 32-bit, 2 narrow), so
+// the per-element loops carry no run-time branch between the paths.  QKV has two copies only
+// (narrow, and fast-or-generic chosen at run time) to stay within its register budget.
+template <int P, int KIND, int MODE>
 __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc, int m_blk, int n_blk, int cg,
                                               int quad, int lane, const int4* colp, const void* silu_tab,
                                               uint8_t* stg, const EpiMaps& maps, uint64_t* xbar, uint32_t& xphase,
@@ -356,7 +354,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
             for (int i = 0; i < 8; ++i) {
                 const int4 ca = colp[64 * hl + d0 + i], cb = colp[64 * hl + 32 + d0 + i];
                 int32_t a, b;
-                if (ep.narrow) {
+                if constexpr (MODE == 2) {
                     a = clamp16(rs_narrow<P, 8>(va, i, ca));
                     b = clamp16(rs_narrow<P, 8>(vb, i, cb));
                 } else if (ep.fast) {
@@ -369,7 +367,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 if (region < 2) {
                     const int64_t t1 = static_cast<int64_t>(a) * rc[i] - static_cast<int64_t>(b) * rsn[i];
                     const int64_t t2 = static_cast<int64_t>(b) * rc[i] + static_cast<int64_t>(a) * rsn[i];
-                    if (ep.narrow) {
+                    if constexpr (MODE == 2) {
                         const int64_t u1 = t1 + rrnd, u2 = t2 + rrnd;
                         oa[i] = static_cast<int16_t>(clamp16(static_cast<int32_t>(__funnelshift_r(
                             static_cast<uint32_t>(u1), static_cast<uint32_t>(static_cast<uint64_t>(u1) >> 32), rshift))));
@@ -409,7 +407,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
         const int j0 = n_blk * 64 + 16 * cg;
         const int gs = ep.gated_shift;
         const int64_t grnd = gs >= 1 ? (int64_t(1) << (gs - 1)) : 0;
-        const bool lean = ep.fast && ep.silu_smem && !ep.silu_wide && ep.bits_s == 16 && ep.silu_d <= 15 &&
+        const bool lean = MODE >= 1 && ep.silu_smem && !ep.silu_wide && ep.bits_s == 16 && ep.silu_d <= 15 &&
                           ep.bits_g == 16 && ep.bits_u == 16;
 #pragma unroll 1
         for (int h8 = 0; h8 < 16; h8 += 8) {  // 8 features at a time keeps the pass free of spills
@@ -420,9 +418,9 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
             if (!row_ok) continue;
             int32_t gm[8];
             const int16_t* tab16 = static_cast<const int16_t*>(silu_tab);
-            if (lean && ep.narrow && ep.bits_m == 32) {
+            if (lean && MODE == 2 && ep.bits_m == 32) {
                 gateup_lean<P, 8, 32, true>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
-            } else if (lean && ep.narrow && ep.bits_m == 16) {
+            } else if (lean && MODE == 2 && ep.bits_m == 16) {
                 gateup_lean<P, 8, 16, true>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
             } else if (lean && ep.bits_m == 32) {
                 gateup_lean<P, 8, 32, false>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
@@ -432,15 +430,14 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int4 cgp = colp[f0 + i], cup = colp[64 + f0 + i];
-                    if (ep.fast) {
+                    if constexpr (MODE >= 1) {
                         const int32_t g = requant_fast<P, 8>(vg, i, cgp, ep.bits_g);
                         const int32_t u = requant_fast<P, 8>(vu, i, cup, ep.bits_u);
                         const int32_t sg = static_cast<int32_t>(silu_lookup(ep, silu_tab, g));
                         const int64_t prod = static_cast<int64_t>(sg) * u + grnd;
                         int32_t hi;
                         uint32_t lo;
-                        if (gs == 0) { hi = static_cast<int32_t>(static_cast<uint64_t>(prod) >> 32); lo = static_cast<uint32_t>(prod); }
-                        else shr31(prod, gs, hi, lo);
+                        shr31(prod, gs, hi, lo);
                         gm[i] = sat_hl(hi, lo, ep.bits_m);
                     } else {
                         const int64_t g = requant_gen<P, 8>(vg, i, cgp, ep.bits_g);
@@ -487,7 +484,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int4 cp = colp[tc + i];
-                    if (ep.fast) {
+                    if constexpr (MODE >= 1) {
                         int32_t hi;
                         uint32_t lo;
                         shr31(mulround<P, 16>(v, i, cp), cp.y, hi, lo);
@@ -540,7 +537,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int4 cp = colp[tc + i];
-                    if (ep.fast) {
+                    if constexpr (MODE >= 1) {
                         int32_t hi;
                         uint32_t lo;
                         shr31(mulround<P, 16>(v, i, cp), cp.y, hi, lo);
@@ -752,8 +749,15 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             if (et < C::BN && t + static_cast<int>(gridDim.x) < tiles)
                 colp_all[((acc_iter + 1) & 1) * C::BN + et] = col_params(ep, ((t + gridDim.x) % num_n) * C::BN + et);
             const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
-            epilogue_tile<P, KIND>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e], xphase,
-                                   abort);
+            if (KIND != EPI_LINEAR && ep.narrow && (KIND == EPI_QKV || KIND == EPI_GATEUP))
+                epilogue_tile<P, KIND, 2>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
+                                          xphase, abort);
+            else if (KIND != EPI_LINEAR && KIND != EPI_QKV && ep.fast)
+                epilogue_tile<P, KIND, 1>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
+                                          xphase, abort);
+            else
+                epilogue_tile<P, KIND, 0>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
+                                          xphase, abort);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
