@@ -167,6 +167,26 @@ int map_planes(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint
     return EII_OK;
 }
 
+// Row-blocked planes [planes][ceil(rows/128)][K/16][128 rows][16 bytes] (the gated activations): a
+// 4-D map whose box (8 K-chunks of 2 KB) lands in shared memory as 8 K-chunks of 128 rows x 16 bytes
+// (no swizzle), the K-major core-matrix layout the MMA reads with 2 KB / 128-byte strides.
+int map_blocked(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint64_t planes) {
+    EncodeTiledFn enc;
+    TRY(get_encode(&enc));
+    // each 2 KB run (128 rows x 16 bytes) is one TMA row of 256 eight-byte elements
+    const uint64_t mblk = (rows + 127) / 128;
+    cuuint64_t dims[4] = {256, K / 16, mblk, planes};
+    cuuint64_t strides[3] = {2048, 128 * K, 128 * K * mblk};
+    cuuint32_t box[4] = {256, 8, 1, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, const_cast<void*>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(EII_ERR_CUDA, "cuTensorMapEncodeTiled(blocked K=%llu rows=%llu P=%llu) failed: %d",
+                                       (unsigned long long)K, (unsigned long long)rows, (unsigned long long)planes, (int)r);
+    return EII_OK;
+}
+
 }  // namespace
 
 struct eii_engine {
@@ -292,7 +312,7 @@ int ensure_rows(eii_engine* e, int rows) {
     TRY(dalloc(W, &e->k, (size_t)rows * 192));
     TRY(dalloc(W, &e->v, (size_t)rows * 192));
     TRY(dalloc(W, &e->ctx_planes, (size_t)4 * rows * D_MODEL));
-    TRY(dalloc(W, &e->gated_planes, (size_t)4 * rows * D_FF));
+    TRY(dalloc(W, &e->gated_planes, (size_t)4 * ((rows + 127) / 128) * 128 * D_FF));  // row-blocked
     e->cap_rows = rows;
     return EII_OK;
 }
@@ -328,8 +348,8 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
         TRY(map_planes(&am.h, e->h_planes, D_MODEL, rows, 2));
         TRY(map_planes(&am.ctx2, e->ctx_planes, D_MODEL, rows, 2));
         TRY(map_planes(&am.ctx4, e->ctx_planes, D_MODEL, rows, 4));
-        TRY(map_planes(&am.gated2, e->gated_planes, D_FF, rows, 2));
-        TRY(map_planes(&am.gated4, e->gated_planes, D_FF, rows, 4));
+        TRY(map_blocked(&am.gated2, e->gated_planes, D_FF, rows, 2));
+        TRY(map_blocked(&am.gated4, e->gated_planes, D_FF, rows, 4));
         TRY(map_out(&am.x32, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 32, 32));
         TRY(map_out(&am.x16, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 16, 32));
         TRY(map_out(&am.q, e->q, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, D_MODEL, rows, D_MODEL * 2, 16, 32));
@@ -437,6 +457,7 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
 
     ep = EpiParams{};
     ep.M = rows; ep.N = D_MODEL; ep.K = D_FF; ep.msh = L.msh_d; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_d;
+    ep.a_blocked = 1;
     TRY(launch_gemm_p<EPI_RESID>(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, L.Pm == 2 ? L.tm_d : L.tm_d64, ep, st,
                                  EII_K_GEMM_DOWN, &am->x32, &am->x16));
     return EII_OK;

@@ -70,7 +70,12 @@ struct EpiParams {
     // needs no 64-bit saturation test; the RoPE shifts are >= 16 for the same reason.
     int narrow;
     int bits_g, bits_u, gated_shift, bits_m, gated_P;
-    uint8_t* gated_planes;  // [gated_P][M][N/2]
+    // gated planes in the row-blocked layout [gated_P][ceil(M/128)][N/32][128 rows][16 bytes]: each
+    // 16-feature group of a 128-row block is one 2 KB run, so an epilogue warp's 32 rows x 16 features
+    // of a plane are 512 contiguous bytes (coalesced stores).  The down GEMM reads it with a 4-D map.
+    uint8_t* gated_planes;
+    // A operand in that row-blocked layout (4-D map, no swizzle) instead of [P][M][K] with 128-byte swizzle
+    int a_blocked;
     // EPI_LOGITS: int32 out[row * ld + col] = RS(acc m, shift) (low 32 bits, no SAT)
     int32_t* logits;
     int64_t ld_logits;
@@ -243,25 +248,6 @@ __device__ __forceinline__ void pack_plane(const int32_t (&x)[N], uint32_t (&w)[
     }
 }
 
-template <int PL, int N>
-__device__ __forceinline__ void store_plane(uint8_t* dst, const int32_t (&x)[N]) {
-    uint32_t w[N / 4];
-    pack_plane<PL, N>(x, w);
-    if constexpr (N == 16) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-    else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
-}
-
-// The byte planes of N values (N = 8 or 16) to plane_stride-separated destinations.
-template <int N>
-__device__ __forceinline__ void store_planes(uint8_t* base, int64_t plane_stride, int nplanes, const int32_t (&x)[N]) {
-    store_plane<0, N>(base, x);
-    store_plane<1, N>(base + plane_stride, x);
-    if (nplanes == 4) {
-        store_plane<2, N>(base + 2 * plane_stride, x);
-        store_plane<3, N>(base + 3 * plane_stride, x);
-    }
-}
-
 // Gate/up/SiLU/gated product for 16 features, all-32-bit path: INT16 gate and up, compact INT16
 // SiLU table with shift d <= 15 (so g * 2^d < 2^31), gated shift in [0, 31].
 template <int P, int N, int BITS_M, bool NARROW>
@@ -403,8 +389,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
     } else if constexpr (KIND == EPI_GATEUP) {
         // cg -> gated features 16 cg .. 16 cg + 15 of the tile: gate cols 16 cg.., up cols 64 + 16 cg..
         if (n0 >= ep.N) return;
-        const int Nh = ep.N / 2;
-        const int j0 = n_blk * 64 + 16 * cg;
+        const int64_t plane_stride = static_cast<int64_t>((ep.M + 127) / 128) * 128 * (ep.N / 2);
+        uint8_t* gdst = ep.gated_planes + static_cast<int64_t>(m_blk) * 64 * ep.N + (n_blk * 4 + cg) * 2048 +
+                        (quad * 32 + lane) * 16;
+        uint32_t keep[4][2];  // packed planes of features 0..7, stored with 8..15 as one 16-byte word
         const int gs = ep.gated_shift;
         const int64_t grnd = gs >= 1 ? (int64_t(1) << (gs - 1)) : 0;
         const bool lean = MODE >= 1 && ep.silu_smem && !ep.silu_wide && ep.bits_s == 16 && ep.silu_d <= 15 &&
@@ -447,8 +435,26 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                     }
                 }
             }
-            store_planes<8>(ep.gated_planes + static_cast<int64_t>(row) * Nh + j0 + h8, static_cast<int64_t>(ep.M) * Nh,
-                            ep.gated_P, gm);
+            if (h8 == 0) {
+                pack_plane<0, 8>(gm, keep[0]);
+                pack_plane<1, 8>(gm, keep[1]);
+                if (ep.gated_P == 4) {
+                    pack_plane<2, 8>(gm, keep[2]);
+                    pack_plane<3, 8>(gm, keep[3]);
+                }
+            } else {
+                uint32_t w[2];
+                pack_plane<0, 8>(gm, w);
+                *reinterpret_cast<uint4*>(gdst) = make_uint4(keep[0][0], keep[0][1], w[0], w[1]);
+                pack_plane<1, 8>(gm, w);
+                *reinterpret_cast<uint4*>(gdst + plane_stride) = make_uint4(keep[1][0], keep[1][1], w[0], w[1]);
+                if (ep.gated_P == 4) {
+                    pack_plane<2, 8>(gm, w);
+                    *reinterpret_cast<uint4*>(gdst + 2 * plane_stride) = make_uint4(keep[2][0], keep[2][1], w[0], w[1]);
+                    pack_plane<3, 8>(gm, w);
+                    *reinterpret_cast<uint4*>(gdst + 3 * plane_stride) = make_uint4(keep[3][0], keep[3][1], w[0], w[1]);
+                }
+            }
         }
     } else if constexpr (KIND == EPI_RESID) {
         // x = SAT32(x + RS(acc m, shift)) on this warp's 32 rows x NCOL columns.  The residual tile is
@@ -635,8 +641,15 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
                     uint8_t* sA = smem + stage * C::STAGE_BYTES;
                     uint8_t* sB = sA + P * C::A_BYTES;
                     mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    if (ep.a_blocked) {
 #pragma unroll
-                    for (int p = 0; p < P; ++p) tma_load_3d(sA + p * C::A_BYTES, &tmA, &full[stage], kb * 128, m_blk * 128, p);
+                        for (int p = 0; p < P; ++p)
+                            tma_load_4d(sA + p * C::A_BYTES, &tmA, &full[stage], 0, kb * 8, m_blk, p);
+                    } else {
+#pragma unroll
+                        for (int p = 0; p < P; ++p)
+                            tma_load_3d(sA + p * C::A_BYTES, &tmA, &full[stage], kb * 128, m_blk * 128, p);
+                    }
                     tma_load_2d(sB, &tmB, &full[stage], kb * 128, n_blk * C::BN);
                     ++fills;
                     if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
@@ -680,7 +693,9 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
                         const uint64_t bdesc = smem_desc_sw128(sB + ks * 32);
 #pragma unroll
                         for (int p = 0; p < P; ++p) {
-                            const uint64_t adesc = smem_desc_sw128(sA + p * C::A_BYTES + ks * 32);
+                            // row-blocked A: 16-byte K chunks 2 KB apart, 8-row groups 128 bytes apart
+                            const uint64_t adesc = ep.a_blocked ? smem_desc_noswz(sA + p * C::A_BYTES + ks * 4096, 2048, 128)
+                                                                : smem_desc_sw128(sA + p * C::A_BYTES + ks * 32);
                             mma_i8(dbase + p * C::BN, adesc, bdesc, p == P - 1 ? id_hi : id_lo,
                                    (kb > 0 || ks > 0) ? 1u : 0u);
                         }
