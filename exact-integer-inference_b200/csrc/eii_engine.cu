@@ -396,10 +396,10 @@ int launch_gemm_p(eii_engine* e, int P, const CUtensorMap& A, const CUtensorMap&
 
 int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, int shift, int bits,
                 uint8_t* planes, int P, int64_t* out64, cudaStream_t st) {
-    const int rows_per_block = 8;
+    const int rows_per_block = 16;  // 8 warps, two rows each
     ProfScope ps(e, EII_K_NORM, st);
-    k_rmsnorm<<<(rows + rows_per_block - 1) / rows_per_block, 32 * rows_per_block, 0, st>>>(x, rows, gain, shift, bits,
-                                                                                           planes, P, out64);
+    k_rmsnorm<<<(rows + rows_per_block - 1) / rows_per_block, 256, 0, st>>>(x, rows, gain, shift, bits, planes, P,
+                                                                           out64);
     CK(cudaGetLastError());
     return EII_OK;
 }

@@ -80,27 +80,40 @@ __device__ __forceinline__ int64_t warp_sum64(int64_t v) {
 
 // out = SAT(RS(3 RS(x U, 16) g, 21 + fw - f_out), bits_out) (python/intref.py:178-181), written
 // as P = bits_out / 8 byte planes [P][M][576] (planes != nullptr) and/or int64 [M,576].
-// One warp per row; lane l owns columns 64 i + 2 l, 64 i + 2 l + 1, i < 9.
+// Two rows per warp: half-warp h owns row 2 w + h, lane l of it columns 64 i + 4 l .. + 3, i < 9
+// (16-byte loads; 4-byte plane stores, 64 contiguous bytes per half-warp).
+__device__ __forceinline__ int64_t half_sum64(int64_t v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
 __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain, int shift_out,
                           int bits_out, uint8_t* __restrict__ planes, int P, int64_t* __restrict__ out64) {
-    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x % 32;
-    if (row >= M) return;
-    const int2* xr = reinterpret_cast<const int2*>(x + static_cast<int64_t>(row) * D_MODEL);
-    int2 v[9];
+    const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
+    const int l = threadIdx.x & 15;
+    const bool live = row < M;
+    const int4* xr = reinterpret_cast<const int4*>(x + static_cast<int64_t>(live ? row : 0) * D_MODEL);
+    int4 v[9];
     int64_t A = 0, B = 0, C = 0;
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
-        v[i] = xr[32 * i + lane];
-        const int64_t h0 = v[i].x >> 16, l0 = v[i].x & 0xFFFF, h1 = v[i].y >> 16, l1 = v[i].y & 0xFFFF;
-        A += h0 * h0 + h1 * h1;
-        B += h0 * l0 + h1 * l1;
-        C += l0 * l0 + l1 * l1;
+        v[i] = live ? xr[16 * i + l] : make_int4(0, 0, 0, 0);
+        const int32_t e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t h = e[u] >> 16, lo = e[u] & 0xFFFF;
+            A += h * h;
+            B += h * lo;
+            C += lo * lo;
+        }
     }
-    A = warp_sum64(A);
-    B = warp_sum64(B);
-    C = warp_sum64(C);
-    const int64_t U = norm_recip_root(A, B, C);
+    A = half_sum64(A);
+    B = half_sum64(B);
+    C = half_sum64(C);
+    if (!live) return;  // both halves of the warp are done with the shuffles
+    const int64_t U = norm_recip_root(A, B, C);  // < 2^31
+    const int32_t U32 = static_cast<int32_t>(U);
     // Fast path (planes output, bits_out 16, 1 <= shift_out <= 31): z = RS(x U, 16) fits int32
     // (|x U| <= 2^40, python/intref.py:178), 3 g fits int32, and RS(z 3 g, shift_out) is a funnel
     // shift of one 32x32 -> 64 multiply-add.
@@ -108,42 +121,48 @@ __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* _
     const int64_t rnd_out = (shift_out >= 1 && shift_out <= 62) ? (int64_t(1) << (shift_out - 1)) : 0;
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
-        const int c = 64 * i + 2 * lane;
-        const int2 g = __ldg(reinterpret_cast<const int2*>(gain) + 32 * i + lane);
+        const int c = 64 * i + 4 * l;
+        const int4 g4 = __ldg(reinterpret_cast<const int4*>(gain) + 16 * i + l);
+        const int32_t e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        const int32_t g[4] = {g4.x, g4.y, g4.z, g4.w};
         if (fast) {
-            int32_t o[2];
+            int32_t o[4];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int64_t xu = static_cast<int64_t>(u ? v[i].y : v[i].x) * U + 32768;
+            for (int u = 0; u < 4; ++u) {
+                const int64_t xu = static_cast<int64_t>(e[u]) * U32 + 32768;
                 const int32_t z = static_cast<int32_t>(__funnelshift_r(static_cast<uint32_t>(xu),
                                                                        static_cast<uint32_t>(static_cast<uint64_t>(xu) >> 32), 16));
-                const int64_t t = static_cast<int64_t>(z) * (3 * (u ? g.y : g.x)) + rnd_out;
+                const int64_t t = static_cast<int64_t>(z) * (3 * g[u]) + rnd_out;
                 const uint32_t tl = static_cast<uint32_t>(t), th = static_cast<uint32_t>(static_cast<uint64_t>(t) >> 32);
                 const uint32_t lo = __funnelshift_r(tl, th, shift_out);
                 const int32_t hi = static_cast<int32_t>(th) >> shift_out;
-                int32_t w = hi == (static_cast<int32_t>(lo) >> 31) ? static_cast<int32_t>(lo) : (hi < 0 ? INT32_MIN : INT32_MAX);
+                const int32_t w = hi == (static_cast<int32_t>(lo) >> 31) ? static_cast<int32_t>(lo) : (hi < 0 ? INT32_MIN : INT32_MAX);
                 o[u] = min(max(w, -32768), 32767);
             }
-            const uint32_t both = (static_cast<uint32_t>(o[0]) & 0xFFFFu) | (static_cast<uint32_t>(o[1]) << 16);
-            // bytes: [o0 lo, o0 hi, o1 lo, o1 hi] -> plane 0 gets (o0 lo, o1 lo), plane 1 (o0 hi, o1 hi)
-            *reinterpret_cast<uint16_t*>(planes + static_cast<int64_t>(row) * D_MODEL + c) =
-                static_cast<uint16_t>(__byte_perm(both, 0, 0x0020));
-            *reinterpret_cast<uint16_t*>(planes + (static_cast<int64_t>(M) + row) * D_MODEL + c) =
-                static_cast<uint16_t>(__byte_perm(both, 0, 0x0031));
+            const uint32_t w01 = (static_cast<uint32_t>(o[0]) & 0xFFFFu) | (static_cast<uint32_t>(o[1]) << 16);
+            const uint32_t w23 = (static_cast<uint32_t>(o[2]) & 0xFFFFu) | (static_cast<uint32_t>(o[3]) << 16);
+            // plane 0 gets the low bytes (o0, o1, o2, o3), plane 1 the high bytes
+            *reinterpret_cast<uint32_t*>(planes + static_cast<int64_t>(row) * D_MODEL + c) = __byte_perm(w01, w23, 0x6420);
+            *reinterpret_cast<uint32_t*>(planes + (static_cast<int64_t>(M) + row) * D_MODEL + c) = __byte_perm(w01, w23, 0x7531);
             continue;
         }
-        const int64_t z0 = rs64(static_cast<int64_t>(v[i].x) * U, 16), z1 = rs64(static_cast<int64_t>(v[i].y) * U, 16);
-        const int64_t o0 = sat64(rs64(z0 * g.x * 3, shift_out), bits_out);
-        const int64_t o1 = sat64(rs64(z1 * g.y * 3, shift_out), bits_out);
+        int64_t o[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t z = rs64(static_cast<int64_t>(e[u]) * U, 16);
+            o[u] = sat64(rs64(z * g[u] * 3, shift_out), bits_out);
+        }
         if (planes) {
             for (int p = 0; p < P; ++p) {
-                const uint16_t pair = static_cast<uint16_t>(plane_byte(o0, p)) | (static_cast<uint16_t>(plane_byte(o1, p)) << 8);
-                *reinterpret_cast<uint16_t*>(planes + (static_cast<int64_t>(p) * M + row) * D_MODEL + c) = pair;
+                const uint32_t quad = static_cast<uint32_t>(plane_byte(o[0], p)) | (static_cast<uint32_t>(plane_byte(o[1], p)) << 8) |
+                                      (static_cast<uint32_t>(plane_byte(o[2], p)) << 16) |
+                                      (static_cast<uint32_t>(plane_byte(o[3], p)) << 24);
+                *reinterpret_cast<uint32_t*>(planes + (static_cast<int64_t>(p) * M + row) * D_MODEL + c) = quad;
             }
         }
         if (out64) {
-            out64[static_cast<int64_t>(row) * D_MODEL + c] = o0;
-            out64[static_cast<int64_t>(row) * D_MODEL + c + 1] = o1;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) out64[static_cast<int64_t>(row) * D_MODEL + c + u] = o[u];
         }
     }
 }
