@@ -217,7 +217,7 @@ def roofline(prof, rows_per_launch, peaks):
     macs = {"gemm_gateup_silu": r * 3072 * 576, "gemm_qkv_rope": r * 960 * 576, "gemm_o_resid": r * 576 * 576,
             "gemm_down_resid": r * 576 * 1536, "gemm_logits": r * VOCAB * 576,
             "attention": (r // T) * 9 * 64 * 2 * (T * (T + 1) // 2)}
-    bytes_ = {"rmsnorm": r * D * 4 + r * D * 2, "embed": r * D * 5, "digest": r * VOCAB * 4}
+    bytes_ = {"rmsnorm": r * D * 4 + r * D * 2, "embed": r * D * 5}
     int8_peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
     if name in macs:
         achieved = 2.0 * macs[name] / per_launch_s / 1e12

@@ -177,17 +177,25 @@ class Engine:
         return out, acc
 
 
-def digest_logits(logits):
-    """Host restatement of the device digest (include/eii.h, eii_forward `digests`)."""
-    lg = np.asarray(logits)
-    n, T, V = lg.shape
-    idx = (np.arange(T, dtype=np.uint64)[:, None] * np.uint64(V) + np.arange(V, dtype=np.uint64)[None, :])
+def _mix64(z):
+    M = np.uint64(0xFFFFFFFFFFFFFFFF)
     with np.errstate(over="ignore"):
-        z = idx + np.uint64(0x9E3779B97F4A7C15)
+        z = (z + np.uint64(0x9E3779B97F4A7C15)) & M
         z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
         z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
-        z = (z ^ (z >> np.uint64(31))) | np.uint64(1)
-        out = np.empty(n, np.uint64)
+        return (z ^ (z >> np.uint64(31))) | np.uint64(1)
+
+
+def digest_logits(logits):
+    """Host restatement of the device digest (include/eii.h, eii_forward `digests`):
+    sum over (t, v) of uint32(logit) * mix64(t) * mix64(2^32 + v), mod 2^64, per sequence."""
+    lg = np.asarray(logits)
+    n, T, V = lg.shape
+    wa = _mix64(np.arange(T, dtype=np.uint64))
+    wb = _mix64(np.arange(V, dtype=np.uint64) + np.uint64(1 << 32))
+    out = np.empty(n, np.uint64)
+    with np.errstate(over="ignore"):
         for s in range(n):
-            out[s] = (lg[s].astype(np.uint32).astype(np.uint64) * z).sum(dtype=np.uint64)
+            rows = (lg[s].astype(np.uint32).astype(np.uint64) * wb[None, :]).sum(axis=1, dtype=np.uint64)
+            out[s] = (rows * wa).sum(dtype=np.uint64)
     return out

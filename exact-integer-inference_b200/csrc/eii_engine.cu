@@ -200,6 +200,7 @@ struct eii_engine {
     int32_t* final_q = nullptr;
     int final_f = 0, f_y = 0, final_shift = 0;
     int fast_logits = 0;
+    uint64_t *dig_a = nullptr, *dig_b = nullptr;  // logits digest weights (positions, vocabulary)
     int32_t *exp_tab = nullptr, *rope_c = nullptr, *rope_s = nullptr;
     LayerDev L[N_LAYERS];
     // chunk workspace
@@ -463,13 +464,16 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     return EII_OK;
 }
 
-int run_logits(eii_engine* e, int rows, int32_t* logits, int64_t ld, cudaStream_t st) {
+// Final norm and logits of `rows` rows (whole sequences of T tokens); with digests != nullptr the
+// per-sequence digests of these rows are accumulated into digests[0 .. rows / T) (zeroed by the caller).
+int run_logits(eii_engine* e, int rows, int T, int32_t* logits, int64_t ld, uint64_t* digests, cudaStream_t st) {
     const ActMaps* am;
     TRY(act_maps(e, rows, &am));
     TRY(launch_norm(e, e->x, rows, e->final_q, e->final_shift, 16, e->h_planes, 2, nullptr, st));
     EpiParams ep{};
     ep.M = rows; ep.N = VOCAB; ep.K = D_MODEL; ep.msh = e->msh_logits; ep.err = e->err_dev;
     ep.logits = logits; ep.ld_logits = ld; ep.fast = e->fast_logits;
+    ep.T = T; ep.dig = reinterpret_cast<unsigned long long*>(digests); ep.dig_a = e->dig_a; ep.dig_b = e->dig_b;
     CUtensorMap lm;
     TRY(map_out(&lm, logits, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, VOCAB, rows, (uint64_t)ld * 4, 32, 32));
     return launch_gemm<2, EPI_LOGITS>(e, am->h, e->tm_emb, ep, st, EII_K_GEMM_LOGITS, &lm);
@@ -640,6 +644,13 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
     TRY(upload(e, &e->rope_c, tmp.data(), ROPE_POS * 32));
     TRY(narrow32(rsn, ROPE_POS * 32, tmp, "rope_sin"));
     TRY(upload(e, &e->rope_s, tmp.data(), ROPE_POS * 32));
+    {   // logits digest weights: position t -> mix64(t), vocabulary id v -> mix64(2^32 + v)
+        std::vector<uint64_t> wa(ROPE_POS), wb(VOCAB);
+        for (int t = 0; t < ROPE_POS; ++t) wa[t] = mix64(static_cast<uint64_t>(t));
+        for (int v = 0; v < VOCAB; ++v) wb[v] = mix64((uint64_t(1) << 32) + static_cast<uint64_t>(v));
+        TRY(upload(e, &e->dig_a, wa.data(), ROPE_POS));
+        TRY(upload(e, &e->dig_b, wb.data(), VOCAB));
+    }
     {
         std::vector<int2> msh(VOCAB);
         for (int i = 0; i < VOCAB; ++i) msh[i] = make_int2((int)emb_m[i], (int)(emb_n[i] + e->f_y - 16));
@@ -911,12 +922,7 @@ int eii_forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, 
         if (logits_dev || digests_dev) {
             int32_t* lg = logits_dev ? logits_dev + (int64_t)s0 * T * ld : e->logits_ws;
             const int64_t lld = logits_dev ? ld : VOCAB;
-            TRY(run_logits(e, rows, lg, lld, st));
-            if (digests_dev) {
-                ProfScope ps(e, EII_K_DIGEST, st);
-                k_digest<<<rows, 256, 0, st>>>(lg, lld, T, rows, reinterpret_cast<unsigned long long*>(digests_dev + s0));
-                CK(cudaGetLastError());
-            }
+            TRY(run_logits(e, rows, T, lg, lld, digests_dev ? digests_dev + s0 : nullptr, st));
         }
     }
     return check_device_error(e, st);
@@ -960,19 +966,16 @@ int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* em
             }
         }
         if (rc == EII_OK && (logits_out || digests)) {
-            rc = run_logits(e, rows, e->logits_ws, VOCAB, st);
+            if (digests && cudaMemsetAsync(dig_dev, 0, sizeof(uint64_t) * ns, st) != cudaSuccess)
+                rc = fail(EII_ERR_CUDA, "digest reset failed");
+            if (rc == EII_OK) rc = run_logits(e, rows, T, e->logits_ws, VOCAB, digests ? dig_dev : nullptr, st);
             if (rc == EII_OK && logits_out &&
                 cudaMemcpyAsync(logits_out + (int64_t)s0 * T * VOCAB, e->logits_ws, sizeof(int32_t) * (size_t)rows * VOCAB,
                                 cudaMemcpyDeviceToHost, st) != cudaSuccess)
                 rc = fail(EII_ERR_CUDA, "logits download failed");
-            if (rc == EII_OK && digests) {
-                cudaMemsetAsync(dig_dev, 0, sizeof(uint64_t) * ns, st);
-                ProfScope ps(e, EII_K_DIGEST, st);
-                k_digest<<<rows, 256, 0, st>>>(e->logits_ws, VOCAB, T, rows, reinterpret_cast<unsigned long long*>(dig_dev));
-                if (cudaGetLastError() != cudaSuccess ||
-                    cudaMemcpyAsync(digests + s0, dig_dev, sizeof(uint64_t) * ns, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-                    rc = fail(EII_ERR_CUDA, "digest failed");
-            }
+            if (rc == EII_OK && digests &&
+                cudaMemcpyAsync(digests + s0, dig_dev, sizeof(uint64_t) * ns, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                rc = fail(EII_ERR_CUDA, "digest download failed");
         }
         if (rc == EII_OK) rc = check_device_error(e, st);
     }

@@ -79,6 +79,12 @@ struct EpiParams {
     // EPI_LOGITS: int32 out[row * ld + col] = RS(acc m, shift) (low 32 bits, no SAT)
     int32_t* logits;
     int64_t ld_logits;
+    // EPI_LOGITS, optional per-sequence digest of the logits (sequence = row / T, position t = row % T):
+    //   dig[seq] += sum over (t, v) of uint32(logit) * dig_b[v] * dig_a[t]  (mod 2^64)
+    // accumulated per row in registers over a CTA's contiguous run of tiles, one atomic per row and run.
+    unsigned long long* dig;
+    const uint64_t* dig_a;
+    const uint64_t* dig_b;
     // EPI_LINEAR: int64 out = SAT(RS(acc m, shift), bits_out), optional int64 acc
     int64_t* out64;
     int64_t* acc64;
@@ -114,10 +120,11 @@ struct GemmCfg {
     static constexpr int THREADS = 64 + EPI_THREADS;
     static constexpr int BAR_BYTES = 512;
     static constexpr int COLP_BYTES = 2 * BN * 16;  // per-tile column (m, shift, 2^(shift-1), m << 8), x2
+    static constexpr int DIGW_BYTES = KIND == EPI_LOGITS ? 2 * BN * 8 : 0;  // per-tile digest column weights, x2
     static constexpr int SILU_BYTES = KIND == EPI_GATEUP ? SILU_SMEM_BYTES : 0;
     static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;  // 1024-aligned
     static constexpr int BAR_OFFSET = STG_OFFSET + EPI_WARPS * STG_BYTES;
-    static constexpr int SMEM = BAR_OFFSET + 1024 + BAR_BYTES + COLP_BYTES + SILU_BYTES;
+    static constexpr int SMEM = BAR_OFFSET + 1024 + BAR_BYTES + COLP_BYTES + DIGW_BYTES + SILU_BYTES;
     static_assert(NB >= 1, "accumulators must fit in TMEM");
     static_assert(STG_BYTES % 1024 == 0, "staging buffers are 1024-byte aligned");
     static_assert(SMEM <= SMEM_LIMIT, "shared memory budget");
@@ -294,7 +301,7 @@ template <int P, int KIND, int MODE>
 __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc, int m_blk, int n_blk, int cg,
                                               int quad, int lane, const int4* colp, const void* silu_tab,
                                               uint8_t* stg, const EpiMaps& maps, uint64_t* xbar, uint32_t& xphase,
-                                              volatile int* abort) {
+                                              volatile int* abort, const uint64_t* digw, uint64_t& dsum) {
     constexpr int BN = (P == 4) ? BN_P4 : 128;
     const int row = m_blk * 128 + quad * 32 + lane;
     const bool row_ok = row < ep.M;
@@ -555,6 +562,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
                     *reinterpret_cast<int4*>(stg + stg_off<128>(lane, 4 * ch + q)) = *reinterpret_cast<int4*>(&o[4 * q]);
+                if (ep.dig) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) dsum += static_cast<uint64_t>(static_cast<uint32_t>(o[i])) * digw[tc + i];
+                }
             } else {  // EPI_LINEAR (generic path only)
                 int64_t* op = ep.out64 + static_cast<int64_t>(row) * ep.N + gc;
 #pragma unroll
@@ -585,6 +596,9 @@ __device__ __forceinline__ int4 col_params(const EpiParams& ep, int c) {
     return make_int4(ms.x, ms.y, rnd, ms.x << 8);
 }
 
+// Digest weight of output column c (0 past N).
+__device__ __forceinline__ uint64_t dig_weight(const EpiParams& ep, int c) { return c < ep.N ? __ldg(ep.dig_b + c) : 0; }
+
 // ---------------------------------------------------------------------------------------------
 template <int P, int KIND>
 __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
@@ -605,12 +619,21 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + C::EPI_WARPS);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     int4* colp_all = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
-    void* silu_tab = reinterpret_cast<uint8_t*>(colp_all) + C::COLP_BYTES;
+    uint64_t* digw_all = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(colp_all) + C::COLP_BYTES);
+    void* silu_tab = reinterpret_cast<uint8_t*>(colp_all) + C::COLP_BYTES + C::DIGW_BYTES;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int num_m = (ep.M + 127) / 128, num_n = (ep.N + C::BN - 1) / C::BN;
     const int tiles = num_m * num_n;
     const int KB = (ep.K + 127) / 128;
+    // Tile schedule shared by the three roles: LOGITS walks a contiguous run of tiles (rows stay on
+    // one CTA for many N tiles, so the digest sums stay in registers); the others stride by the grid.
+    int t_first = blockIdx.x, t_end = tiles, t_step = gridDim.x;
+    if constexpr (KIND == EPI_LOGITS) {
+        t_first = static_cast<int>(static_cast<int64_t>(blockIdx.x) * tiles / gridDim.x);
+        t_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * tiles / gridDim.x);
+        t_step = 1;
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -634,7 +657,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             uint32_t phase = 0;
             uint32_t fills = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            for (int t = t_first; t < t_end && ok; t += t_step) {
                 const int m_blk = t / num_n, n_blk = t % num_n;
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort, ep.err, ERR_TIMEOUT_PRODUCER)) { ok = false; break; }
@@ -673,7 +696,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             int acc_iter = 0;
             bool ok = true;
             bool issued = false;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++acc_iter) {
+            for (int t = t_first; t < t_end && ok; t += t_step, ++acc_iter) {
                 const int n_blk = t % num_n;
                 const int buf = acc_iter % C::NB;
                 const uint32_t acc_phase = (acc_iter / C::NB) & 1;
@@ -731,15 +754,30 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             }
         }
         int acc_iter = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++acc_iter) {
+        int dig_m = -1;     // LOGITS digest: row block whose sums this lane holds
+        uint64_t dsum = 0;  //   sum over the columns seen so far of uint32(logit) * dig_b[col]
+        auto dig_flush = [&]() {
+            const int r = dig_m * 128 + quad * 32 + lane;
+            if (dig_m >= 0 && r < ep.M)
+                atomicAdd(ep.dig + r / ep.T, static_cast<unsigned long long>(dsum * __ldg(ep.dig_a + r % ep.T)));
+            dsum = 0;
+        };
+        for (int t = t_first; t < t_end; t += t_step, ++acc_iter) {
             const int m_blk = t / num_n, n_blk = t % num_n;
+            if (KIND == EPI_LOGITS && ep.dig && m_blk != dig_m) {
+                dig_flush();
+                dig_m = m_blk;
+            }
             const int buf = acc_iter % C::NB;
             const uint32_t acc_phase = (acc_iter / C::NB) & 1;
             // Per-tile column parameters, double buffered: a warp that writes buffer b for this tile
             // has passed the previous tile's barrier, so every warp is done with tile - 2.  The
             // barrier below also publishes the staged SiLU table before the first tile.
             int4* colp = colp_all + (acc_iter & 1) * C::BN;
-            if (acc_iter == 0 && et < C::BN) colp[et] = col_params(ep, n_blk * C::BN + et);
+            if (acc_iter == 0 && et < C::BN) {
+                colp[et] = col_params(ep, n_blk * C::BN + et);
+                if (KIND == EPI_LOGITS && ep.dig) digw_all[et] = dig_weight(ep, n_blk * C::BN + et);
+            }
             // RESID: the residual tile of this warp (32 rows x BN/4 int32) goes into its staging buffer by
             // TMA while the accumulators are being computed.
             bool xload = false;
@@ -761,22 +799,27 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             tc_fence_after();
             // parameters of this CTA's next tile go into the other buffer now (published by the next
             // tile's barrier), so their global-load latency is hidden behind this tile's epilogue
-            if (et < C::BN && t + static_cast<int>(gridDim.x) < tiles)
-                colp_all[((acc_iter + 1) & 1) * C::BN + et] = col_params(ep, ((t + gridDim.x) % num_n) * C::BN + et);
+            if (et < C::BN && t + t_step < t_end) {
+                const int nc = ((t + t_step) % num_n) * C::BN + et;
+                colp_all[((acc_iter + 1) & 1) * C::BN + et] = col_params(ep, nc);
+                if (KIND == EPI_LOGITS && ep.dig) digw_all[((acc_iter + 1) & 1) * C::BN + et] = dig_weight(ep, nc);
+            }
+            const uint64_t* digw = digw_all + (acc_iter & 1) * C::BN;
             const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
             if (KIND != EPI_LINEAR && ep.narrow && (KIND == EPI_QKV || KIND == EPI_GATEUP))
                 epilogue_tile<P, KIND, 2>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                          xphase, abort);
+                                          xphase, abort, digw, dsum);
             else if (KIND != EPI_LINEAR && KIND != EPI_QKV && ep.fast)
                 epilogue_tile<P, KIND, 1>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                          xphase, abort);
+                                          xphase, abort, digw, dsum);
             else
                 epilogue_tile<P, KIND, 0>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                          xphase, abort);
+                                          xphase, abort, digw, dsum);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
+        if (KIND == EPI_LOGITS && ep.dig) dig_flush();
         if (lane == 0) bulk_wait0();  // this warp's tile stores are complete before the CTA exits
     }
     tc_fence_before();

@@ -294,35 +294,13 @@ __global__ void k_i64_to_i32(const int64_t* __restrict__ a, int64_t n, int32_t* 
 }
 
 // --------------------------------------------------------------------------- digest
-// Per-sequence 64-bit digest of int32 logits [n_seq*T, V] (row stride ld):
-//   digest = sum over (t, v) of uint32(logit) * mix(t * V + v)  (mod 2^64),
-// mix = the splitmix64 finaliser, forced odd.  Order-independent, so blocks combine it with
-// 64-bit atomic adds; digests must be zeroed before the launch.
-__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+// splitmix64 finaliser forced odd: the logits digest weights (position t -> mix64(t), vocabulary
+// id v -> mix64(2^32 + v)); the digest itself is accumulated in the logits GEMM epilogue.
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z += 0x9E3779B97F4A7C15ull;
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
     z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
     return (z ^ (z >> 31)) | 1ull;
-}
-
-__global__ void k_digest(const int32_t* __restrict__ logits, int64_t ld, int T, int n_rows,
-                         unsigned long long* __restrict__ digests) {
-    const int row = blockIdx.x;
-    if (row >= n_rows) return;
-    const int t = row % T;
-    const int4* src = reinterpret_cast<const int4*>(logits + row * ld);
-    uint64_t h = 0;
-    for (int c4 = threadIdx.x; c4 < VOCAB / 4; c4 += blockDim.x) {
-        const int4 v = __ldg(src + c4);
-        const uint64_t base = static_cast<uint64_t>(t) * VOCAB + 4ull * c4;
-        h += static_cast<uint64_t>(static_cast<uint32_t>(v.x)) * mix64(base);
-        h += static_cast<uint64_t>(static_cast<uint32_t>(v.y)) * mix64(base + 1);
-        h += static_cast<uint64_t>(static_cast<uint32_t>(v.z)) * mix64(base + 2);
-        h += static_cast<uint64_t>(static_cast<uint32_t>(v.w)) * mix64(base + 3);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) h += __shfl_xor_sync(0xffffffffu, h, o);
-    if ((threadIdx.x & 31) == 0) atomicAdd(digests + row / T, static_cast<unsigned long long>(h));
 }
 
 }  // namespace eii

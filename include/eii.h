@@ -54,8 +54,10 @@ void eii_close(eii_engine* e);
  *   resid_out  nullable, [n_seq][30][T][576] int32 residual after each block (exp_resid_out.i32)
  *   logits_out nullable, [n_seq][T][49152] int32 logits, f = 16 (exp_logits.i32)
  *   digests    nullable, [n_seq] uint64 order-independent digest of each sequence's logits:
- *              sum over (t, v) of uint32(logit[t][v]) * mix64(t * 49152 + v) mod 2^64, mix64 the
- *              splitmix64 finaliser with the low bit forced to 1. */
+ *              sum over (t, v) of uint32(logit[t][v]) * mix64(t) * mix64(2^32 + v) mod 2^64, mix64
+ *              the splitmix64 finaliser with the low bit forced to 1 (so every weight is odd and
+ *              any single changed logit changes the digest).  It is accumulated inside the logits
+ *              GEMM epilogue; the logits are not read back to compute it. */
 int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* embed_out,
                 int32_t* resid_out, int32_t* logits_out, uint64_t* digests);
 
@@ -130,7 +132,7 @@ int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_in, const in
 #define EII_K_GEMM_GATEUP 5
 #define EII_K_GEMM_DOWN 6
 #define EII_K_GEMM_LOGITS 7
-#define EII_K_DIGEST 8
+#define EII_K_DIGEST 8 /* no launches: the digest is fused into the logits GEMM */
 #define EII_K_GEMM_LINEAR 9
 #define EII_NUM_KERNEL_KINDS 10
 const char* eii_kernel_name(int kind);

@@ -105,11 +105,15 @@ def test_host_digest_matches_definition():
     cols = np.arange(0, 49152, 4099)
     for s in range(2):
         # the definition evaluated with Python ints on a strided sample of columns
-        want = sum(int(np.uint32(lg[s, t, v])) * mix(t * 49152 + int(v)) for t in range(3) for v in cols) % (1 << 64)
+        want = sum(int(np.uint32(lg[s, t, v])) * mix(t) * mix((1 << 32) + int(v)) for t in range(3) for v in cols) % (1 << 64)
         sub = np.zeros_like(lg[s:s + 1])
         sub[0][:, cols] = lg[s][:, cols]
         assert int(_eii.digest_logits(sub)[0]) == want
     assert got.dtype == np.uint64
+    # one changed logit changes the digest
+    lg2 = lg.copy()
+    lg2[1, 2, 777] += 1
+    assert _eii.digest_logits(lg2)[1] != got[1] and _eii.digest_logits(lg2)[0] == got[0]
 
 
 def test_package_model_writer_matches_reference_export(tmp_path):
