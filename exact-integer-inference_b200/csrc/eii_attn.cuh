@@ -84,6 +84,9 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
 
     if (warp == 0) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
     if (tid == 0) { mbar_init(bar, 1); *abort = 0; fence_mbar_init(); }
+    for (int u = tid; u <= DMAX; u += ATTN_TC_THREADS) E[u] = ap.exp_tab[u];  // model table
+    griddep_wait();  // q, k, v are the previous kernel's output
+    griddep_launch();
 
     // ---- stage K, Q (3 heads) and V^T as byte planes; rows/keys >= T are zero
     for (int idx = tid; idx < 128 * 4 * 4; idx += ATTN_TC_THREADS) {
@@ -125,7 +128,6 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
             VT[8192 + sw128(dq * 16 + d, j)] = static_cast<uint8_t>((v[d] >> 8) & 0xFF);
         }
     }
-    for (int u = tid; u <= DMAX; u += ATTN_TC_THREADS) E[u] = ap.exp_tab[u];
     fence_async_smem();
     tc_fence_before();
     __syncthreads();

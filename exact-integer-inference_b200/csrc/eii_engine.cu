@@ -362,6 +362,32 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
     return EII_OK;
 }
 
+// Every hot-path kernel is launched with programmatic stream serialization: it may be scheduled
+// while the previous kernel in the stream drains (each kernel does its weight-only setup, then
+// griddep_wait() before touching earlier kernels' outputs).  EII_PDL=0 launches them plainly.
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("EII_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 template <int P, int KIND>
 int launch_gemm_raw(int device, int num_sms, const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& C0,
                     const CUtensorMap& C1, const CUtensorMap& C2, const EpiParams& ep, cudaStream_t st) {
@@ -374,8 +400,7 @@ int launch_gemm_raw(int device, int num_sms, const CUtensorMap& A, const CUtenso
     }
     const int tiles = ((ep.M + 127) / 128) * ((ep.N + C::BN - 1) / C::BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    k_plane_gemm<P, KIND><<<grid, C::THREADS, C::SMEM, st>>>(A, B, C0, C1, C2, ep);
-    CK(cudaGetLastError());
+    CK(launch_k(k_plane_gemm<P, KIND>, dim3(grid), dim3(C::THREADS), C::SMEM, st, A, B, C0, C1, C2, ep));
     return EII_OK;
 }
 
@@ -399,18 +424,16 @@ int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, 
                 uint8_t* planes, int P, int64_t* out64, cudaStream_t st) {
     const int rows_per_block = 16;  // 8 warps, two rows each
     ProfScope ps(e, EII_K_NORM, st);
-    k_rmsnorm<<<(rows + rows_per_block - 1) / rows_per_block, 256, 0, st>>>(x, rows, gain, shift, bits, planes, P,
-                                                                           out64);
-    CK(cudaGetLastError());
+    CK(launch_k(k_rmsnorm, dim3((rows + rows_per_block - 1) / rows_per_block), dim3(256), 0, st, x, rows, gain, shift,
+                bits, planes, P, out64));
     return EII_OK;
 }
 
 int launch_embed(eii_engine* e, const int64_t* ids, int rows, cudaStream_t st) {
     const int rows_per_block = 8;
     ProfScope ps(e, EII_K_EMBED, st);
-    k_embed<<<(rows + rows_per_block - 1) / rows_per_block, 32 * rows_per_block, 0, st>>>(ids, rows, e->emb_q, e->emb_m,
-                                                                                         e->emb_n, e->x, e->err_dev);
-    CK(cudaGetLastError());
+    CK(launch_k(k_embed, dim3((rows + rows_per_block - 1) / rows_per_block), dim3(32 * rows_per_block), 0, st, ids, rows,
+                (const int8_t*)e->emb_q, (const int32_t*)e->emb_m, (const int32_t*)e->emb_n, e->x, e->err_dev));
     return EII_OK;
 }
 
@@ -434,11 +457,10 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     {
         ProfScope ps(e, EII_K_ATTENTION, st);
         if (T <= 128 && !e->force_cuda_core_attention)
-            k_attention_tc<<<nseq * N_KV, ATTN_TC_THREADS, ATTN_TC_SMEM, st>>>(ap, e->err_dev);
+            CK(launch_k(k_attention_tc, dim3(nseq * N_KV), dim3(ATTN_TC_THREADS), ATTN_TC_SMEM, st, ap, e->err_dev));
         else
-            k_attention<<<nseq * N_KV, ATTN_WARPS * 32, attn_smem_bytes(T), st>>>(ap);
+            CK(launch_k(k_attention, dim3(nseq * N_KV), dim3(ATTN_WARPS * 32), attn_smem_bytes(T), st, ap));
     }
-    CK(cudaGetLastError());
 
     ep = EpiParams{};
     ep.M = rows; ep.N = D_MODEL; ep.K = D_MODEL; ep.msh = L.msh_o; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_o;

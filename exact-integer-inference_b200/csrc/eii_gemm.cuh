@@ -648,11 +648,13 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
             prefetch_tmap(&tmA);
             prefetch_tmap(&tmB);
+            griddep_wait();  // A is the previous kernel's output
             int stage = 0;
             uint32_t phase = 0;
             uint32_t fills = 0;
@@ -753,6 +755,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
                     reinterpret_cast<int4*>(silu_tab)[q] = __ldg(reinterpret_cast<const int4*>(ep.silu_neg) + q);
             }
         }
+        griddep_wait();  // outputs (and RESID's residual input) are shared with earlier kernels
         int acc_iter = 0;
         int dig_m = -1;     // LOGITS digest: row block whose sums this lane holds
         uint64_t dsum = 0;  //   sum over the columns seen so far of uint32(logit) * dig_b[col]

@@ -5,6 +5,7 @@
 #include <cstdint>
 
 #include "eii_int.cuh"
+#include "eii_ptx.cuh"
 
 namespace eii {
 
@@ -23,6 +24,8 @@ __global__ void k_embed(const int64_t* __restrict__ ids, int M, const int8_t* __
                         int32_t* __restrict__ x, int* err) {
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
+    griddep_wait();
+    griddep_launch();
     if (row >= M) return;
     int64_t id = ids[row];
     if (id < 0 || id >= VOCAB) {
@@ -93,6 +96,8 @@ __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* _
     const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
     const int l = threadIdx.x & 15;
     const bool live = row < M;
+    griddep_wait();
+    griddep_launch();
     const int4* xr = reinterpret_cast<const int4*>(x + static_cast<int64_t>(live ? row : 0) * D_MODEL);
     int4 v[9];
     int64_t A = 0, B = 0, C = 0;
@@ -209,6 +214,8 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attention(AttnParams ap) {
     int32_t* E = reinterpret_cast<int32_t*>(Vs + T * 33);  // [DMAX + 1]
     int32_t* wbuf = E + DMAX + 1 + 3;  // per warp: [T] scores/probabilities + [32] q row
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    griddep_wait();
+    griddep_launch();
 
     for (int i = threadIdx.x; i < T * 32; i += blockDim.x) {
         const int j = i / 32, w = i % 32;

@@ -66,6 +66,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// griddep_wait: returns once the grids this one depends on (the previous kernel in the stream, when
+// launched with programmatic stream serialization) have completed and their writes are visible; a
+// no-op otherwise.  griddep_launch: lets the dependent grid be scheduled once every CTA of this grid
+// has issued it (its own griddep_wait still waits for this grid to complete).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -237,3 +237,15 @@ def test_forward_t24_without_narrow_requant(base_model, base_model_path, monkeyp
         _check_set(e, base_model, "t24")
     finally:
         e.close()
+
+
+def test_forward_t128_without_programmatic_launch(base_model, base_model_path, monkeypatch):
+    """Kernels launched plainly (EII_PDL=0) and with programmatic stream serialization give the
+    same integers (each kernel waits for its predecessor before touching its outputs)."""
+    import _eii
+    monkeypatch.setenv("EII_PDL", "0")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        _check_set(e, base_model, "t128")
+    finally:
+        e.close()
