@@ -284,25 +284,36 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
             if (i < T) {
                 const int js = jstar_s[i];
                 int32_t out[16];
+                const bool cfast = ap.shift_c >= 1 && ap.shift_c <= 31;
+                const int64_t crnd = cfast ? (int64_t(1) << (ap.shift_c - 1)) : 0;
 #pragma unroll
                 for (int q = 0; q < 16; ++q) {
                     const int d = col + q;
                     int64_t a = static_cast<int64_t>(static_cast<int32_t>(c2[q])) * 65536 +
-                                static_cast<int64_t>(static_cast<int32_t>(c1[q])) * 256 +
-                                static_cast<int64_t>(static_cast<int32_t>(c0[q]));
+                                (static_cast<int64_t>(static_cast<int32_t>(c1[q])) * 256 +
+                                 static_cast<int64_t>(static_cast<int32_t>(c0[q])));
                     if (js >= 0) {
                         const int32_t vj = static_cast<int32_t>(VT[sw128(d, js)]) |
                                            (static_cast<int32_t>(static_cast<int8_t>(VT[8192 + sw128(d, js)])) << 8);
                         a += static_cast<int64_t>(vj) * 65536;
                     }
-                    out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
+                    if (cfast) {
+                        int32_t hi;
+                        uint32_t lo;
+                        shr31(a + crnd, ap.shift_c, hi, lo);
+                        out[q] = sat_hl(hi, lo, ap.bits_c);
+                    } else {
+                        out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
+                    }
                 }
+                // row-blocked planes: this warp's 32 rows x 16 dims are 512 contiguous bytes per plane
+                const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
+                uint8_t* dst = ap.ctx_planes + blocked_off(row0 + i, hh * 64 + col, D_MODEL);
                 for (int p = 0; p < ap.P; ++p) {
                     uint8_t b[16];
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) b[q] = plane_byte(out[q], p);
-                    *reinterpret_cast<uint4*>(ap.ctx_planes + (static_cast<int64_t>(p) * ap.M + row0 + i) * D_MODEL +
-                                              hh * 64 + col) = *reinterpret_cast<uint4*>(b);
+                    for (int q = 0; q < 16; ++q) b[q] = static_cast<uint8_t>(static_cast<uint32_t>(out[q]) >> (8 * p));
+                    *reinterpret_cast<uint4*>(dst + p * pstride) = *reinterpret_cast<uint4*>(b);
                 }
             }
         }

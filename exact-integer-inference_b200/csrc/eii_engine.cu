@@ -312,7 +312,7 @@ int ensure_rows(eii_engine* e, int rows) {
     TRY(dalloc(W, &e->q, (size_t)rows * D_MODEL));
     TRY(dalloc(W, &e->k, (size_t)rows * 192));
     TRY(dalloc(W, &e->v, (size_t)rows * 192));
-    TRY(dalloc(W, &e->ctx_planes, (size_t)4 * rows * D_MODEL));
+    TRY(dalloc(W, &e->ctx_planes, (size_t)4 * ((rows + 127) / 128) * 128 * D_MODEL));  // row-blocked
     TRY(dalloc(W, &e->gated_planes, (size_t)4 * ((rows + 127) / 128) * 128 * D_FF));  // row-blocked
     e->cap_rows = rows;
     return EII_OK;
@@ -347,8 +347,8 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
     if (it == e->maps.end()) {
         ActMaps am;
         TRY(map_planes(&am.h, e->h_planes, D_MODEL, rows, 2));
-        TRY(map_planes(&am.ctx2, e->ctx_planes, D_MODEL, rows, 2));
-        TRY(map_planes(&am.ctx4, e->ctx_planes, D_MODEL, rows, 4));
+        TRY(map_blocked(&am.ctx2, e->ctx_planes, D_MODEL, rows, 2));
+        TRY(map_blocked(&am.ctx4, e->ctx_planes, D_MODEL, rows, 4));
         TRY(map_blocked(&am.gated2, e->gated_planes, D_FF, rows, 2));
         TRY(map_blocked(&am.gated4, e->gated_planes, D_FF, rows, 4));
         TRY(map_out(&am.x32, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 32, 32));
@@ -464,6 +464,7 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
 
     ep = EpiParams{};
     ep.M = rows; ep.N = D_MODEL; ep.K = D_MODEL; ep.msh = L.msh_o; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_o;
+    ep.a_blocked = 1;
     TRY(launch_gemm_p<EPI_RESID>(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, L.Pc == 2 ? L.tm_o : L.tm_o64, ep, st,
                                  EII_K_GEMM_O, &am->x32, &am->x16));
 

@@ -172,6 +172,16 @@ __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* _
     }
 }
 
+// --------------------------------------------------------------------------- row-blocked planes
+// Activation byte planes read by the GEMMs through the row-blocked layout
+// [P][ceil(M/128)][K/16][128 rows][16 bytes]: byte k of row r of a plane sits at blocked_off(r, k, K),
+// so 32 consecutive rows x 16 bytes are 512 contiguous bytes (coalesced epilogue stores) and a GEMM
+// reads a 128-row x 128-byte K block as eight 2 KB runs (see map_blocked on the host).
+__host__ __device__ __forceinline__ int64_t blocked_off(int64_t r, int k, int K) {
+    return (r >> 7) * 128 * K + (k >> 4) * 2048 + (r & 127) * 16 + (k & 15);
+}
+__host__ __device__ __forceinline__ int64_t blocked_plane_stride(int64_t M, int K) { return ((M + 127) / 128) * 128 * K; }
+
 // --------------------------------------------------------------------------- attention
 // Integer causal attention of one sequence and one KV group (3 query heads), CUDA cores.
 //   s_ij = SAT16(RS(q_i . k_j, shift_s)), j <= i; rowmax; e = E[rowmax - s] (0 beyond DMAX);
@@ -186,7 +196,7 @@ struct AttnParams {
     const int16_t* k;  // [M, 192]
     const int16_t* v;  // [M, 192]
     const int32_t* exp_tab;  // [DMAX + 1]
-    uint8_t* ctx_planes;     // [P][M][576]
+    uint8_t* ctx_planes;     // row-blocked [P][ceil(M/128)][576/16][128 rows][16 bytes] (see blocked_off)
     int P;
     int M, T;
     int shift_s, shift_c, bits_c;
@@ -275,9 +285,10 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attention(AttnParams ap) {
         const int64_t c0 = sat64(rs64(a0, ap.shift_c), ap.bits_c), c1 = sat64(rs64(a1, ap.shift_c), ap.bits_c);
         const int64_t r = row0 + i;
         const int col = hh * 64 + 2 * lane;
+        const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
         for (int p = 0; p < ap.P; ++p) {
             const uint16_t pair = static_cast<uint16_t>(plane_byte(c0, p)) | (static_cast<uint16_t>(plane_byte(c1, p)) << 8);
-            *reinterpret_cast<uint16_t*>(ap.ctx_planes + (static_cast<int64_t>(p) * ap.M + r) * D_MODEL + col) = pair;
+            *reinterpret_cast<uint16_t*>(ap.ctx_planes + p * pstride + blocked_off(r, col, D_MODEL)) = pair;
         }
         __syncwarp();
     }
