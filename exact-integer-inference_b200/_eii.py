@@ -46,6 +46,13 @@ _SIGS = {
                          ctypes.c_int),
     "eii_linear": ([_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
                     ctypes.c_int, ctypes.c_int, _P, _P], ctypes.c_int),
+    "eii_decoder_open": ([_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)], ctypes.c_int),
+    "eii_decoder_prefill": ([_P, _P, ctypes.c_int, _P, _P], ctypes.c_int),
+    "eii_decoder_step": ([_P, _P, _P, _P], ctypes.c_int),
+    "eii_decoder_step_device": ([_P, _P, _P, ctypes.c_int64, _P, _P], ctypes.c_int),
+    "eii_decoder_position": ([_P], ctypes.c_int),
+    "eii_decoder_reset": ([_P], ctypes.c_int),
+    "eii_decoder_close": ([_P], None),
 }
 
 
@@ -175,6 +182,59 @@ class Engine:
         check(lib().eii_linear(self.h, ptr(a), M, K, int(bits_in), ptr(W), ptr(m), ptr(n), N, int(f_in), int(f_out),
                                int(bits_out), ptr(out), ptr(acc)))
         return out, acc
+
+
+class Decoder:
+    """Incremental decoding with a K/V cache (include/eii.h, eii_decoder_*), bit-exact with
+    recomputation: step t returns row t of Engine.forward on the first t + 1 tokens."""
+
+    def __init__(self, engine, n_seq, max_T):
+        h = ctypes.c_void_p()
+        check(lib().eii_decoder_open(engine.h, int(n_seq), int(max_T), ctypes.byref(h)))
+        self.h = h
+        self.engine = engine  # the engine must outlive the decoder
+        self.n_seq = int(n_seq)
+
+    def close(self):
+        if self.h:
+            lib().eii_decoder_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def position(self):
+        return lib().eii_decoder_position(self.h)
+
+    def reset(self):
+        check(lib().eii_decoder_reset(self.h))
+
+    def prefill(self, ids, logits=True, digests=False):
+        """ids [n_seq, T0] -> {"logits": [n_seq, T0, V] int32, "digests": [n_seq] uint64}."""
+        ids = _c(ids, np.int64)
+        n, T0 = ids.shape
+        lg = np.empty((n, T0, VOCAB), np.int32) if logits else None
+        dg = np.empty(n, np.uint64) if digests else None
+        check(lib().eii_decoder_prefill(self.h, ptr(ids), T0, ptr(lg), ptr(dg)))
+        return {k: v for k, v in (("logits", lg), ("digests", dg)) if v is not None}
+
+    def step(self, ids, logits=True, digests=False):
+        """ids [n_seq] (one token per sequence) -> {"logits": [n_seq, V] int32, "digests": [n_seq]}."""
+        ids = _c(ids, np.int64).reshape(-1)
+        lg = np.empty((self.n_seq, VOCAB), np.int32) if logits else None
+        dg = np.empty(self.n_seq, np.uint64) if digests else None
+        check(lib().eii_decoder_step(self.h, ptr(ids), ptr(lg), ptr(dg)))
+        return {k: v for k, v in (("logits", lg), ("digests", dg)) if v is not None}
+
+    def step_device(self, ids_ptr, logits_ptr=None, ld=VOCAB, digests_ptr=None, stream=None):
+        check(lib().eii_decoder_step_device(self.h, ctypes.c_void_p(ids_ptr),
+                                            ctypes.c_void_p(logits_ptr) if logits_ptr else None, ld,
+                                            ctypes.c_void_p(digests_ptr) if digests_ptr else None,
+                                            ctypes.c_void_p(stream) if stream else None))
 
 
 def _mix64(z):

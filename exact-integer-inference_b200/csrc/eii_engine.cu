@@ -227,6 +227,15 @@ struct eii_engine {
     int64_t prof_n[EII_NUM_KERNEL_KINDS] = {};
 };
 
+// K/V cache of a decoder: per layer [n_seq][max_T][192] int16 post-RoPE k and v.
+struct eii_decoder {
+    eii_engine* e = nullptr;
+    int n_seq = 0, max_T = 0, pos = 0;
+    int16_t* kc = nullptr;
+    int16_t* vc = nullptr;
+    std::vector<void*> mem;
+};
+
 namespace {
 
 template <class T>
@@ -437,11 +446,23 @@ int launch_embed(eii_engine* e, const int64_t* ids, int rows, cudaStream_t st) {
     return EII_OK;
 }
 
-int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
+// K/V cache hook of run_layer for incremental decoding: the layer's cache [n_seq][max_T][192]
+// (post-RoPE k, and v) starting at sequence seq0 of the launch.  pos < 0: a prompt pass of T
+// tokens per sequence (rows stored at positions 0..T-1, attention as usual); pos >= 0: one token
+// per sequence at position pos (stored there, attention against positions 0..pos of the cache).
+struct KvHook {
+    int16_t* kc;
+    int16_t* vc;
+    int max_T;
+    int pos;
+};
+
+int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHook* kv = nullptr) {
     LayerDev& L = e->L[l];
     const ActMaps* am;
     TRY(act_maps(e, rows, &am));
     const int nseq = rows / T;
+    const bool decode = kv && kv->pos >= 0;
     TRY(launch_norm(e, e->x, rows, L.ln1, L.norm1_shift, L.h.bits, e->h_planes, 2, nullptr, st));
 
     EpiParams ep{};
@@ -449,12 +470,27 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
     ep.T = T; ep.q_out = e->q; ep.k_out = e->k; ep.v_out = e->v; ep.rope_c = e->rope_c; ep.rope_s = e->rope_s;
     ep.bits_q = L.q.bits; ep.bits_k = L.k.bits; ep.bits_v = L.v.bits; ep.bits_qr = L.qr.bits; ep.bits_kr = L.kr.bits;
     ep.rope_shift_q = L.rope_shift_q; ep.rope_shift_k = L.rope_shift_k; ep.fast = L.fast_qkv; ep.narrow = L.narrow_qkv;
+    ep.pos0 = decode ? kv->pos : 0;
     TRY(launch_gemm<2, EPI_QKV>(e, am->h, L.tm_qkv, ep, st, EII_K_GEMM_QKV, &am->q, &am->k, &am->v));
 
+    if (kv) {  // keep this pass's k, v rows: T per sequence (prompt) or one at position pos (step)
+        const size_t row = 192 * sizeof(int16_t), pitch = row * kv->max_T;
+        const int p0 = decode ? kv->pos : 0;
+        CK(cudaMemcpy2DAsync(kv->kc + (size_t)p0 * 192, pitch, e->k, row * T, row * T, nseq, cudaMemcpyDeviceToDevice, st));
+        CK(cudaMemcpy2DAsync(kv->vc + (size_t)p0 * 192, pitch, e->v, row * T, row * T, nseq, cudaMemcpyDeviceToDevice, st));
+    }
+    if (decode) {
+        AttnDecodeParams dp{};
+        dp.q = e->q; dp.kc = kv->kc; dp.vc = kv->vc; dp.max_T = kv->max_T; dp.L = kv->pos + 1; dp.exp_tab = e->exp_tab;
+        dp.ctx_planes = e->ctx_planes; dp.P = L.Pc; dp.M = rows;
+        dp.shift_s = L.shift_s; dp.shift_c = L.shift_c; dp.bits_c = L.c.bits;
+        ProfScope ps(e, EII_K_ATTENTION, st);
+        CK(launch_k(k_attention_decode, dim3(nseq), dim3(N_HEADS * 32), 0, st, dp));
+    }
     AttnParams ap{};
     ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;
     ap.M = rows; ap.T = T; ap.shift_s = L.shift_s; ap.shift_c = L.shift_c; ap.bits_c = L.c.bits;
-    {
+    if (!decode) {
         ProfScope ps(e, EII_K_ATTENTION, st);
         if (T <= 128 && !e->force_cuda_core_attention)
             CK(launch_k(k_attention_tc, dim3(nseq * N_KV), dim3(ATTN_TC_THREADS), ATTN_TC_SMEM, st, ap, e->err_dev));
@@ -489,14 +525,16 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st) {
 
 // Final norm and logits of `rows` rows (whole sequences of T tokens); with digests != nullptr the
 // per-sequence digests of these rows are accumulated into digests[0 .. rows / T) (zeroed by the caller).
-int run_logits(eii_engine* e, int rows, int T, int32_t* logits, int64_t ld, uint64_t* digests, cudaStream_t st) {
+int run_logits(eii_engine* e, int rows, int T, int32_t* logits, int64_t ld, uint64_t* digests, cudaStream_t st,
+               int pos0 = 0) {
     const ActMaps* am;
     TRY(act_maps(e, rows, &am));
     TRY(launch_norm(e, e->x, rows, e->final_q, e->final_shift, 16, e->h_planes, 2, nullptr, st));
     EpiParams ep{};
     ep.M = rows; ep.N = VOCAB; ep.K = D_MODEL; ep.msh = e->msh_logits; ep.err = e->err_dev;
     ep.logits = logits; ep.ld_logits = ld; ep.fast = e->fast_logits;
-    ep.T = T; ep.dig = reinterpret_cast<unsigned long long*>(digests); ep.dig_a = e->dig_a; ep.dig_b = e->dig_b;
+    ep.T = T; ep.pos0 = pos0;
+    ep.dig = reinterpret_cast<unsigned long long*>(digests); ep.dig_a = e->dig_a; ep.dig_b = e->dig_b;
     CUtensorMap lm;
     TRY(map_out(&lm, logits, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, VOCAB, rows, (uint64_t)ld * 4, 32, 32));
     return launch_gemm<2, EPI_LOGITS>(e, am->h, e->tm_emb, ep, st, EII_K_GEMM_LOGITS, &lm);
@@ -840,6 +878,13 @@ int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
     return EII_OK;
 }
 
+
+// ------------------------------------------------------------------------- incremental decoding
+KvHook dec_hook(eii_decoder* d, int l, int seq0, int pos) {
+    const size_t off = ((size_t)l * d->n_seq + seq0) * d->max_T * 192;
+    return KvHook{d->kc + off, d->vc + off, d->max_T, pos};
+}
+
 int check_forward_args(eii_engine* e, int n_seq, int T) {
     if (!e) return fail(EII_ERR_ARG, "engine is null");
     if (n_seq < 1) return fail(EII_ERR_ARG, "n_seq must be >= 1 (got %d)", n_seq);
@@ -851,6 +896,95 @@ int check_ids_host(const int64_t* ids, int64_t n) {
     for (int64_t i = 0; i < n; ++i)
         if (ids[i] < 0 || ids[i] >= VOCAB) return fail(EII_ERR_ARG, "ids[%lld] = %lld outside [0, %d)", (long long)i, (long long)ids[i], VOCAB);
     return EII_OK;
+}
+
+// The forward pass of n_seq sequences of T tokens from host ids (eii_forward), or with a decoder:
+// pos < 0 a prompt pass that also fills the K/V cache, pos >= 0 one decoding step (T = 1) at that
+// position.  Sequences are processed in chunks of the engine's workspace.
+int forward_host(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* embed_out, int32_t* resid_out,
+                 int32_t* logits_out, uint64_t* digests, eii_decoder* dec, int pos) {
+    if (!ids) return fail(EII_ERR_ARG, "ids is null");
+    TRY(check_ids_host(ids, (int64_t)n_seq * T));
+    CK(cudaSetDevice(e->device));
+    cudaStream_t st = e->stream;
+    const int cs = chunk_seqs_for(n_seq, T);
+    TRY(ensure_rows(e, cs * T));
+    TRY(ensure_ids(e, (int64_t)cs * T));
+    if (logits_out || digests) TRY(ensure_logits_ws(e, cs * T));
+    uint64_t* dig_dev = nullptr;
+    std::vector<void*> tmp;
+    if (digests) TRY(dalloc(tmp, &dig_dev, (size_t)cs));
+    int rc = EII_OK;
+    const size_t row_bytes = (size_t)D_MODEL * sizeof(int32_t);
+    for (int s0 = 0; s0 < n_seq && rc == EII_OK; s0 += cs) {
+        const int ns = (n_seq - s0) < cs ? (n_seq - s0) : cs;
+        const int rows = ns * T;
+        if (cudaMemcpyAsync(e->ids_dev, ids + (int64_t)s0 * T, sizeof(int64_t) * rows, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+            rc = fail(EII_ERR_CUDA, "ids upload failed");
+            break;
+        }
+        rc = launch_embed(e, e->ids_dev, rows, st);
+        if (rc == EII_OK && embed_out &&
+            cudaMemcpyAsync(embed_out + (int64_t)s0 * T * D_MODEL, e->x, row_bytes * rows, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            rc = fail(EII_ERR_CUDA, "embed download failed");
+        for (int l = 0; l < N_LAYERS && rc == EII_OK; ++l) {
+            KvHook kv;
+            if (dec) kv = dec_hook(dec, l, s0, pos);
+            rc = run_layer(e, l, rows, T, st, dec ? &kv : nullptr);
+            if (rc == EII_OK && resid_out) {
+                // resid_out is [n_seq][30][T][576]: one T x 576 block per sequence and layer.
+                const size_t blk = row_bytes * T;
+                if (cudaMemcpy2DAsync(resid_out + ((int64_t)s0 * N_LAYERS + l) * T * D_MODEL, blk * N_LAYERS, e->x, blk,
+                                      blk, ns, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                    rc = fail(EII_ERR_CUDA, "residual download failed");
+            }
+        }
+        if (rc == EII_OK && (logits_out || digests)) {
+            if (digests && cudaMemsetAsync(dig_dev, 0, sizeof(uint64_t) * ns, st) != cudaSuccess)
+                rc = fail(EII_ERR_CUDA, "digest reset failed");
+            if (rc == EII_OK) rc = run_logits(e, rows, T, e->logits_ws, VOCAB, digests ? dig_dev : nullptr, st, pos < 0 ? 0 : pos);
+            if (rc == EII_OK && logits_out &&
+                cudaMemcpyAsync(logits_out + (int64_t)s0 * T * VOCAB, e->logits_ws, sizeof(int32_t) * (size_t)rows * VOCAB,
+                                cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                rc = fail(EII_ERR_CUDA, "logits download failed");
+            if (rc == EII_OK && digests &&
+                cudaMemcpyAsync(digests + s0, dig_dev, sizeof(uint64_t) * ns, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                rc = fail(EII_ERR_CUDA, "digest download failed");
+        }
+        if (rc == EII_OK) rc = check_device_error(e, st);
+    }
+    free_list(tmp);
+    return rc;
+}
+
+// Device-resident forward (eii_forward_device), or a decoder prompt pass / step as in forward_host.
+int forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int32_t* logits_dev, int64_t ld,
+                   uint64_t* digests_dev, void* stream, eii_decoder* dec, int pos) {
+    if (!ids_dev) return fail(EII_ERR_ARG, "ids_dev is null");
+    if (logits_dev && (ld < VOCAB || (ld % 4) != 0 || (reinterpret_cast<uintptr_t>(logits_dev) & 15)))
+        return fail(EII_ERR_ARG, "logits_dev must be 16-byte aligned with ld >= %d, ld %% 4 == 0", VOCAB);
+    CK(cudaSetDevice(e->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+    const int cs = chunk_seqs_for(n_seq, T);
+    TRY(ensure_rows(e, cs * T));
+    if (!logits_dev && digests_dev) TRY(ensure_logits_ws(e, cs * T));
+    if (digests_dev) CK(cudaMemsetAsync(digests_dev, 0, sizeof(uint64_t) * n_seq, st));
+    for (int s0 = 0; s0 < n_seq; s0 += cs) {
+        const int ns = (n_seq - s0) < cs ? (n_seq - s0) : cs;
+        const int rows = ns * T;
+        TRY(launch_embed(e, ids_dev + (int64_t)s0 * T, rows, st));
+        for (int l = 0; l < N_LAYERS; ++l) {
+            KvHook kv;
+            if (dec) kv = dec_hook(dec, l, s0, pos);
+            TRY(run_layer(e, l, rows, T, st, dec ? &kv : nullptr));
+        }
+        if (logits_dev || digests_dev) {
+            int32_t* lg = logits_dev ? logits_dev + (int64_t)s0 * T * ld : e->logits_ws;
+            const int64_t lld = logits_dev ? ld : VOCAB;
+            TRY(run_logits(e, rows, T, lg, lld, digests_dev ? digests_dev + s0 : nullptr, st, pos < 0 ? 0 : pos));
+        }
+    }
+    return check_device_error(e, st);
 }
 
 }  // namespace
@@ -928,82 +1062,80 @@ void eii_close(eii_engine* e) {
 int eii_forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int32_t* logits_dev, int64_t ld,
                        uint64_t* digests_dev, void* stream) {
     TRY(check_forward_args(e, n_seq, T));
-    if (!ids_dev) return fail(EII_ERR_ARG, "ids_dev is null");
-    if (logits_dev && (ld < VOCAB || (ld % 4) != 0 || (reinterpret_cast<uintptr_t>(logits_dev) & 15)))
-        return fail(EII_ERR_ARG, "logits_dev must be 16-byte aligned with ld >= %d, ld %% 4 == 0", VOCAB);
-    CK(cudaSetDevice(e->device));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
-    const int cs = chunk_seqs_for(n_seq, T);
-    TRY(ensure_rows(e, cs * T));
-    if (!logits_dev && digests_dev) TRY(ensure_logits_ws(e, cs * T));
-    if (digests_dev) CK(cudaMemsetAsync(digests_dev, 0, sizeof(uint64_t) * n_seq, st));
-    for (int s0 = 0; s0 < n_seq; s0 += cs) {
-        const int ns = (n_seq - s0) < cs ? (n_seq - s0) : cs;
-        const int rows = ns * T;
-        TRY(launch_embed(e, ids_dev + (int64_t)s0 * T, rows, st));
-        for (int l = 0; l < N_LAYERS; ++l) TRY(run_layer(e, l, rows, T, st));
-        if (logits_dev || digests_dev) {
-            int32_t* lg = logits_dev ? logits_dev + (int64_t)s0 * T * ld : e->logits_ws;
-            const int64_t lld = logits_dev ? ld : VOCAB;
-            TRY(run_logits(e, rows, T, lg, lld, digests_dev ? digests_dev + s0 : nullptr, st));
-        }
-    }
-    return check_device_error(e, st);
+    return forward_device(e, ids_dev, n_seq, T, logits_dev, ld, digests_dev, stream, nullptr, -1);
 }
 
 int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* embed_out, int32_t* resid_out,
                 int32_t* logits_out, uint64_t* digests) {
     TRY(check_forward_args(e, n_seq, T));
-    if (!ids) return fail(EII_ERR_ARG, "ids is null");
-    TRY(check_ids_host(ids, (int64_t)n_seq * T));
+    return forward_host(e, ids, n_seq, T, embed_out, resid_out, logits_out, digests, nullptr, -1);
+}
+
+int eii_decoder_open(eii_engine* e, int n_seq, int max_T, eii_decoder** out) {
+    if (!out) return fail(EII_ERR_ARG, "out is null");
+    *out = nullptr;
+    if (!e) return fail(EII_ERR_ARG, "engine is null");
+    if (n_seq < 1) return fail(EII_ERR_ARG, "n_seq must be >= 1 (got %d)", n_seq);
+    if (max_T < 1 || max_T > DECODE_MAX_L) return fail(EII_ERR_ARG, "max_T must be in [1, %d] (got %d)", DECODE_MAX_L, max_T);
     CK(cudaSetDevice(e->device));
-    cudaStream_t st = e->stream;
-    const int cs = chunk_seqs_for(n_seq, T);
-    TRY(ensure_rows(e, cs * T));
-    TRY(ensure_ids(e, (int64_t)cs * T));
-    if (logits_out || digests) TRY(ensure_logits_ws(e, cs * T));
-    uint64_t* dig_dev = nullptr;
-    std::vector<void*> tmp;
-    if (digests) TRY(dalloc(tmp, &dig_dev, (size_t)cs));
-    int rc = EII_OK;
-    const size_t row_bytes = (size_t)D_MODEL * sizeof(int32_t);
-    for (int s0 = 0; s0 < n_seq && rc == EII_OK; s0 += cs) {
-        const int ns = (n_seq - s0) < cs ? (n_seq - s0) : cs;
-        const int rows = ns * T;
-        if (cudaMemcpyAsync(e->ids_dev, ids + (int64_t)s0 * T, sizeof(int64_t) * rows, cudaMemcpyHostToDevice, st) != cudaSuccess) {
-            rc = fail(EII_ERR_CUDA, "ids upload failed");
-            break;
-        }
-        rc = launch_embed(e, e->ids_dev, rows, st);
-        if (rc == EII_OK && embed_out &&
-            cudaMemcpyAsync(embed_out + (int64_t)s0 * T * D_MODEL, e->x, row_bytes * rows, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-            rc = fail(EII_ERR_CUDA, "embed download failed");
-        for (int l = 0; l < N_LAYERS && rc == EII_OK; ++l) {
-            rc = run_layer(e, l, rows, T, st);
-            if (rc == EII_OK && resid_out) {
-                // resid_out is [n_seq][30][T][576]: one T x 576 block per sequence and layer.
-                const size_t blk = row_bytes * T;
-                if (cudaMemcpy2DAsync(resid_out + ((int64_t)s0 * N_LAYERS + l) * T * D_MODEL, blk * N_LAYERS, e->x, blk,
-                                      blk, ns, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-                    rc = fail(EII_ERR_CUDA, "residual download failed");
-            }
-        }
-        if (rc == EII_OK && (logits_out || digests)) {
-            if (digests && cudaMemsetAsync(dig_dev, 0, sizeof(uint64_t) * ns, st) != cudaSuccess)
-                rc = fail(EII_ERR_CUDA, "digest reset failed");
-            if (rc == EII_OK) rc = run_logits(e, rows, T, e->logits_ws, VOCAB, digests ? dig_dev : nullptr, st);
-            if (rc == EII_OK && logits_out &&
-                cudaMemcpyAsync(logits_out + (int64_t)s0 * T * VOCAB, e->logits_ws, sizeof(int32_t) * (size_t)rows * VOCAB,
-                                cudaMemcpyDeviceToHost, st) != cudaSuccess)
-                rc = fail(EII_ERR_CUDA, "logits download failed");
-            if (rc == EII_OK && digests &&
-                cudaMemcpyAsync(digests + s0, dig_dev, sizeof(uint64_t) * ns, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-                rc = fail(EII_ERR_CUDA, "digest download failed");
-        }
-        if (rc == EII_OK) rc = check_device_error(e, st);
+    eii_decoder* d = new eii_decoder();
+    d->e = e;
+    d->n_seq = n_seq;
+    d->max_T = max_T;
+    const size_t n = (size_t)N_LAYERS * n_seq * max_T * 192;
+    int rc = dalloc(d->mem, &d->kc, n);
+    if (rc == EII_OK) rc = dalloc(d->mem, &d->vc, n);
+    if (rc != EII_OK) {
+        free_list(d->mem);
+        delete d;
+        return rc;
     }
-    free_list(tmp);
-    return rc;
+    *out = d;
+    return EII_OK;
+}
+
+int eii_decoder_prefill(eii_decoder* d, const int64_t* ids, int T0, int32_t* logits_out, uint64_t* digests) {
+    if (!d) return fail(EII_ERR_ARG, "decoder is null");
+    if (d->pos != 0) return fail(EII_ERR_ARG, "prefill comes first (the decoder is at position %d; reset it)", d->pos);
+    if (T0 < 1 || T0 > d->max_T) return fail(EII_ERR_ARG, "T0 must be in [1, %d] (got %d)", d->max_T, T0);
+    CK(cudaSetDevice(d->e->device));
+    TRY(forward_host(d->e, ids, d->n_seq, T0, nullptr, nullptr, logits_out, digests, d, -1));
+    d->pos = T0;
+    return EII_OK;
+}
+
+int eii_decoder_step(eii_decoder* d, const int64_t* ids, int32_t* logits_out, uint64_t* digests) {
+    if (!d) return fail(EII_ERR_ARG, "decoder is null");
+    if (d->pos >= d->max_T) return fail(EII_ERR_ARG, "the K/V cache is full (max_T = %d)", d->max_T);
+    CK(cudaSetDevice(d->e->device));
+    TRY(forward_host(d->e, ids, d->n_seq, 1, nullptr, nullptr, logits_out, digests, d, d->pos));
+    ++d->pos;
+    return EII_OK;
+}
+
+int eii_decoder_step_device(eii_decoder* d, const int64_t* ids_dev, int32_t* logits_dev, int64_t ld,
+                            uint64_t* digests_dev, void* stream) {
+    if (!d) return fail(EII_ERR_ARG, "decoder is null");
+    if (d->pos >= d->max_T) return fail(EII_ERR_ARG, "the K/V cache is full (max_T = %d)", d->max_T);
+    TRY(forward_device(d->e, ids_dev, d->n_seq, 1, logits_dev, ld, digests_dev, stream, d, d->pos));
+    ++d->pos;
+    return EII_OK;
+}
+
+int eii_decoder_position(const eii_decoder* d) { return d ? d->pos : -1; }
+
+int eii_decoder_reset(eii_decoder* d) {
+    if (!d) return fail(EII_ERR_ARG, "decoder is null");
+    d->pos = 0;
+    return EII_OK;
+}
+
+void eii_decoder_close(eii_decoder* d) {
+    if (!d) return;
+    cudaSetDevice(d->e->device);
+    if (d->e->stream) cudaStreamSynchronize(d->e->stream);
+    free_list(d->mem);
+    delete d;
 }
 
 int eii_embed(eii_engine* e, const int64_t* ids, int n, int64_t* x_out) {

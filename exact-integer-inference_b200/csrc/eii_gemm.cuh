@@ -45,6 +45,7 @@ struct EpiParams {
     int* err;
     // EPI_QKV: q [M,576] k [M,192] v [M,192] int16; RoPE tables int32 [512,32]; position = row % T
     int T;
+    int pos0;  // position of the first row of each T-row sequence (incremental decoding: the step's position)
     int16_t* q_out;
     int16_t* k_out;
     int16_t* v_out;
@@ -79,7 +80,7 @@ struct EpiParams {
     // EPI_LOGITS: int32 out[row * ld + col] = RS(acc m, shift) (low 32 bits, no SAT)
     int32_t* logits;
     int64_t ld_logits;
-    // EPI_LOGITS, optional per-sequence digest of the logits (sequence = row / T, position t = row % T):
+    // EPI_LOGITS, optional per-sequence digest of the logits (sequence = row / T, position t = pos0 + row % T):
     //   dig[seq] += sum over (t, v) of uint32(logit) * dig_b[v] * dig_a[t]  (mod 2^64)
     // accumulated per row in registers over a CTA's contiguous run of tiles, one atomic per row and run.
     unsigned long long* dig;
@@ -319,7 +320,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
         const int bits_r = region == 0 ? ep.bits_qr : ep.bits_kr;
         const int rshift = region == 0 ? ep.rope_shift_q : ep.rope_shift_k;
         const CUtensorMap* omap = region == 0 ? maps.c0 : (region == 1 ? maps.c1 : maps.c2);
-        const int pos = row_ok ? row % ep.T : 0;
+        const int pos = row_ok ? ep.pos0 + row % ep.T : 0;
         const int64_t rrnd = rshift >= 1 ? (int64_t(1) << (rshift - 1)) : 0;
         // staging: dims [sub, sub + 16) and [32 + sub, 32 + sub + 16) of the head, 32 rows each (SW32)
         uint8_t* sa = stg;
@@ -762,7 +763,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
         auto dig_flush = [&]() {
             const int r = dig_m * 128 + quad * 32 + lane;
             if (dig_m >= 0 && r < ep.M)
-                atomicAdd(ep.dig + r / ep.T, static_cast<unsigned long long>(dsum * __ldg(ep.dig_a + r % ep.T)));
+                atomicAdd(ep.dig + r / ep.T, static_cast<unsigned long long>(dsum * __ldg(ep.dig_a + ep.pos0 + r % ep.T)));
             dsum = 0;
         };
         for (int t = t_first; t < t_end; t += t_step, ++acc_iter) {

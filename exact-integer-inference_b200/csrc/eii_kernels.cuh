@@ -294,6 +294,106 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attention(AttnParams ap) {
     }
 }
 
+// --------------------------------------------------------------------------- decode attention
+// One query row per sequence against a K/V cache (incremental decoding): row i = L - 1 of the causal
+// attention above, with keys 0 .. L-1 read from the cache [n_seq][max_T][192] (post-RoPE k, and v,
+// exactly as the prompt pass stored them).  Block = one sequence, warp w = head w (KV group w / 3);
+// lanes split the keys for the scores and the 64 dims (two each) for P.V.  Same integer operations
+// as k_attention, so the row equals the one a full recomputation produces.
+struct AttnDecodeParams {
+    const int16_t* q;        // [n, 576] queries of this step
+    const int16_t* kc;       // cache of this layer, first sequence of the launch
+    const int16_t* vc;
+    int max_T;               // cache rows per sequence
+    int L;                   // keys per sequence (position + 1), <= DECODE_MAX_L
+    const int32_t* exp_tab;  // [DMAX + 1]
+    uint8_t* ctx_planes;     // row-blocked planes (blocked_off), rows = sequences
+    int P, M;
+    int shift_s, shift_c, bits_c;
+};
+
+constexpr int DECODE_MAX_L = ROPE_POS;
+
+__global__ void __launch_bounds__(N_HEADS * 32) k_attention_decode(AttnDecodeParams ap) {
+    __shared__ int32_t E[DMAX + 1 + 3];
+    __shared__ int32_t Pw[N_HEADS][DECODE_MAX_L];
+    const int seq = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int hh = warp, g = hh / 3, L = ap.L;
+    griddep_wait();
+    griddep_launch();
+    for (int i = threadIdx.x; i <= DMAX; i += blockDim.x) E[i] = ap.exp_tab[i];
+    uint32_t qr[32];  // the query row of this head, 64 int16 as 32 pairs
+    {
+        const uint4* q4 = reinterpret_cast<const uint4*>(ap.q + static_cast<int64_t>(seq) * D_MODEL + hh * 64);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const uint4 t = __ldg(q4 + w);
+            qr[4 * w] = t.x; qr[4 * w + 1] = t.y; qr[4 * w + 2] = t.z; qr[4 * w + 3] = t.w;
+        }
+    }
+    __syncthreads();
+    const int16_t* kb = ap.kc + static_cast<int64_t>(seq) * ap.max_T * 192 + g * 64;
+    const int16_t* vb = ap.vc + static_cast<int64_t>(seq) * ap.max_T * 192 + g * 64;
+    int32_t* pw = Pw[warp];
+    // scores s_j = SAT16(RS(q . k_j, shift_s)), keys j = lane + 32 m
+    int32_t lmax = INT32_MIN;
+    for (int j = lane; j < L; j += 32) {
+        const uint4* k4 = reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(j) * 192);
+        int64_t acc = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const uint4 t = __ldg(k4 + w);
+            acc += dot_pair(qr[4 * w], t.x) + dot_pair(qr[4 * w + 1], t.y) + dot_pair(qr[4 * w + 2], t.z) +
+                   dot_pair(qr[4 * w + 3], t.w);
+        }
+        const int32_t sj = static_cast<int32_t>(sat64(rs64(acc, ap.shift_s), 16));
+        pw[j] = sj;
+        lmax = max(lmax, sj);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    __syncwarp();
+    // e_j = E[rowmax - s_j] (0 beyond DMAX), Z = sum e
+    int64_t lz = 0;
+    for (int j = lane; j < L; j += 32) {
+        const int32_t dd = lmax - pw[j];
+        const int32_t ej = dd <= DMAX ? E[dd] : 0;
+        pw[j] = ej;
+        lz += ej;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lz += __shfl_xor_sync(0xffffffffu, lz, o);
+    // P_j = floor((e_j 65536 + floor(Z/2)) / Z), exact (double estimate, integer remainder fix-up)
+    const int64_t Z = lz, half = Z / 2;
+    const double rz = 1.0 / static_cast<double>(Z);
+    for (int j = lane; j < L; j += 32) {
+        const int64_t n = static_cast<int64_t>(pw[j]) * 65536 + half;
+        int64_t p = static_cast<int64_t>(static_cast<double>(n) * rz);
+        int64_t r = n - p * Z;
+        if (r < 0) { --p; r += Z; }
+        if (r < 0) { --p; r += Z; }
+        if (r >= Z) { ++p; r -= Z; }
+        if (r >= Z) { ++p; }
+        pw[j] = static_cast<int32_t>(p);
+    }
+    __syncwarp();
+    // ctx_d = SAT(RS(sum_j P_j v_jd, shift_c), bits_c), dims 2 lane and 2 lane + 1
+    int64_t a0 = 0, a1 = 0;
+    for (int j = 0; j < L; ++j) {
+        const int64_t p = pw[j];
+        const uint32_t vv = __ldg(reinterpret_cast<const uint32_t*>(vb + static_cast<int64_t>(j) * 192) + lane);
+        a0 += p * static_cast<int16_t>(vv & 0xFFFF);
+        a1 += p * static_cast<int16_t>(vv >> 16);
+    }
+    const int64_t c0 = sat64(rs64(a0, ap.shift_c), ap.bits_c), c1 = sat64(rs64(a1, ap.shift_c), ap.bits_c);
+    const int col = hh * 64 + 2 * lane;
+    const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
+    for (int p = 0; p < ap.P; ++p) {
+        const uint16_t pair = static_cast<uint16_t>(plane_byte(c0, p)) | (static_cast<uint16_t>(plane_byte(c1, p)) << 8);
+        *reinterpret_cast<uint16_t*>(ap.ctx_planes + p * pstride + blocked_off(seq, col, D_MODEL)) = pair;
+    }
+}
+
 // --------------------------------------------------------------------------- plane split
 // int64 activations [M,K] (values within b = 8P bits) -> P byte planes [P][M][K].
 __global__ void k_split_planes(const int64_t* __restrict__ a, int64_t count, int P, int64_t plane_stride,

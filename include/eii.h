@@ -68,6 +68,29 @@ int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* em
 int eii_forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int32_t* logits_dev,
                        int64_t ld_logits, uint64_t* digests_dev, void* stream);
 
+/* Incremental (cached) decoding, bit-exact with recomputation.  No reference counterpart: the
+ * reference recomputes the whole prefix (python/intref.py:288-301) and lists cached decoding as
+ * open work.  A decoder holds, per layer, the post-RoPE k and v rows [n_seq][max_T][192] of its
+ * sequences (max_T <= 512, the RoPE table length).  eii_decoder_prefill runs the forward pass on
+ * T0 prompt tokens per sequence (outputs as eii_forward: logits [n_seq][T0][49152], digests) and
+ * fills the cache; each eii_decoder_step then takes one token per sequence (ids [n_seq]) at the
+ * current position t and returns its logits row [n_seq][49152] and/or per-sequence digests with
+ * position weight t.  The logits of step t equal row t of eii_forward on the first t + 1 tokens,
+ * and the prefill and step digests add up (mod 2^64) to the eii_forward digest of the whole
+ * sequence.  Decoding may also start at position 0 without a prefill.  The decoder uses the
+ * engine's stream and workspace: calls on one engine (and its decoders) are serialised, and the
+ * engine must outlive its decoders. */
+typedef struct eii_decoder eii_decoder;
+int eii_decoder_open(eii_engine* e, int n_seq, int max_T, eii_decoder** out);
+int eii_decoder_prefill(eii_decoder* d, const int64_t* ids, int T0, int32_t* logits_out, uint64_t* digests);
+int eii_decoder_step(eii_decoder* d, const int64_t* ids, int32_t* logits_out, uint64_t* digests);
+/* Device pointers as in eii_forward_device (logits_dev rows of ld_logits elements). */
+int eii_decoder_step_device(eii_decoder* d, const int64_t* ids_dev, int32_t* logits_dev, int64_t ld_logits,
+                            uint64_t* digests_dev, void* stream);
+int eii_decoder_position(const eii_decoder* d); /* tokens in the cache, -1 for a null decoder */
+int eii_decoder_reset(eii_decoder* d);          /* back to position 0 (the cache is reused) */
+void eii_decoder_close(eii_decoder* d);
+
 /* Single steps for the drop-in Python Model (host int64 buffers, python/intref.py names). */
 
 /* Model.embed (python/intref.py:163-166): ids [n] -> x [n][576]. */

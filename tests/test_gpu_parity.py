@@ -249,3 +249,67 @@ def test_forward_t128_without_programmatic_launch(base_model, base_model_path, m
         _check_set(e, base_model, "t128")
     finally:
         e.close()
+
+
+# ------------------------------------------------------------------------------ incremental decoding
+def _decode_check(eng, ids, T0):
+    """Prefill T0 tokens, decode the rest one token per step; every logits row must equal the full
+    forward's, and the prefill and step digests must add up to the forward digest."""
+    import _eii
+    n, T = ids.shape
+    ref = eng.forward(ids, logits=True, digests=True)
+    dec = _eii.Decoder(eng, n, T)
+    try:
+        total = np.zeros(n, np.uint64)
+        if T0 > 0:
+            out = dec.prefill(ids[:, :T0], logits=True, digests=True)
+            assert np.array_equal(out["logits"], ref["logits"][:, :T0])
+            total += out["digests"]
+        assert dec.position == T0
+        for t in range(T0, T):
+            out = dec.step(ids[:, t], logits=True, digests=True)
+            d = first_diff(out["logits"], ref["logits"][:, t])
+            assert d is None, (t, d)
+            total += out["digests"]
+        assert dec.position == T
+        assert np.array_equal(total, ref["digests"])
+        with pytest.raises(_eii.EiiError) as ei:
+            dec.step(ids[:, 0])
+        assert ei.value.code == _eii.EII_ERR_ARG  # the cache is full
+    finally:
+        dec.close()
+
+
+def test_decode_matches_recomputation(eng):
+    ids = np.stack([synth.window_ids(64, 24), synth.window_ids(65, 24), synth.window_ids(66, 24)])
+    _decode_check(eng, ids, 5)
+
+
+def test_decode_from_empty_cache(eng):
+    _decode_check(eng, synth.window_ids(70, 9)[None, :], 0)
+
+
+def test_decode_outlier_model_long_prompt(eng_outlier):
+    """T = 160 (beyond the tensor-core attention's 128): prompt 150, then 10 steps."""
+    g = golden("vectors_t160.json")
+    ids = synth.window_ids(g["window"], g["tokens"])[None, :]
+    _decode_check(eng_outlier, ids, 150)
+
+
+def test_decoder_arguments(eng):
+    import _eii
+    with pytest.raises(_eii.EiiError):
+        _eii.Decoder(eng, 2, 513)
+    dec = _eii.Decoder(eng, 2, 8)
+    try:
+        with pytest.raises(_eii.EiiError):
+            dec.prefill(np.zeros((2, 9), np.int64))
+        dec.prefill(np.zeros((2, 3), np.int64), logits=False)
+        with pytest.raises(_eii.EiiError):
+            dec.prefill(np.zeros((2, 3), np.int64), logits=False)  # prefill comes first
+        with pytest.raises(_eii.EiiError):
+            dec.step(np.array([0, 49152], np.int64))
+        dec.reset()
+        assert dec.position == 0
+    finally:
+        dec.close()
