@@ -255,6 +255,39 @@ def load_peaks():
 
 
 # ------------------------------------------------------------------------------------ arms
+def decode_bench(eng, ids_host, ids_dev, ns, fwd_digests, stream, barrier, max_over_ranks):
+    """Incremental decoding of this shard: a prompt of T/2 tokens (eii_decoder_prefill), then one token
+    per sequence per step (eii_decoder_step_device) to T.  The first step is warm-up; the others are
+    timed with CUDA events (max over ranks).  Exactness: the prompt and step digests must add up to
+    the digests of the full forward pass timed above (equal logits rows give equal sums)."""
+    import torch
+    import _eii
+    T0 = T // 2
+    dec = _eii.Decoder(eng, ns, T)
+    try:
+        pre = dec.prefill(ids_host[:, :T0], logits=False, digests=True)["digests"]
+        ids_t = ids_dev[:, T0:].t().contiguous()  # [T - T0, ns]: the token of each step
+        step_logits = torch.empty((ns, VOCAB), dtype=torch.int32, device="cuda")
+        step_dig = torch.zeros((T - T0, ns), dtype=torch.int64, device="cuda")
+        dec.step_device(ids_t[0].data_ptr(), step_logits.data_ptr(), VOCAB, step_dig[0].data_ptr(), stream)
+        barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for t in range(1, T - T0):
+            dec.step_device(ids_t[t].data_ptr(), step_logits.data_ptr(), VOCAB, step_dig[t].data_ptr(), stream)
+        ev1.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(ev0.elapsed_time(ev1))
+        total = (torch.from_numpy(pre.view(np.int64).copy()).cuda() + step_dig.sum(dim=0)).cpu().numpy()
+        exact = bool(np.array_equal(total, fwd_digests.cpu().numpy()))
+    finally:
+        dec.close()
+    return {"unit": UNIT, "n_seq": N_SEQ, "prompt_tokens": T0, "timed_steps": T - T0 - 1, "ms": round(ms, 3),
+            "ms_per_step": round(ms / (T - T0 - 1), 3),
+            "path": "eii_decoder_prefill, then eii_decoder_step_device (K/V cache, one token per sequence per step)",
+            "exact_vs_forward_digests": exact}
+
+
 def run_ours(args):
     import torch
     import _eii
@@ -346,6 +379,7 @@ def run_ours(args):
     eng.profile_enable(False)
     launches_per_step = sum(v[1] for v in prof.values())
     chunk_rows = max(1, int(os.environ.get("EII_CHUNK_ROWS", "16384")) // T) * T
+    decode = decode_bench(eng, ids_host, ids_dev, ns, digests, stream, barrier, max_over_ranks)
     counts = torch.tensor([checked, exact, digest_match], dtype=torch.int64, device="cuda")
     all_dig = torch.from_numpy(dig_host.view(np.int64).copy()).cuda()
     if dist:
@@ -377,6 +411,7 @@ def run_ours(args):
                       "digests_device_eq_host_ranks": int(counts[2]),
                       "digest_of_digests": hashlib.sha256(all_dig.cpu().numpy().tobytes()).hexdigest()[:16]},
             "kernels": {k: {"ms": round(v[0], 3), "launches": v[1]} for k, v in prof.items()},
+            "decode": dict(decode, value=round(N_SEQ * decode["timed_steps"] / (decode["ms"] / 1e3), 1)),
         }
         if world == 1 and not args.no_cpu_baseline:
             with tempfile.TemporaryDirectory() as td:

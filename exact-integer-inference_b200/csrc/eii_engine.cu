@@ -485,7 +485,7 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
         dp.ctx_planes = e->ctx_planes; dp.P = L.Pc; dp.M = rows;
         dp.shift_s = L.shift_s; dp.shift_c = L.shift_c; dp.bits_c = L.c.bits;
         ProfScope ps(e, EII_K_ATTENTION, st);
-        CK(launch_k(k_attention_decode, dim3(nseq), dim3(N_HEADS * 32), 0, st, dp));
+        CK(launch_k(k_attention_decode, dim3(nseq * N_KV), dim3(DECODE_THREADS), 0, st, dp));
     }
     AttnParams ap{};
     ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;

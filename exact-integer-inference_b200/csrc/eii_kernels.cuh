@@ -297,8 +297,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attention(AttnParams ap) {
 // --------------------------------------------------------------------------- decode attention
 // One query row per sequence against a K/V cache (incremental decoding): row i = L - 1 of the causal
 // attention above, with keys 0 .. L-1 read from the cache [n_seq][max_T][192] (post-RoPE k, and v,
-// exactly as the prompt pass stored them).  Block = one sequence, warp w = head w (KV group w / 3);
-// lanes split the keys for the scores and the 64 dims (two each) for P.V.  Same integer operations
+// exactly as the prompt pass stored them).  Same integer operations
 // as k_attention, so the row equals the one a full recomputation produces.
 struct AttnDecodeParams {
     const int16_t* q;        // [n, 576] queries of this step
@@ -314,79 +313,146 @@ struct AttnDecodeParams {
 
 constexpr int DECODE_MAX_L = ROPE_POS;
 
-__global__ void __launch_bounds__(N_HEADS * 32) k_attention_decode(AttnDecodeParams ap) {
+// 4-way byte dot products with mixed signedness (PTX dp4a.atype.btype): u8 x u8, s8 x u8, u8 x s8.
+__device__ __forceinline__ int32_t dp4a_uu(uint32_t a, uint32_t b, int32_t c) {
+    uint32_t d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(static_cast<uint32_t>(c)));
+    return static_cast<int32_t>(d);
+}
+__device__ __forceinline__ int32_t dp4a_su(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int32_t dp4a_us(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+constexpr int DECODE_THREADS = 128;
+
+// Block = one (sequence, KV group): each key row k_j is read once and scored against the group's
+// three query heads; scores, then e, then P live in shared memory; P.V runs one thread per (head,
+// dim pair).
+__global__ void __launch_bounds__(DECODE_THREADS) k_attention_decode(AttnDecodeParams ap) {
     __shared__ int32_t E[DMAX + 1 + 3];
-    __shared__ int32_t Pw[N_HEADS][DECODE_MAX_L];
-    const int seq = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int hh = warp, g = hh / 3, L = ap.L;
+    __shared__ uint2 qb[3][16];  // per head, 4 dims per entry: (low bytes u8 x4, high bytes s8 x4)
+    __shared__ int32_t S[3][DECODE_MAX_L];
+    __shared__ int32_t red_max[3][DECODE_THREADS / 32];
+    __shared__ int64_t red_z[3][DECODE_THREADS / 32];
+    const int seq = blockIdx.x / N_KV, g = blockIdx.x % N_KV;
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32, L = ap.L;
     griddep_wait();
     griddep_launch();
-    for (int i = threadIdx.x; i <= DMAX; i += blockDim.x) E[i] = ap.exp_tab[i];
-    uint32_t qr[32];  // the query row of this head, 64 int16 as 32 pairs
-    {
-        const uint4* q4 = reinterpret_cast<const uint4*>(ap.q + static_cast<int64_t>(seq) * D_MODEL + hh * 64);
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            const uint4 t = __ldg(q4 + w);
-            qr[4 * w] = t.x; qr[4 * w + 1] = t.y; qr[4 * w + 2] = t.z; qr[4 * w + 3] = t.w;
-        }
+    for (int i = tid; i <= DMAX; i += DECODE_THREADS) E[i] = ap.exp_tab[i];
+    if (tid < 48) {
+        const uint2 w = __ldg(reinterpret_cast<const uint2*>(ap.q + static_cast<int64_t>(seq) * D_MODEL + (g * 3 + tid / 16) * 64) +
+                              tid % 16);
+        qb[tid / 16][tid % 16] = make_uint2(__byte_perm(w.x, w.y, 0x6420), __byte_perm(w.x, w.y, 0x7531));
     }
     __syncthreads();
     const int16_t* kb = ap.kc + static_cast<int64_t>(seq) * ap.max_T * 192 + g * 64;
     const int16_t* vb = ap.vc + static_cast<int64_t>(seq) * ap.max_T * 192 + g * 64;
-    int32_t* pw = Pw[warp];
-    // scores s_j = SAT16(RS(q . k_j, shift_s)), keys j = lane + 32 m
-    int32_t lmax = INT32_MIN;
-    for (int j = lane; j < L; j += 32) {
+    // scores s_hj = SAT16(RS(q_h . k_j, shift_s))
+    int32_t lmax[3] = {INT32_MIN, INT32_MIN, INT32_MIN};
+    for (int j = tid; j < L; j += DECODE_THREADS) {
         const uint4* k4 = reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(j) * 192);
-        int64_t acc = 0;
+        // q.k = 65536 D2 + 256 D1 + D0 over byte planes with 4-way byte dot products (each partial
+        // sum is below 64 * 255 * 255 < 2^31, as in the tensor-core attention)
+        int32_t d0[3] = {0, 0, 0}, d1[3] = {0, 0, 0}, d2[3] = {0, 0, 0};
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
             const uint4 t = __ldg(k4 + w);
-            acc += dot_pair(qr[4 * w], t.x) + dot_pair(qr[4 * w + 1], t.y) + dot_pair(qr[4 * w + 2], t.z) +
-                   dot_pair(qr[4 * w + 3], t.w);
+            const uint32_t k0a = __byte_perm(t.x, t.y, 0x6420), k1a = __byte_perm(t.x, t.y, 0x7531);
+            const uint32_t k0b = __byte_perm(t.z, t.w, 0x6420), k1b = __byte_perm(t.z, t.w, 0x7531);
+#pragma unroll
+            for (int h = 0; h < 3; ++h) {
+                const uint2 qa = qb[h][2 * w], qc = qb[h][2 * w + 1];
+                d0[h] = dp4a_uu(qa.x, k0a, d0[h]);
+                d0[h] = dp4a_uu(qc.x, k0b, d0[h]);
+                d1[h] = dp4a_su(qa.y, k0a, d1[h]);
+                d1[h] = dp4a_su(qc.y, k0b, d1[h]);
+                d1[h] = dp4a_us(qa.x, k1a, d1[h]);
+                d1[h] = dp4a_us(qc.x, k1b, d1[h]);
+                d2[h] = __dp4a(static_cast<int>(qa.y), static_cast<int>(k1a), d2[h]);
+                d2[h] = __dp4a(static_cast<int>(qc.y), static_cast<int>(k1b), d2[h]);
+            }
         }
-        const int32_t sj = static_cast<int32_t>(sat64(rs64(acc, ap.shift_s), 16));
-        pw[j] = sj;
-        lmax = max(lmax, sj);
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            const int64_t acc = static_cast<int64_t>(d2[h]) * 65536 + static_cast<int64_t>(d1[h]) * 256 + d0[h];
+            const int32_t sj = static_cast<int32_t>(sat64(rs64(acc, ap.shift_s), 16));
+            S[h][j] = sj;
+            lmax[h] = max(lmax[h], sj);
+        }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
-    __syncwarp();
-    // e_j = E[rowmax - s_j] (0 beyond DMAX), Z = sum e
-    int64_t lz = 0;
-    for (int j = lane; j < L; j += 32) {
-        const int32_t dd = lmax - pw[j];
-        const int32_t ej = dd <= DMAX ? E[dd] : 0;
-        pw[j] = ej;
-        lz += ej;
+    for (int h = 0; h < 3; ++h) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lmax[h] = max(lmax[h], __shfl_xor_sync(0xffffffffu, lmax[h], o));
+        if (lane == 0) red_max[h][warp] = lmax[h];
+    }
+    __syncthreads();
+    int32_t rmax[3];
+#pragma unroll
+    for (int h = 0; h < 3; ++h) {
+        rmax[h] = red_max[h][0];
+#pragma unroll
+        for (int w = 1; w < DECODE_THREADS / 32; ++w) rmax[h] = max(rmax[h], red_max[h][w]);
+    }
+    // e_hj = E[rowmax_h - s_hj] (0 beyond DMAX), Z_h = sum_j e_hj
+    int64_t lz[3] = {0, 0, 0};
+    for (int j = tid; j < L; j += DECODE_THREADS) {
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            const int32_t dd = rmax[h] - S[h][j];
+            const int32_t ej = dd <= DMAX ? E[dd] : 0;
+            S[h][j] = ej;
+            lz[h] += ej;
+        }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lz += __shfl_xor_sync(0xffffffffu, lz, o);
-    // P_j = floor((e_j 65536 + floor(Z/2)) / Z), exact (double estimate, integer remainder fix-up)
-    const int64_t Z = lz, half = Z / 2;
-    const double rz = 1.0 / static_cast<double>(Z);
-    for (int j = lane; j < L; j += 32) {
-        const int64_t n = static_cast<int64_t>(pw[j]) * 65536 + half;
-        int64_t p = static_cast<int64_t>(static_cast<double>(n) * rz);
-        int64_t r = n - p * Z;
-        if (r < 0) { --p; r += Z; }
-        if (r < 0) { --p; r += Z; }
-        if (r >= Z) { ++p; r -= Z; }
-        if (r >= Z) { ++p; }
-        pw[j] = static_cast<int32_t>(p);
+    for (int h = 0; h < 3; ++h) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lz[h] += __shfl_xor_sync(0xffffffffu, lz[h], o);
+        if (lane == 0) red_z[h][warp] = lz[h];
     }
-    __syncwarp();
-    // ctx_d = SAT(RS(sum_j P_j v_jd, shift_c), bits_c), dims 2 lane and 2 lane + 1
+    __syncthreads();
+    // P_hj = floor((e_hj 65536 + floor(Z_h/2)) / Z_h), exact (double estimate, integer remainder fix-up)
+#pragma unroll
+    for (int h = 0; h < 3; ++h) {
+        int64_t Z = 0;
+#pragma unroll
+        for (int w = 0; w < DECODE_THREADS / 32; ++w) Z += red_z[h][w];
+        const int64_t half = Z / 2;
+        const double rz = 1.0 / static_cast<double>(Z);
+        for (int j = tid; j < L; j += DECODE_THREADS) {
+            const int64_t n = static_cast<int64_t>(S[h][j]) * 65536 + half;
+            int64_t p = static_cast<int64_t>(static_cast<double>(n) * rz);
+            int64_t r = n - p * Z;
+            if (r < 0) { --p; r += Z; }
+            if (r < 0) { --p; r += Z; }
+            if (r >= Z) { ++p; r -= Z; }
+            if (r >= Z) { ++p; }
+            S[h][j] = static_cast<int32_t>(p);
+        }
+    }
+    __syncthreads();
+    // ctx_hd = SAT(RS(sum_j P_hj v_jd, shift_c), bits_c): thread (head tid / 32, dims 2 lane, 2 lane + 1)
+    if (tid >= 96) return;
+    const int h = tid / 32;
     int64_t a0 = 0, a1 = 0;
-    for (int j = 0; j < L; ++j) {
-        const int64_t p = pw[j];
-        const uint32_t vv = __ldg(reinterpret_cast<const uint32_t*>(vb + static_cast<int64_t>(j) * 192) + lane);
+    const uint32_t* vl = reinterpret_cast<const uint32_t*>(vb) + lane;
+    const int32_t* ph = S[h];
+#pragma unroll 8
+    for (int j = 0; j < L; ++j) {  // 8 keys' loads in flight per lane
+        const int64_t p = ph[j];
+        const uint32_t vv = __ldg(vl + static_cast<int64_t>(j) * 96);
         a0 += p * static_cast<int16_t>(vv & 0xFFFF);
         a1 += p * static_cast<int16_t>(vv >> 16);
     }
     const int64_t c0 = sat64(rs64(a0, ap.shift_c), ap.bits_c), c1 = sat64(rs64(a1, ap.shift_c), ap.bits_c);
-    const int col = hh * 64 + 2 * lane;
+    const int col = (g * 3 + h) * 64 + 2 * lane;
     const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
     for (int p = 0; p < ap.P; ++p) {
         const uint16_t pair = static_cast<uint16_t>(plane_byte(c0, p)) | (static_cast<uint16_t>(plane_byte(c1, p)) << 8);
