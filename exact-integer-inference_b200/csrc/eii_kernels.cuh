@@ -337,7 +337,7 @@ constexpr int DECODE_THREADS = 128;
 __global__ void __launch_bounds__(DECODE_THREADS) k_attention_decode(AttnDecodeParams ap) {
     __shared__ int32_t E[DMAX + 1 + 3];
     __shared__ uint2 qb[3][16];  // per head, 4 dims per entry: (low bytes u8 x4, high bytes s8 x4)
-    __shared__ int32_t S[3][DECODE_MAX_L];
+    __shared__ __align__(16) int32_t S[3][DECODE_MAX_L];  // also the P.V partial sums (6 KB) at the end
     __shared__ int32_t red_max[3][DECODE_THREADS / 32];
     __shared__ int64_t red_z[3][DECODE_THREADS / 32];
     const int seq = blockIdx.x / N_KV, g = blockIdx.x % N_KV;
@@ -438,20 +438,40 @@ __global__ void __launch_bounds__(DECODE_THREADS) k_attention_decode(AttnDecodeP
         }
     }
     __syncthreads();
-    // ctx_hd = SAT(RS(sum_j P_hj v_jd, shift_c), bits_c): thread (head tid / 32, dims 2 lane, 2 lane + 1)
+    // ctx_hd = SAT(RS(sum_j P_hj v_jd, shift_c), bits_c): thread (key quarter tid / 32, dims 2 lane,
+    // 2 lane + 1) sums keys j = quarter (mod 4) for the three heads; the quarters add up in shared memory.
+    const int kq = tid / 32;
+    int64_t a0[3] = {0, 0, 0}, a1[3] = {0, 0, 0};
+    const uint32_t* vl = reinterpret_cast<const uint32_t*>(vb) + lane;
+#pragma unroll 4
+    for (int j = kq; j < L; j += 4) {
+        const uint32_t vv = __ldg(vl + static_cast<int64_t>(j) * 96);
+        const int32_t v0 = static_cast<int16_t>(vv & 0xFFFF), v1 = static_cast<int16_t>(vv >> 16);
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            const int64_t p = S[h][j];
+            a0[h] += p * v0;
+            a1[h] += p * v1;
+        }
+    }
+    __syncthreads();  // S is no longer read: reuse it for the partial sums
+    int64_t* part = reinterpret_cast<int64_t*>(&S[0][0]);  // [4 quarters][3 heads][32 lanes][2]
+#pragma unroll
+    for (int h = 0; h < 3; ++h) {
+        part[((kq * 3 + h) * 32 + lane) * 2] = a0[h];
+        part[((kq * 3 + h) * 32 + lane) * 2 + 1] = a1[h];
+    }
+    __syncthreads();
     if (tid >= 96) return;
     const int h = tid / 32;
-    int64_t a0 = 0, a1 = 0;
-    const uint32_t* vl = reinterpret_cast<const uint32_t*>(vb) + lane;
-    const int32_t* ph = S[h];
-#pragma unroll 8
-    for (int j = 0; j < L; ++j) {  // 8 keys' loads in flight per lane
-        const int64_t p = ph[j];
-        const uint32_t vv = __ldg(vl + static_cast<int64_t>(j) * 96);
-        a0 += p * static_cast<int16_t>(vv & 0xFFFF);
-        a1 += p * static_cast<int16_t>(vv >> 16);
+    int64_t c0 = 0, c1 = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        c0 += part[((q * 3 + h) * 32 + lane) * 2];
+        c1 += part[((q * 3 + h) * 32 + lane) * 2 + 1];
     }
-    const int64_t c0 = sat64(rs64(a0, ap.shift_c), ap.bits_c), c1 = sat64(rs64(a1, ap.shift_c), ap.bits_c);
+    c0 = sat64(rs64(c0, ap.shift_c), ap.bits_c);
+    c1 = sat64(rs64(c1, ap.shift_c), ap.bits_c);
     const int col = (g * 3 + h) * 64 + 2 * lane;
     const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
     for (int p = 0; p < ap.P; ++p) {
