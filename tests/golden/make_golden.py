@@ -17,9 +17,11 @@ What it does, for the seeded synthetic model of oracle/synth.py:
   4. runs intref.Model.forward on the 64-sequence check subset of the 4096-sequence batch
      (T=128) and records per-sequence sha256 digests of the int32 logits and last residual;
   5. runs intref.Model.linear / matmul_exact + rs on seeded activations spanning the full
-     INT16 / INT32 ranges for the four contraction shapes and records digests of acc and out.
+     INT16 / INT32 ranges for the four contraction shapes and records digests of acc and out;
+  6. runs intref.Model.block(l, x, trace) on the t24 tokens for the layers in TRACE_LAYERS and
+     records the sha256 of every trace site (int64, C order) and the site exponents (trace_t24.json).
 
-    python tests/golden/make_golden.py [--keep DIR] [--skip-subset]
+    python tests/golden/make_golden.py [--keep DIR] [--skip-subset] [--only-trace]
 """
 import argparse
 import hashlib
@@ -42,6 +44,7 @@ REF = os.environ.get("EII_REFERENCE", "/root/reference")
 SETS = (("t24", 64, 24, False), ("t128", 64, 128, False), ("t160", 100, 160, True))
 SUBSET_SEED = 2
 SUBSET_N = 64
+TRACE_LAYERS = (0, 4, 11, 13, 28)
 
 
 def sha256_bytes(b):
@@ -99,12 +102,41 @@ def gemm_activations(bits, M, K, seed):
     return a
 
 
+def trace_golden(torch, common, intref):
+    """Digests of the reference's per-site block trace (python/intref.py:192-286) on the t24 tokens."""
+    patch(torch, common, intref, False)
+    M_ = intref.Model(wide=True)
+    ids = synth.window_ids(64, 24)
+    x = M_.embed(ids)
+    layers = {}
+    for l in range(max(TRACE_LAYERS) + 1):
+        if l in TRACE_LAYERS:
+            tr = {}
+            x_next = M_.block(l, x, trace=tr)
+            layers[str(l)] = {"f": {k: int(v) for k, v in tr["_f"].items()},
+                              "sites": {k: {"shape": list(np.shape(v)),
+                                            "sha256": sha256_bytes(np.ascontiguousarray(v, dtype=np.int64).tobytes())}
+                                        for k, v in tr.items() if k != "_f"}}
+            x = x_next
+        else:
+            x = M_.block(l, x)
+        print("trace layer", l, "done", flush=True)
+    with open(os.path.join(HERE, "trace_t24.json"), "w") as f:
+        json.dump({"window": 64, "tokens": 24, "model": "base", "note": "sha256 of int64 C-order arrays of "
+                   "Model.block(l, x, trace) sites; x is the reference's own residual entering layer l",
+                   "layers": layers}, f, indent=1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--keep", default=None, help="directory to keep the exported vector sets in")
     ap.add_argument("--skip-subset", action="store_true")
+    ap.add_argument("--only-trace", action="store_true")
     args = ap.parse_args()
     torch, common, intref = import_reference()
+    if args.only_trace:
+        trace_golden(torch, common, intref)
+        return
     out_root = args.keep or tempfile.mkdtemp(prefix="eii_golden_")
     refbin = os.path.join(REPO, "oracle", "_ref", "intref")
     if not os.path.exists(refbin):
@@ -191,6 +223,7 @@ def main():
             json.dump({"T": T, "subset_seed": SUBSET_SEED, "rows": rows, "sequences": seqs,
                        "seconds": round(time.time() - t0, 1)}, f, indent=1)
         print("subset done", round(time.time() - t0, 1), "s")
+    trace_golden(torch, common, intref)
     print("vector sets in", out_root)
 
 

@@ -122,3 +122,37 @@ def test_silu_tables_obey_the_odd_part_identity(base_model):
         assert np.array_equal(pred, tab[32768 + g])
         checked += 1
     assert checked == 30
+
+
+def trace_inputs(mdl):
+    """The t24 residual entering each layer of the trace fixture (oracle forward, itself pinned)."""
+    g = golden("trace_t24.json")
+    ids = synth.window_ids(g["window"], g["tokens"])
+    x = ofw.embed(mdl, ids)
+    out = {}
+    for l in range(max(int(k) for k in g["layers"]) + 1):
+        if str(l) in g["layers"]:
+            out[l] = x.copy()
+        x = ofw.block_batch(mdl, l, x, g["tokens"])
+    return g, out
+
+
+def check_trace(tr, want):
+    """Every site of a block trace against the reference's digests (and the exponents)."""
+    assert {k: int(v) for k, v in tr["_f"].items()} == want["f"]
+    bad = []
+    for k, s in want["sites"].items():
+        a = np.ascontiguousarray(tr[k], dtype=np.int64)
+        if list(a.shape) != s["shape"] or sha256_arr(a, np.int64) != s["sha256"]:
+            bad.append(k)
+    assert not bad, bad
+    assert set(tr) - {"_f"} == set(want["sites"])
+
+
+def test_oracle_block_trace_matches_reference(base_model):
+    """Per-site trace of Model.block (python/intref.py:192-286) on the t24 tokens at five layers."""
+    g, xs = trace_inputs(base_model)
+    for l, x in xs.items():
+        tr = {}
+        ofw.block_batch(base_model, l, x, g["tokens"], trace=tr)
+        check_trace(tr, g["layers"][str(l)])
