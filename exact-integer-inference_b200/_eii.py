@@ -46,6 +46,7 @@ _SIGS = {
                          ctypes.c_int),
     "eii_linear": ([_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
                     ctypes.c_int, ctypes.c_int, _P, _P], ctypes.c_int),
+    "eii_block_trace": ([_P, ctypes.c_int, _P, ctypes.c_int, _P], ctypes.c_int),
     "eii_decoder_open": ([_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)], ctypes.c_int),
     "eii_decoder_prefill": ([_P, _P, ctypes.c_int, _P, _P], ctypes.c_int),
     "eii_decoder_step": ([_P, _P, _P, _P], ctypes.c_int),
@@ -54,6 +55,24 @@ _SIGS = {
     "eii_decoder_reset": ([_P], ctypes.c_int),
     "eii_decoder_close": ([_P], None),
 }
+
+
+# eii_trace (include/eii.h): the sites of Model.block(trace) (python/intref.py:192-286), in struct order
+TRACE_SITES = ("resid_in", "norm1_U", "norm1_z", "norm1_out", "q_proj", "k_proj", "v_proj", "q_rope", "k_rope",
+               "attn_score", "attn_prob", "attn_ctx", "o_res", "resid_mid", "norm2_U", "norm2_z", "norm2_out",
+               "gate_proj", "up_proj", "silu_gate", "mlp_gated", "down_res", "resid_out")
+
+
+class _Trace(ctypes.Structure):
+    _fields_ = [(k, _P) for k in TRACE_SITES]
+
+
+def trace_shapes(T):
+    D, K, F, H = D_MODEL, 192, 1536, 9
+    sh = {k: (T, D) for k in TRACE_SITES}
+    sh.update(norm1_U=(T,), norm2_U=(T,), k_proj=(T, K), v_proj=(T, K), k_rope=(T, K), attn_score=(H, T, T),
+              attn_prob=(H, T, T), gate_proj=(T, F), up_proj=(T, F), silu_gate=(T, F), mlp_gated=(T, F))
+    return sh
 
 
 def lib():
@@ -156,6 +175,15 @@ class Engine:
         out = np.empty_like(x)
         check(lib().eii_block(self.h, layer, ptr(x), rows // T, T, ptr(out)))
         return out
+
+    def block_trace(self, layer, x):
+        """Model.block(l, x, trace) of one sequence x [T, 576] -> (new residual, {site: int64 array})."""
+        x = _c(x, np.int64)
+        T = x.shape[0]
+        out = {k: np.empty(s, np.int64) for k, s in trace_shapes(T).items()}
+        tr = _Trace(*[ctypes.c_void_p(out[k].ctypes.data) for k in TRACE_SITES])
+        check(lib().eii_block_trace(self.h, int(layer), ptr(x), T, ctypes.byref(tr)))
+        return out["resid_out"].copy(), out
 
     def rmsnorm(self, x, gain_q, gain_f, f_out, bits_out):
         x = _c(x, np.int64)

@@ -430,11 +430,12 @@ int launch_gemm_p(eii_engine* e, int P, const CUtensorMap& A, const CUtensorMap&
 }
 
 int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, int shift, int bits,
-                uint8_t* planes, int P, int64_t* out64, cudaStream_t st) {
+                uint8_t* planes, int P, int64_t* out64, cudaStream_t st, int64_t* u_out = nullptr,
+                int64_t* z_out = nullptr) {
     const int rows_per_block = 16;  // 8 warps, two rows each
     ProfScope ps(e, EII_K_NORM, st);
     CK(launch_k(k_rmsnorm, dim3((rows + rows_per_block - 1) / rows_per_block), dim3(256), 0, st, x, rows, gain, shift,
-                bits, planes, P, out64));
+                bits, planes, P, out64, u_out, z_out));
     return EII_OK;
 }
 
@@ -457,13 +458,41 @@ struct KvHook {
     int pos;
 };
 
-int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHook* kv = nullptr) {
+// Per-site trace hook of run_layer (python/intref.py:192-286 with trace): device buffers for the
+// sites the fused kernels never materialise.  The norms run a second time in their generic form
+// (U, z, int64 output), the projections and residual terms run as EPI_LINEAR GEMMs on the same
+// operands (int64 output), and the attention runs on CUDA cores with score/probability outputs.
+struct TraceHook {
+    int64_t *u1, *z1, *n1, *q, *k, *v, *ores, *u2, *z2, *n2, *gu, *dres;
+    int32_t *score, *prob, *xmid;
+};
+
+int trace_linear(eii_engine* e, int P, const CUtensorMap& A, bool a_blocked, const int8_t* W, int K, int N,
+                 const int2* msh, int bits_out, int64_t* out, int rows, cudaStream_t st) {
+    CUtensorMap tmB;
+    TRY(map_2d(&tmB, W, K, N, P == 4 ? BN_P4 : 128));
+    EpiParams ep{};
+    ep.M = rows; ep.N = N; ep.K = K; ep.msh = msh; ep.err = e->err_dev; ep.out64 = out; ep.bits_out = bits_out;
+    ep.a_blocked = a_blocked ? 1 : 0;
+    return launch_gemm_p<EPI_LINEAR>(e, P, A, tmB, ep, st, EII_K_GEMM_LINEAR);
+}
+
+int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHook* kv = nullptr,
+              const TraceHook* trh = nullptr) {
     LayerDev& L = e->L[l];
     const ActMaps* am;
     TRY(act_maps(e, rows, &am));
     const int nseq = rows / T;
     const bool decode = kv && kv->pos >= 0;
     TRY(launch_norm(e, e->x, rows, L.ln1, L.norm1_shift, L.h.bits, e->h_planes, 2, nullptr, st));
+    if (trh) {
+        TRY(launch_norm(e, e->x, rows, L.ln1, L.norm1_shift, L.h.bits, nullptr, 0, trh->n1, st, trh->u1, trh->z1));
+        TRY(trace_linear(e, 2, am->h, false, L.w_qkv, D_MODEL, 576, L.msh_qkv, L.q.bits, trh->q, rows, st));
+        TRY(trace_linear(e, 2, am->h, false, L.w_qkv + 576 * D_MODEL, D_MODEL, 192, L.msh_qkv + 576, L.k.bits, trh->k,
+                         rows, st));
+        TRY(trace_linear(e, 2, am->h, false, L.w_qkv + 768 * D_MODEL, D_MODEL, 192, L.msh_qkv + 768, L.v.bits, trh->v,
+                         rows, st));
+    }
 
     EpiParams ep{};
     ep.M = rows; ep.N = 960; ep.K = D_MODEL; ep.msh = L.msh_qkv; ep.err = e->err_dev;
@@ -490,21 +519,34 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     AttnParams ap{};
     ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;
     ap.M = rows; ap.T = T; ap.shift_s = L.shift_s; ap.shift_c = L.shift_c; ap.bits_c = L.c.bits;
+    if (trh) {
+        ap.score_out = trh->score;
+        ap.prob_out = trh->prob;
+    }
     if (!decode) {
         ProfScope ps(e, EII_K_ATTENTION, st);
-        if (T <= 128 && !e->force_cuda_core_attention)
+        if (T <= 128 && !e->force_cuda_core_attention && !trh)
             CK(launch_k(k_attention_tc, dim3(nseq * N_KV), dim3(ATTN_TC_THREADS), ATTN_TC_SMEM, st, ap, e->err_dev));
         else
             CK(launch_k(k_attention, dim3(nseq * N_KV), dim3(ATTN_WARPS * 32), attn_smem_bytes(T), st, ap));
     }
 
+    if (trh)
+        TRY(trace_linear(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, true, L.w_o, D_MODEL, D_MODEL, L.msh_o, 64, trh->ores,
+                         rows, st));
     ep = EpiParams{};
     ep.M = rows; ep.N = D_MODEL; ep.K = D_MODEL; ep.msh = L.msh_o; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_o;
     ep.a_blocked = 1;
     TRY(launch_gemm_p<EPI_RESID>(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, L.Pc == 2 ? L.tm_o : L.tm_o64, ep, st,
                                  EII_K_GEMM_O, &am->x32, &am->x16));
+    if (trh) CK(cudaMemcpyAsync(trh->xmid, e->x, sizeof(int32_t) * rows * D_MODEL, cudaMemcpyDeviceToDevice, st));
 
     TRY(launch_norm(e, e->x, rows, L.ln2, L.norm2_shift, L.h2.bits, e->h_planes, 2, nullptr, st));
+    if (trh) {
+        TRY(launch_norm(e, e->x, rows, L.ln2, L.norm2_shift, L.h2.bits, nullptr, 0, trh->n2, st, trh->u2, trh->z2));
+        // gate and up columns interleaved per 128-column tile, as W_gu is stored
+        TRY(trace_linear(e, 2, am->h, false, L.w_gu, D_MODEL, 2 * D_FF, L.msh_gu, L.g.bits, trh->gu, rows, st));
+    }
 
     ep = EpiParams{};
     ep.M = rows; ep.N = 2 * D_FF; ep.K = D_MODEL; ep.msh = L.msh_gu; ep.err = e->err_dev;
@@ -514,6 +556,9 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     ep.fast = L.fast_gu; ep.narrow = L.narrow_gu;
     ep.bits_m = L.m.bits; ep.gated_P = L.Pm; ep.gated_planes = e->gated_planes;
     TRY(launch_gemm<2, EPI_GATEUP>(e, am->h, L.tm_gu, ep, st, EII_K_GEMM_GATEUP));
+    if (trh)
+        TRY(trace_linear(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, true, L.w_d, D_FF, D_MODEL, L.msh_d, 64, trh->dres,
+                         rows, st));
 
     ep = EpiParams{};
     ep.M = rows; ep.N = D_MODEL; ep.K = D_FF; ep.msh = L.msh_d; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_d;
@@ -1176,6 +1221,89 @@ int eii_block(eii_engine* e, int layer, const int64_t* x_in, int n_seq, int T, i
     CK(cudaMemcpyAsync(h.data(), e->x, h.size() * 4, cudaMemcpyDeviceToHost, e->stream));
     TRY(check_device_error(e, e->stream));
     for (size_t i = 0; i < h.size(); ++i) x_out[i] = h[i];
+    return EII_OK;
+}
+
+int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_trace* tr) {
+    TRY(check_forward_args(e, 1, T));
+    if (layer < 0 || layer >= N_LAYERS) return fail(EII_ERR_ARG, "layer %d out of range", layer);
+    if (!x_in || !tr) return fail(EII_ERR_ARG, "null buffer");
+    LayerDev& L = e->L[layer];
+    if (L.g.bits != L.u.bits) return fail(EII_ERR_FORMAT, "trace: gate and up formats differ at layer %d", layer);
+    CK(cudaSetDevice(e->device));
+    cudaStream_t st = e->stream;
+    const int rows = T;
+    const size_t RD = (size_t)rows * D_MODEL, RK = (size_t)rows * 192, RF = (size_t)rows * D_FF;
+    TRY(ensure_rows(e, rows));
+    TRY(upload_x(e, x_in, rows));
+    std::vector<void*> tmp;
+    TraceHook h{};
+    int rc = EII_OK;
+    auto A64 = [&](int64_t** p, size_t n) { if (rc == EII_OK) rc = dalloc(tmp, p, n); };
+    auto A32 = [&](int32_t** p, size_t n) { if (rc == EII_OK) rc = dalloc(tmp, p, n); };
+    A64(&h.u1, rows); A64(&h.z1, RD); A64(&h.n1, RD); A64(&h.q, RD); A64(&h.k, RK); A64(&h.v, RK); A64(&h.ores, RD);
+    A64(&h.u2, rows); A64(&h.z2, RD); A64(&h.n2, RD); A64(&h.gu, 2 * RF); A64(&h.dres, RD);
+    A32(&h.score, (size_t)N_HEADS * T * T); A32(&h.prob, (size_t)N_HEADS * T * T); A32(&h.xmid, RD);
+    if (rc == EII_OK && (cudaMemsetAsync(h.score, 0, sizeof(int32_t) * N_HEADS * T * T, st) != cudaSuccess ||
+                         cudaMemsetAsync(h.prob, 0, sizeof(int32_t) * N_HEADS * T * T, st) != cudaSuccess))
+        rc = fail(EII_ERR_CUDA, "trace buffers");
+    if (rc == EII_OK) rc = run_layer(e, layer, rows, T, st, nullptr, &h);
+    // downloads
+    std::vector<int64_t> u1(rows), z1(RD), n1(RD), q(RD), k(RK), v(RK), ores(RD), u2(rows), z2(RD), n2(RD), gu(2 * RF),
+        dres(RD);
+    std::vector<int32_t> score((size_t)N_HEADS * T * T), prob((size_t)N_HEADS * T * T), xmid(RD), xout(RD);
+    std::vector<int16_t> qr(RD), kr(RK);
+    std::vector<int32_t> silu(65536);
+    const int64_t cstride = blocked_plane_stride(rows, D_MODEL), gstride = blocked_plane_stride(rows, D_FF);
+    std::vector<uint8_t> ctxp((size_t)L.Pc * cstride), gatedp((size_t)L.Pm * gstride);
+    struct Dl { void* dst; const void* src; size_t bytes; };
+    const Dl dls[] = {{u1.data(), h.u1, rows * 8ull}, {z1.data(), h.z1, RD * 8}, {n1.data(), h.n1, RD * 8},
+                      {q.data(), h.q, RD * 8}, {k.data(), h.k, RK * 8}, {v.data(), h.v, RK * 8},
+                      {ores.data(), h.ores, RD * 8}, {u2.data(), h.u2, rows * 8ull}, {z2.data(), h.z2, RD * 8},
+                      {n2.data(), h.n2, RD * 8}, {gu.data(), h.gu, 2 * RF * 8}, {dres.data(), h.dres, RD * 8},
+                      {score.data(), h.score, score.size() * 4}, {prob.data(), h.prob, prob.size() * 4},
+                      {xmid.data(), h.xmid, RD * 4}, {xout.data(), e->x, RD * 4}, {qr.data(), e->q, RD * 2},
+                      {kr.data(), e->k, RK * 2}, {silu.data(), L.silu, 65536 * 4},
+                      {ctxp.data(), e->ctx_planes, ctxp.size()}, {gatedp.data(), e->gated_planes, gatedp.size()}};
+    for (const Dl& d : dls)
+        if (rc == EII_OK && cudaMemcpyAsync(d.dst, d.src, d.bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            rc = fail(EII_ERR_CUDA, "trace download failed");
+    if (rc == EII_OK) rc = check_device_error(e, st);
+    free_list(tmp);
+    if (rc != EII_OK) return rc;
+    // planes -> values (row-blocked layout; low planes unsigned, top plane signed)
+    auto unblock = [&](const std::vector<uint8_t>& buf, int P, int K, int64_t stride, int64_t* out) {
+        for (int r = 0; r < rows; ++r)
+            for (int c = 0; c < K; ++c) {
+                const int64_t off = blocked_off(r, c, K);
+                int64_t val = 0;
+                for (int p = 0; p < P; ++p) {
+                    const uint8_t b = buf[p * stride + off];
+                    val += (p == P - 1 ? (int64_t)(int8_t)b : (int64_t)b) * ((int64_t)1 << (8 * p));
+                }
+                out[(size_t)r * K + c] = val;
+            }
+    };
+    auto put = [](int64_t* dst, const auto& src) {
+        if (dst) for (size_t i = 0; i < src.size(); ++i) dst[i] = (int64_t)src[i];
+    };
+    if (tr->resid_in) memcpy(tr->resid_in, x_in, RD * 8);
+    put(tr->norm1_U, u1); put(tr->norm1_z, z1); put(tr->norm1_out, n1);
+    put(tr->q_proj, q); put(tr->k_proj, k); put(tr->v_proj, v); put(tr->q_rope, qr); put(tr->k_rope, kr);
+    put(tr->attn_score, score); put(tr->attn_prob, prob);
+    if (tr->attn_ctx) unblock(ctxp, L.Pc, D_MODEL, cstride, tr->attn_ctx);
+    put(tr->o_res, ores); put(tr->resid_mid, xmid);
+    put(tr->norm2_U, u2); put(tr->norm2_z, z2); put(tr->norm2_out, n2);
+    for (int r = 0; r < rows; ++r)
+        for (int j = 0; j < D_FF; ++j) {  // W_gu tile t = j / 64 holds gate j at column 128 t + j % 64, up j at + 64
+            const size_t cg = (size_t)r * 2 * D_FF + 128 * (j / 64) + j % 64;
+            const int64_t g = gu[cg], u = gu[cg + 64];
+            if (tr->gate_proj) tr->gate_proj[(size_t)r * D_FF + j] = g;
+            if (tr->up_proj) tr->up_proj[(size_t)r * D_FF + j] = u;
+            if (tr->silu_gate) tr->silu_gate[(size_t)r * D_FF + j] = silu[(size_t)(g + 32768)];
+        }
+    if (tr->mlp_gated) unblock(gatedp, L.Pm, D_FF, gstride, tr->mlp_gated);
+    put(tr->down_res, dres); put(tr->resid_out, xout);
     return EII_OK;
 }
 

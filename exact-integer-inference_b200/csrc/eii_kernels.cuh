@@ -92,7 +92,8 @@ __device__ __forceinline__ int64_t half_sum64(int64_t v) {
 }
 
 __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain, int shift_out,
-                          int bits_out, uint8_t* __restrict__ planes, int P, int64_t* __restrict__ out64) {
+                          int bits_out, uint8_t* __restrict__ planes, int P, int64_t* __restrict__ out64,
+                          int64_t* __restrict__ u_out, int64_t* __restrict__ z_out) {
     const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
     const int l = threadIdx.x & 15;
     const bool live = row < M;
@@ -122,7 +123,9 @@ __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* _
     // Fast path (planes output, bits_out 16, 1 <= shift_out <= 31): z = RS(x U, 16) fits int32
     // (|x U| <= 2^40, python/intref.py:178), 3 g fits int32, and RS(z 3 g, shift_out) is a funnel
     // shift of one 32x32 -> 64 multiply-add.
-    const bool fast = planes && !out64 && P == 2 && bits_out == 16 && shift_out >= 1 && shift_out <= 31;
+    // the per-row U and z of python/intref.py:183 for a trace (generic path only)
+    if (u_out && l == 0) u_out[row] = U;
+    const bool fast = planes && !out64 && !z_out && P == 2 && bits_out == 16 && shift_out >= 1 && shift_out <= 31;
     const int64_t rnd_out = (shift_out >= 1 && shift_out <= 62) ? (int64_t(1) << (shift_out - 1)) : 0;
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
@@ -155,6 +158,7 @@ __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* _
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int64_t z = rs64(static_cast<int64_t>(e[u]) * U, 16);
+            if (z_out) z_out[static_cast<int64_t>(row) * D_MODEL + c + u] = z;
             o[u] = sat64(rs64(z * g[u] * 3, shift_out), bits_out);
         }
         if (planes) {
@@ -200,6 +204,10 @@ struct AttnParams {
     int P;
     int M, T;
     int shift_s, shift_c, bits_c;
+    // optional trace outputs of k_attention (python/intref.py:249-250): [M/T][9][T][T] scores (s for
+    // j <= i) and probabilities P; entries above the diagonal are left to the caller (zeroed)
+    int32_t* score_out;
+    int32_t* prob_out;
 };
 
 constexpr int ATTN_WARPS = 8;
@@ -251,6 +259,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attention(AttnParams ap) {
             const int32_t s = static_cast<int32_t>(sat64(rs64(acc, ap.shift_s), 16));
             sc[j] = s;
             lmax = max(lmax, s);
+            if (ap.score_out) ap.score_out[((static_cast<int64_t>(seq) * N_HEADS + hh) * T + i) * T + j] = s;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
@@ -273,6 +282,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attention(AttnParams ap) {
             if (r >= Z) { ++p; r -= Z; }
             if (r >= Z) { ++p; }
             sc[j] = static_cast<int32_t>(p);
+            if (ap.prob_out) ap.prob_out[((static_cast<int64_t>(seq) * N_HEADS + hh) * T + i) * T + j] = static_cast<int32_t>(p);
         }
         __syncwarp();
         int64_t a0 = 0, a1 = 0;

@@ -174,10 +174,19 @@ class Model:
         return out, acc
 
     def block(self, l, x, trace=None):
-        if trace is not None:
-            raise NotImplementedError("per-site trace is not implemented by the B200 engine yet")
+        """Model.block (python/intref.py:192-286); with a trace dict, every site and the "_f" exponents."""
         x = np.asarray(x, dtype=I64)
-        return self._eng.block(l, x, T=x.shape[0])
+        if trace is None:
+            return self._eng.block(l, x, T=x.shape[0])
+        out, sites = self._eng.block_trace(l, x)
+        trace.update(sites)
+        f = {k: self.fmt(k, l)[1] for k in ("norm1_out", "q_proj", "k_proj", "v_proj", "q_rope", "k_rope", "attn_ctx",
+                                             "norm2_out", "gate_proj", "up_proj", "silu_gate")}
+        bits_m, f_m0 = self.fmt("mlp_gated", l)
+        f["mlp_gated"] = min(f_m0, f["silu_gate"] + f["up_proj"]) if bits_m == 32 else f_m0  # python/intref.py:274
+        trace["_f"] = {"resid_in": F_RES, "o_res": F_RES, "resid_mid": F_RES, "down_res": F_RES, "resid_out": F_RES,
+                       "attn_score": F_SCORE, "attn_prob": 16, **f}
+        return out
 
     def forward(self, ids, narrow_residual=False):
         if narrow_residual:

@@ -100,6 +100,19 @@ int eii_embed(eii_engine* e, const int64_t* ids, int n, int64_t* x_out);
  * x_in, x_out [n_seq*T][576] (may alias). */
 int eii_block(eii_engine* e, int layer, const int64_t* x_in, int n_seq, int T, int64_t* x_out);
 
+/* Model.block(l, x, trace) (python/intref.py:192-286): layer `layer` on one sequence of T rows
+ * (x_in [T][576]) with every per-site value of the reference's trace, as int64 (any pointer may be
+ * null).  Shapes: norm*_U [T]; attn_score, attn_prob [9][T][T] (zero above the diagonal, as the
+ * reference stores them); k_proj, v_proj, k_rope [T][192]; gate_proj, up_proj, silu_gate,
+ * mlp_gated [T][1536]; the rest [T][576].  The exponents of the sites are the layer's formats
+ * (python/intref.py:285-286). */
+typedef struct eii_trace {
+    int64_t *resid_in, *norm1_U, *norm1_z, *norm1_out, *q_proj, *k_proj, *v_proj, *q_rope, *k_rope;
+    int64_t *attn_score, *attn_prob, *attn_ctx, *o_res, *resid_mid, *norm2_U, *norm2_z, *norm2_out;
+    int64_t *gate_proj, *up_proj, *silu_gate, *mlp_gated, *down_res, *resid_out;
+} eii_trace;
+int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_trace* trace);
+
 /* Model.rmsnorm (python/intref.py:168-184) with an explicit gain (q int16-valued [576], f):
  * x [rows][576] int32-valued -> out [rows][576]; bits_out 16 or 32. */
 int eii_rmsnorm(eii_engine* e, const int64_t* x, int rows, const int64_t* gain_q, int gain_f, int f_out,

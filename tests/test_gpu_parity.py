@@ -313,3 +313,18 @@ def test_decoder_arguments(eng):
         assert dec.position == 0
     finally:
         dec.close()
+
+
+# ------------------------------------------------------------------------------ per-site trace
+def test_block_trace_matches_reference(base_model, base_model_path):
+    """Model.block(l, x, trace) of the drop-in module (eii_block_trace) against the digests of the
+    reference's own trace of every site, at five layers (every format variant)."""
+    import intref as drop
+    from test_oracle_golden import check_trace, trace_inputs
+    g, xs = trace_inputs(base_model)
+    M = drop.Model(model_bin=base_model_path)
+    for l, x in xs.items():
+        tr = {}
+        out = M.block(l, x, trace=tr)
+        check_trace(tr, g["layers"][str(l)])
+        assert np.array_equal(out, tr["resid_out"])
