@@ -47,6 +47,7 @@ _SIGS = {
     "eii_linear": ([_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
                     ctypes.c_int, ctypes.c_int, _P, _P], ctypes.c_int),
     "eii_block_trace": ([_P, ctypes.c_int, _P, ctypes.c_int, _P], ctypes.c_int),
+    "eii_set_residual_grid": ([_P, _P, _P], ctypes.c_int),
     "eii_decoder_open": ([_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)], ctypes.c_int),
     "eii_decoder_prefill": ([_P, _P, ctypes.c_int, _P, _P], ctypes.c_int),
     "eii_decoder_step": ([_P, _P, _P, _P], ctypes.c_int),
@@ -175,6 +176,15 @@ class Engine:
         out = np.empty_like(x)
         check(lib().eii_block(self.h, layer, ptr(x), rows // T, T, ptr(out)))
         return out
+
+    def set_residual_grid(self, shift_in, shift_out):
+        """Narrow residual grid shifts per layer (k of resid_in|l, resid_out|l), or None, None for off."""
+        if shift_in is None and shift_out is None:
+            check(lib().eii_set_residual_grid(self.h, None, None))
+            return
+        a = _c(shift_in, np.int32)
+        b = _c(shift_out, np.int32)
+        check(lib().eii_set_residual_grid(self.h, ptr(a), ptr(b)))
 
     def block_trace(self, layer, x):
         """Model.block(l, x, trace) of one sequence x [T, 576] -> (new residual, {site: int64 array})."""

@@ -201,6 +201,9 @@ struct eii_engine {
     int final_f = 0, f_y = 0, final_shift = 0;
     int fast_logits = 0;
     uint64_t *dig_a = nullptr, *dig_b = nullptr;  // logits digest weights (positions, vocabulary)
+    // narrow_residual mode: shifts of the residual grid before / after each layer (-1: off)
+    int grid_in[N_LAYERS], grid_out[N_LAYERS];
+    bool grid_on = false;
     int32_t *exp_tab = nullptr, *rope_c = nullptr, *rope_s = nullptr;
     LayerDev L[N_LAYERS];
     // chunk workspace
@@ -477,8 +480,16 @@ int trace_linear(eii_engine* e, int P, const CUtensorMap& A, bool a_blocked, con
     return launch_gemm_p<EPI_LINEAR>(e, P, A, tmB, ep, st, EII_K_GEMM_LINEAR);
 }
 
+int launch_grid(eii_engine* e, int rows, int s, cudaStream_t st) {
+    const int64_t n = (int64_t)rows * D_MODEL;
+    const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)e->num_sms * 16);
+    CK(launch_k(k_residual_grid, dim3(blocks), dim3(256), 0, st, e->x, n, s));
+    return EII_OK;
+}
+
 int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHook* kv = nullptr,
               const TraceHook* trh = nullptr) {
+    if (e->grid_on && !trh) TRY(launch_grid(e, rows, e->grid_in[l], st));
     LayerDev& L = e->L[l];
     const ActMaps* am;
     TRY(act_maps(e, rows, &am));
@@ -565,6 +576,7 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     ep.a_blocked = 1;
     TRY(launch_gemm_p<EPI_RESID>(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, L.Pm == 2 ? L.tm_d : L.tm_d64, ep, st,
                                  EII_K_GEMM_DOWN, &am->x32, &am->x16));
+    if (e->grid_on && !trh) TRY(launch_grid(e, rows, e->grid_out[l], st));
     return EII_OK;
 }
 
@@ -1114,6 +1126,24 @@ int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* em
                 int32_t* logits_out, uint64_t* digests) {
     TRY(check_forward_args(e, n_seq, T));
     return forward_host(e, ids, n_seq, T, embed_out, resid_out, logits_out, digests, nullptr, -1);
+}
+
+int eii_set_residual_grid(eii_engine* e, const int32_t* shift_in, const int32_t* shift_out) {
+    if (!e) return fail(EII_ERR_ARG, "engine is null");
+    if (!shift_in && !shift_out) {
+        e->grid_on = false;
+        return EII_OK;
+    }
+    if (!shift_in || !shift_out) return fail(EII_ERR_ARG, "give both shift arrays, or neither to turn the grid off");
+    for (int l = 0; l < N_LAYERS; ++l)
+        if (shift_in[l] < 0 || shift_in[l] > 16 || shift_out[l] < 0 || shift_out[l] > 16)
+            return fail(EII_ERR_ARG, "residual grid shifts must be in [0, 16] (layer %d: %d, %d)", l, shift_in[l], shift_out[l]);
+    for (int l = 0; l < N_LAYERS; ++l) {
+        e->grid_in[l] = shift_in[l];
+        e->grid_out[l] = shift_out[l];
+    }
+    e->grid_on = true;
+    return EII_OK;
 }
 
 int eii_decoder_open(eii_engine* e, int n_seq, int max_T, eii_decoder** out) {

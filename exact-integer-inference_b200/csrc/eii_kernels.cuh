@@ -48,6 +48,20 @@ __global__ void k_embed(const int64_t* __restrict__ ids, int M, const int8_t* __
     }
 }
 
+// --------------------------------------------------------------------------- residual grid
+// Narrow comparison mode (python/intref.py:303-308): x = SAT16(RS(x, s)) << s, per element, with
+// the per-layer shift s = k of the residual site (0 <= s <= 16, so the result fits int32).
+__global__ void k_residual_grid(int32_t* __restrict__ x, int64_t n, int s) {
+    griddep_wait();
+    griddep_launch();
+    const int64_t rnd = s >= 1 ? (int64_t(1) << (s - 1)) : 0;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = (static_cast<int64_t>(x[i]) + rnd) >> s;
+        x[i] = static_cast<int32_t>(static_cast<uint32_t>(min(max(r, int64_t(-32768)), int64_t(32767))) << s);
+    }
+}
+
 // --------------------------------------------------------------------------- RMSNorm
 // Exact reciprocal root of python/intref.py:170-177 / c/intref.c:96-104:
 //   S = A 2^32 + B 2^17 + C = sum x^2 (exact, 128-bit), U = isqrt(floor(2^80 / Tt)), Tt = S + EPS_S.

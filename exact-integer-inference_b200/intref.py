@@ -11,9 +11,15 @@ Put this package directory on sys.path where the reference's python/ directory w
 Differences a caller must know:
   * Weights come from a model.bin (the file python/export_vectors.py writes), not from the HF
     checkpoint: pass model_bin=... or set EII_MODEL_BIN.  The per-layer formats are the ones stored
-    in model.bin (wide mode); wide=False is not implemented and raises.
+    in model.bin (wide mode).  wide=False (narrow comparison mode) derives the INT16 formats of the
+    flagged sites from them (f = 31 - k in wide mode, 15 - k in narrow mode) and regenerates the SiLU
+    tables whose format changes, in memory.
+  * forward(ids, narrow_residual=True) needs the k of the resid_in / resid_out sites: from the
+    reference's scaling_proposal.json (proposal_path=...) or, by default, the format table shipped
+    with this package (formats.json, derived from that file).
   * forward/block/embed/rmsnorm/linear run on the GPU through libeii.so; there is no CPU path.
-  * trace= is not implemented yet and raises NotImplementedError.
+  * block(l, x, trace=dict) fills the reference's per-site trace; rmsnorm(trace=...) raises
+    NotImplementedError.
   * exp_table/silu_table/rope_tables return the tables of the most recently loaded model.bin
     (the reference regenerates them with mpmath; the engine, like c/intref.c, reads them).
   * rs, sat and dequant are the host-side numpy helpers of the reference's conventions.
@@ -107,16 +113,18 @@ def rope_tables(T):
 class Model:
     def __init__(self, wide=True, proposal_path=None, model_bin=None, device=0):
         global _last_model
-        if not wide:
-            raise NotImplementedError("narrow mode (wide=False) is not implemented by the B200 engine")
         path = model_bin or os.environ.get("EII_MODEL_BIN")
         if not path:
             raise ValueError("pass model_bin= or set EII_MODEL_BIN to a model.bin written by export_vectors.py")
         with open(path, "rb") as f:
             buf = f.read()
         self._parse(buf)
+        if not wide:
+            buf = self._narrow(buf)
+            self._parse(buf)
+        self._proposal_path = proposal_path
         self._eng = _eii.Engine(np.frombuffer(buf, dtype=np.uint8), device)
-        self.wide = True
+        self.wide = bool(wide)
         self.cfg = {"num_hidden_layers": NL}
         self.L = NL
         _last_model = self
@@ -137,17 +145,54 @@ class Model:
         self.f_y = int(take(1, I64)[0])
         self._exp = take(DMAX + 1, I64)
         self.rope = (take(512 * 32, I64).reshape(512, 32), take(512 * 32, I64).reshape(512, 32))
-        self.layers, self._fm = [], []
+        self.layers, self._fm, self._fm_off, self._silu_off = [], [], [], []
         for _ in range(NL):
+            self._fm_off.append(off)
             fm = [int(v) for v in take(24, I64)]
             d = {"ln1": (take(D, I64), int(take(1, I64)[0])), "ln2": (take(D, I64), int(take(1, I64)[0]))}
             for nm, N, K in _LIN:
                 d[nm] = (take(N * K, np.int8).reshape(N, K).astype(np.float64), take(N, I64), take(N, I64))
+            self._silu_off.append(off)
             d["silu"] = take(65536, I64)
             self.layers.append(d)
             self._fm.append(fm)
         if off != len(buf):
             raise ValueError("model.bin size does not match the layout of c/intref.c:8-13")
+
+    def _narrow(self, buf):
+        """The model.bin of the narrow comparison mode (python/intref.py:152-160): every INT32 site
+        (f = 31 - k) becomes INT16 with f = 15 - k, and the SiLU tables whose (f_g, f_s, bits_s)
+        change are regenerated (the package's restatement of python/intref.py:81-93)."""
+        import synthetic
+        out = bytearray(buf)
+        cache = {}
+        for l in range(NL):
+            fm = self._fm[l]
+            new = list(fm)
+            for i in range(0, 24, 2):
+                if fm[i] == 32:
+                    new[i], new[i + 1] = 16, fm[i + 1] - 16
+            out[self._fm_off[l]:self._fm_off[l] + 24 * 8] = np.asarray(new, dtype=I64).tobytes()
+            gi, si = _SITES.index("gate_proj"), _SITES.index("silu_gate")
+            old_key = (fm[2 * gi + 1], fm[2 * si + 1], fm[2 * si])
+            key = (new[2 * gi + 1], new[2 * si + 1], new[2 * si])
+            if key != old_key:
+                if key not in cache:
+                    cache[key] = synthetic._silu(key)[1]
+                out[self._silu_off[l]:self._silu_off[l] + 65536 * 8] = np.asarray(cache[key], dtype=I64).tobytes()
+        return bytes(out)
+
+    def _resid_k(self):
+        """k of the resid_in|l and resid_out|l sites (the narrow residual grid)."""
+        import json
+        if self._proposal_path:
+            with open(self._proposal_path) as f:
+                sites = json.load(f)["sites"]
+            return ([int(sites[f"resid_in|{l}"]["k"]) for l in range(NL)],
+                    [int(sites[f"resid_out|{l}"]["k"]) for l in range(NL)])
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "formats.json")) as f:
+            rk = json.load(f)["resid_k"]
+        return [int(v) for v in rk["resid_in"]], [int(v) for v in rk["resid_out"]]
 
     def fmt(self, site, l):
         """(bits, f) of a site at layer l, as stored in model.bin (python/intref.py:154-160)."""
@@ -189,12 +234,19 @@ class Model:
         return out
 
     def forward(self, ids, narrow_residual=False):
+        """python/intref.py:288-301; narrow_residual puts the residual on its INT16 grid before and
+        after every layer (python/intref.py:303-308), on the GPU (eii_set_residual_grid)."""
         if narrow_residual:
-            raise NotImplementedError("narrow_residual is not implemented by the B200 engine")
-        x = self.embed(ids)
-        for l in range(self.L):
-            x = self.block(l, x)
-        return self._eng.logits(x)
+            k_in, k_out = self._resid_k()
+            self._eng.set_residual_grid(k_in, k_out)
+        try:
+            x = self.embed(ids)
+            for l in range(self.L):
+                x = self.block(l, x)
+            return self._eng.logits(x)
+        finally:
+            if narrow_residual:
+                self._eng.set_residual_grid(None, None)
 
     def close(self):
         self._eng.close()

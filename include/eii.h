@@ -68,6 +68,14 @@ int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* em
 int eii_forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int32_t* logits_dev,
                        int64_t ld_logits, uint64_t* digests_dev, void* stream);
 
+/* Narrow comparison mode of Model.forward(ids, narrow_residual=True) (python/intref.py:288-308):
+ * the residual is put on its INT16 per-tensor grid, x = SAT16(RS(x, s)) << s, before layer l with
+ * s = shift_in[l] and after it with s = shift_out[l] (s = k of the resid_in|l / resid_out|l sites
+ * of the format proposal, in [0, 16]).  It applies to eii_forward*, eii_block and the decoder
+ * until turned off with two null pointers.  The narrow site formats (wide=False) need no engine
+ * setting: they are a model.bin with INT16 formats and tables (see the drop-in Model). */
+int eii_set_residual_grid(eii_engine* e, const int32_t* shift_in, const int32_t* shift_out);
+
 /* Incremental (cached) decoding, bit-exact with recomputation.  No reference counterpart: the
  * reference recomputes the whole prefix (python/intref.py:288-301) and lists cached decoding as
  * open work.  A decoder holds, per layer, the post-RoPE k and v rows [n_seq][max_T][192] of its

@@ -19,9 +19,11 @@ What it does, for the seeded synthetic model of oracle/synth.py:
   5. runs intref.Model.linear / matmul_exact + rs on seeded activations spanning the full
      INT16 / INT32 ranges for the four contraction shapes and records digests of acc and out;
   6. runs intref.Model.block(l, x, trace) on the t24 tokens for the layers in TRACE_LAYERS and
-     records the sha256 of every trace site (int64, C order) and the site exponents (trace_t24.json).
+     records the sha256 of every trace site (int64, C order) and the site exponents (trace_t24.json);
+  7. runs intref.Model(wide).forward(ids, narrow_residual) on the t24 tokens for the narrow comparison
+     modes and records the logits digests (narrow_t24.json).
 
-    python tests/golden/make_golden.py [--keep DIR] [--skip-subset] [--only-trace]
+    python tests/golden/make_golden.py [--keep DIR] [--skip-subset] [--only-trace] [--only-narrow]
 """
 import argparse
 import hashlib
@@ -127,15 +129,38 @@ def trace_golden(torch, common, intref):
                    "layers": layers}, f, indent=1)
 
 
+def narrow_golden(torch, common, intref):
+    """Logits digests of the reference's narrow comparison modes (python/intref.py:152-160,288-308) on
+    the t24 tokens: formats narrowed (wide=False) with and without the residual grid, and the residual
+    grid alone (wide=True)."""
+    patch(torch, common, intref, False)
+    ids = synth.window_ids(64, 24)
+    out = {}
+    for wide, nres in ((False, False), (False, True), (True, True)):
+        M_ = intref.Model(wide=wide)
+        lg = M_.forward(ids, narrow_residual=nres)
+        out[f"wide={int(wide)},narrow_residual={int(nres)}"] = {
+            "logits_int64_sha256": sha256_bytes(np.ascontiguousarray(lg, dtype=np.int64).tobytes()),
+            "logits_row0_first8": np.asarray(lg[0, :8]).tolist()}
+        print("narrow", wide, nres, "done", flush=True)
+    with open(os.path.join(HERE, "narrow_t24.json"), "w") as f:
+        json.dump({"window": 64, "tokens": 24, "model": "base", "note": "Model(wide).forward(ids, narrow_residual) "
+                   "int64 logits [T, 49152] of the reference", "modes": out}, f, indent=1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--keep", default=None, help="directory to keep the exported vector sets in")
     ap.add_argument("--skip-subset", action="store_true")
     ap.add_argument("--only-trace", action="store_true")
+    ap.add_argument("--only-narrow", action="store_true")
     args = ap.parse_args()
     torch, common, intref = import_reference()
     if args.only_trace:
         trace_golden(torch, common, intref)
+        return
+    if args.only_narrow:
+        narrow_golden(torch, common, intref)
         return
     out_root = args.keep or tempfile.mkdtemp(prefix="eii_golden_")
     refbin = os.path.join(REPO, "oracle", "_ref", "intref")
@@ -224,6 +249,7 @@ def main():
                        "seconds": round(time.time() - t0, 1)}, f, indent=1)
         print("subset done", round(time.time() - t0, 1), "s")
     trace_golden(torch, common, intref)
+    narrow_golden(torch, common, intref)
     print("vector sets in", out_root)
 
 

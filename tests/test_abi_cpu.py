@@ -78,8 +78,6 @@ def test_dropin_module_conventions():
     assert np.array_equal(drop.sat(x, 16), ofw.sat(x, 16))
     with pytest.raises(AssertionError):
         drop.rs(x, np.zeros_like(x))
-    with pytest.raises(NotImplementedError):
-        drop.Model(wide=False)
     saved = os.environ.pop("EII_MODEL_BIN", None)
     try:
         with pytest.raises(ValueError):
@@ -123,3 +121,22 @@ def test_package_model_writer_matches_reference_export(tmp_path):
     synthetic.write_model_bin(p)
     h = hashlib.sha256(open(p, "rb").read()).hexdigest()
     assert h == golden("vectors_t24.json")["files"]["model.bin"]["sha256"]
+
+
+def test_dropin_narrow_formats(base_model_path):
+    """wide=False: the drop-in's narrow model.bin carries the narrow formats of the reference's
+    format table (python/intref.py:154-160) at every layer, and INT16 SiLU tables where silu_gate
+    was INT32 (layers 11 and 28)."""
+    import json
+    import intref as drop
+    M = drop.Model.__new__(drop.Model)
+    buf = open(base_model_path, "rb").read()
+    M._parse(buf)
+    wide_silu = [Ly["silu"].copy() for Ly in M.layers]
+    M._parse(M._narrow(buf))
+    want = json.load(open(os.path.join(REPO, "oracle", "formats.json")))["narrow"]
+    assert [list(fm) for fm in M._fm] == want
+    changed = [l for l in range(30) if not np.array_equal(M.layers[l]["silu"], wide_silu[l])]
+    assert changed == [11, 28]
+    for l in changed:
+        assert M.layers[l]["silu"].min() >= -32768 and M.layers[l]["silu"].max() <= 32767

@@ -328,3 +328,20 @@ def test_block_trace_matches_reference(base_model, base_model_path):
         out = M.block(l, x, trace=tr)
         check_trace(tr, g["layers"][str(l)])
         assert np.array_equal(out, tr["resid_out"])
+
+
+# ------------------------------------------------------------------------------ narrow comparison mode
+@pytest.mark.parametrize("wide,nres", [(False, False), (False, True), (True, True)])
+def test_narrow_modes_match_reference(base_model_path, wide, nres):
+    """Model(wide).forward(ids, narrow_residual) of the drop-in module against the reference's own
+    logits digests (python/intref.py:152-160, 288-308) on the t24 tokens."""
+    import intref as drop
+    g = golden("narrow_t24.json")
+    want = g["modes"][f"wide={int(wide)},narrow_residual={int(nres)}"]
+    M = drop.Model(wide=wide, model_bin=base_model_path)
+    try:
+        lg = M.forward(synth.window_ids(g["window"], g["tokens"]), narrow_residual=nres)
+    finally:
+        M.close()
+    assert lg[0, :8].tolist() == want["logits_row0_first8"]
+    assert sha256_arr(lg, np.int64) == want["logits_int64_sha256"]
