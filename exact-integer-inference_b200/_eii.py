@@ -48,6 +48,10 @@ _SIGS = {
                     ctypes.c_int, ctypes.c_int, _P, _P], ctypes.c_int),
     "eii_block_trace": ([_P, ctypes.c_int, _P, ctypes.c_int, _P], ctypes.c_int),
     "eii_set_residual_grid": ([_P, _P, _P], ctypes.c_int),
+    "eii_table_exp": ([_P], ctypes.c_int),
+    "eii_table_silu": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
+    "eii_table_rope": ([ctypes.c_int, _P, _P], ctypes.c_int),
+    "eii_verify_tables": ([_P, ctypes.c_size_t], ctypes.c_int),
     "eii_decoder_open": ([_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)], ctypes.c_int),
     "eii_decoder_prefill": ([_P, _P, ctypes.c_int, _P, _P], ctypes.c_int),
     "eii_decoder_step": ([_P, _P, _P, _P], ctypes.c_int),
@@ -220,6 +224,37 @@ class Engine:
         check(lib().eii_linear(self.h, ptr(a), M, K, int(bits_in), ptr(W), ptr(m), ptr(n), N, int(f_in), int(f_out),
                                int(bits_out), ptr(out), ptr(acc)))
         return out, acc
+
+
+def table_exp():
+    """exp table (python/intref.py:73-78), regenerated independently of mpmath (include/eii.h)."""
+    out = np.empty(1537, np.int64)
+    check(lib().eii_table_exp(ptr(out)))
+    return out
+
+
+def table_silu(f_in, f_out, bits):
+    """SiLU table over the 65536 INT16 inputs (python/intref.py:81-94), regenerated independently."""
+    out = np.empty(65536, np.int64)
+    check(lib().eii_table_silu(int(f_in), int(f_out), int(bits), ptr(out)))
+    return out
+
+
+def table_rope(n_pos=512):
+    """RoPE tables (python/intref.py:97-108) [n_pos, 32] cos and sin, regenerated independently."""
+    c = np.empty((n_pos, 32), np.int64)
+    s = np.empty((n_pos, 32), np.int64)
+    check(lib().eii_table_rope(int(n_pos), ptr(c), ptr(s)))
+    return c, s
+
+
+def verify_tables(model_bin):
+    """Regenerate every table of a model.bin (path or bytes) and compare; raises EiiError on a difference."""
+    if not isinstance(model_bin, (bytes, bytearray, memoryview, np.ndarray)):
+        with open(model_bin, "rb") as f:
+            model_bin = f.read()
+    buf = np.frombuffer(model_bin, dtype=np.uint8) if not isinstance(model_bin, np.ndarray) else model_bin
+    check(lib().eii_verify_tables(ptr(buf), buf.nbytes))
 
 
 class Decoder:

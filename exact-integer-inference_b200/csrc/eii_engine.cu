@@ -32,6 +32,7 @@
 
 #include "eii.h"
 #include "eii_attn.cuh"
+#include "eii_tables.h"
 #include "eii_gemm.cuh"
 #include "eii_kernels.cuh"
 
@@ -1126,6 +1127,79 @@ int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* em
                 int32_t* logits_out, uint64_t* digests) {
     TRY(check_forward_args(e, n_seq, T));
     return forward_host(e, ids, n_seq, T, embed_out, resid_out, logits_out, digests, nullptr, -1);
+}
+
+int eii_table_exp(int64_t* out) {
+    if (!out) return fail(EII_ERR_ARG, "out is null");
+    if (!tables::exp_table(out)) return fail(EII_ERR_FORMAT, "exp table: a value is within 2^-200 of a rounding point");
+    return EII_OK;
+}
+
+int eii_table_silu(int f_in, int f_out, int bits, int64_t* out) {
+    if (!out) return fail(EII_ERR_ARG, "out is null");
+    if (f_in < 0 || f_in > 40 || f_out < -20 || f_out > 40 || bits < 2 || bits > 63)
+        return fail(EII_ERR_ARG, "SiLU table format (f_in %d, f_out %d, bits %d) out of range", f_in, f_out, bits);
+    if (!tables::silu_table(f_in, f_out, bits, out))
+        return fail(EII_ERR_FORMAT, "SiLU table (%d, %d, %d): a value is within 2^-200 of a rounding point", f_in, f_out, bits);
+    return EII_OK;
+}
+
+int eii_table_rope(int n_pos, int64_t* cos_out, int64_t* sin_out) {
+    if (!cos_out || !sin_out) return fail(EII_ERR_ARG, "null output");
+    if (n_pos < 1 || n_pos > 4096) return fail(EII_ERR_ARG, "n_pos must be in [1, 4096] (got %d)", n_pos);
+    if (!tables::rope_tables(n_pos, cos_out, sin_out))
+        return fail(EII_ERR_FORMAT, "RoPE tables: a value is within 2^-200 of a rounding point");
+    return EII_OK;
+}
+
+int eii_verify_tables(const void* data, size_t nbytes) {
+    if (!data) return fail(EII_ERR_ARG, "model.bin buffer is null");
+    const uint8_t* p = static_cast<const uint8_t*>(data);
+    // offsets of the model.bin layout (c/intref.c:8-13): emb_q, emb_m, emb_n, final gain + f, f_y, exp,
+    // rope cos, rope sin, then per layer fm[24], ln1[576] + f, ln2[576] + f, 7 weights + m + n, silu[65536]
+    size_t off = (size_t)VOCAB * D_MODEL + 2 * 8 * (size_t)VOCAB + 8 * (size_t)(D_MODEL + 1) + 8;
+    const size_t exp_off = off;
+    off += 8 * (size_t)(DMAX + 1);
+    const size_t rope_off = off;
+    off += 2 * 8 * (size_t)ROPE_POS * 32;
+    static const int N_[7] = {576, 192, 192, 576, 1536, 1536, 576}, K_[7] = {576, 576, 576, 576, 576, 576, 1536};
+    size_t layer_bytes = 24 * 8 + 2 * 8 * (D_MODEL + 1) + 65536 * 8;
+    for (int i = 0; i < 7; ++i) layer_bytes += (size_t)N_[i] * K_[i] + 2 * 8 * (size_t)N_[i];
+    if (nbytes != off + N_LAYERS * layer_bytes)
+        return fail(EII_ERR_FORMAT, "model.bin is %zu bytes, the layout of c/intref.c:8-13 needs %zu", nbytes,
+                    off + N_LAYERS * layer_bytes);
+    auto i64 = [&](size_t o) { int64_t v; memcpy(&v, p + o, 8); return v; };
+    std::vector<int64_t> gen(65536), gen2((size_t)ROPE_POS * 32);
+    TRY(eii_table_exp(gen.data()));
+    for (int d = 0; d <= DMAX; ++d)
+        if (gen[d] != i64(exp_off + 8 * (size_t)d))
+            return fail(EII_ERR_FORMAT, "exp table differs at d = %d: model.bin %lld, regenerated %lld", d,
+                        (long long)i64(exp_off + 8 * (size_t)d), (long long)gen[d]);
+    TRY(eii_table_rope(ROPE_POS, gen.data(), gen2.data()));
+    for (int i = 0; i < ROPE_POS * 32; ++i) {
+        if (gen[i] != i64(rope_off + 8 * (size_t)i))
+            return fail(EII_ERR_FORMAT, "RoPE cos differs at [%d][%d]", i / 32, i % 32);
+        if (gen2[i] != i64(rope_off + 8 * (size_t)(ROPE_POS * 32 + i)))
+            return fail(EII_ERR_FORMAT, "RoPE sin differs at [%d][%d]", i / 32, i % 32);
+    }
+    std::map<long long, std::vector<int64_t>> cache;
+    for (int l = 0; l < N_LAYERS; ++l) {
+        const size_t lo = off + (size_t)l * layer_bytes;
+        const int f_g = (int)i64(lo + 8 * 17), bits_s = (int)i64(lo + 8 * 20), f_s = (int)i64(lo + 8 * 21);
+        const long long key = ((long long)f_g << 32) | ((long long)(f_s + 64) << 8) | bits_s;
+        auto it = cache.find(key);
+        if (it == cache.end()) {
+            std::vector<int64_t> t(65536);
+            TRY(eii_table_silu(f_g, f_s, bits_s, t.data()));
+            it = cache.emplace(key, std::move(t)).first;
+        }
+        const size_t so = lo + layer_bytes - 65536 * 8;
+        for (int i = 0; i < 65536; ++i)
+            if (it->second[i] != i64(so + 8 * (size_t)i))
+                return fail(EII_ERR_FORMAT, "SiLU table of layer %d (f_g %d, f_s %d, bits %d) differs at input %d", l,
+                            f_g, f_s, bits_s, i - 32768);
+    }
+    return EII_OK;
 }
 
 int eii_set_residual_grid(eii_engine* e, const int32_t* shift_in, const int32_t* shift_out) {

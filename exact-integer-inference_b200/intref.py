@@ -13,7 +13,7 @@ Differences a caller must know:
     checkpoint: pass model_bin=... or set EII_MODEL_BIN.  The per-layer formats are the ones stored
     in model.bin (wide mode).  wide=False (narrow comparison mode) derives the INT16 formats of the
     flagged sites from them (f = 31 - k in wide mode, 15 - k in narrow mode) and regenerates the SiLU
-    tables whose format changes, in memory.
+    tables whose format changes, in memory (eii_table_silu).
   * forward(ids, narrow_residual=True) needs the k of the resid_in / resid_out sites: from the
     reference's scaling_proposal.json (proposal_path=...) or, by default, the format table shipped
     with this package (formats.json, derived from that file).
@@ -162,8 +162,7 @@ class Model:
     def _narrow(self, buf):
         """The model.bin of the narrow comparison mode (python/intref.py:152-160): every INT32 site
         (f = 31 - k) becomes INT16 with f = 15 - k, and the SiLU tables whose (f_g, f_s, bits_s)
-        change are regenerated (the package's restatement of python/intref.py:81-93)."""
-        import synthetic
+        change are regenerated (eii_table_silu, python/intref.py:81-94)."""
         out = bytearray(buf)
         cache = {}
         for l in range(NL):
@@ -178,7 +177,7 @@ class Model:
             key = (new[2 * gi + 1], new[2 * si + 1], new[2 * si])
             if key != old_key:
                 if key not in cache:
-                    cache[key] = synthetic._silu(key)[1]
+                    cache[key] = _eii.table_silu(*key)
                 out[self._silu_off[l]:self._silu_off[l] + 65536 * 8] = np.asarray(cache[key], dtype=I64).tobytes()
         return bytes(out)
 

@@ -68,6 +68,20 @@ int eii_forward(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* em
 int eii_forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int32_t* logits_dev,
                        int64_t ld_logits, uint64_t* digests_dev, void* stream);
 
+/* Independent regeneration of the model.bin tables (python/intref.py:66-108: exp_table, silu_table,
+ * rope_tables), host only (no device needed).  The reference computes them with mpmath at 50
+ * digits and lists an independent cross-check as open work; these compute every value in 320-bit
+ * binary fixed point from their own series and round half up only where an error bound proves
+ * the decision (EII_ERR_FORMAT otherwise).
+ *   eii_table_exp:  out[1537],  E[d] = floor(2^30 exp(-d/128) + 1/2)
+ *   eii_table_silu: out[65536], SAT_bits(floor(x / (1 + exp(-x)) 2^f_out + 1/2)), x = (i - 32768) 2^-f_in
+ *   eii_table_rope: cos_out, sin_out [n_pos][32], floor(2^30 cos/sin(p 100000^(-2j/64)) + 1/2)
+ * eii_verify_tables regenerates every table of a model.bin image and reports the first difference. */
+int eii_table_exp(int64_t* out);
+int eii_table_silu(int f_in, int f_out, int bits, int64_t* out);
+int eii_table_rope(int n_pos, int64_t* cos_out, int64_t* sin_out);
+int eii_verify_tables(const void* model_bin, size_t nbytes);
+
 /* Narrow comparison mode of Model.forward(ids, narrow_residual=True) (python/intref.py:288-308):
  * the residual is put on its INT16 per-tensor grid, x = SAT16(RS(x, s)) << s, before layer l with
  * s = shift_in[l] and after it with s = shift_out[l] (s = k of the resid_in|l / resid_out|l sites

@@ -21,9 +21,12 @@ What it does, for the seeded synthetic model of oracle/synth.py:
   6. runs intref.Model.block(l, x, trace) on the t24 tokens for the layers in TRACE_LAYERS and
      records the sha256 of every trace site (int64, C order) and the site exponents (trace_t24.json);
   7. runs intref.Model(wide).forward(ids, narrow_residual) on the t24 tokens for the narrow comparison
-     modes and records the logits digests (narrow_t24.json).
+     modes and records the logits digests (narrow_t24.json);
+  8. records digests of the reference's exp, RoPE and SiLU tables for every format pair of its
+     format table (tables.json).
 
     python tests/golden/make_golden.py [--keep DIR] [--skip-subset] [--only-trace] [--only-narrow]
+                                       [--only-tables]
 """
 import argparse
 import hashlib
@@ -148,14 +151,37 @@ def narrow_golden(torch, common, intref):
                    "int64 logits [T, 49152] of the reference", "modes": out}, f, indent=1)
 
 
+def tables_golden(intref):
+    """Digests of the reference's own mpmath tables (python/intref.py:66-108): exp_table(),
+    rope_tables(512) and silu_table(f_g, f_s, bits_s) for every (gate, silu) format pair of the
+    reference's format table, wide and narrow modes (oracle/formats.json)."""
+    with open(os.path.join(REPO, "oracle", "formats.json")) as f:
+        fmt = json.load(f)
+    keys = sorted({(fm[17], fm[21], fm[20]) for mode in ("wide", "narrow") for fm in fmt[mode]})
+    out = {"exp": sha256_bytes(np.ascontiguousarray(intref.exp_table(), dtype=np.int64).tobytes())}
+    C, S = intref.rope_tables(512)
+    out["rope_cos"] = sha256_bytes(np.ascontiguousarray(C, dtype=np.int64).tobytes())
+    out["rope_sin"] = sha256_bytes(np.ascontiguousarray(S, dtype=np.int64).tobytes())
+    out["silu"] = {f"{fi},{fo},{b}": sha256_bytes(np.ascontiguousarray(intref.silu_table(fi, fo, b), dtype=np.int64).tobytes())
+                   for fi, fo, b in keys}
+    with open(os.path.join(HERE, "tables.json"), "w") as f:
+        json.dump({"note": "sha256 of int64 C-order tables from the reference's own python/intref.py functions "
+                   "(mpmath 50 digits); silu keys are f_in,f_out,bits", "tables": out}, f, indent=1)
+    print("tables done:", len(keys), "SiLU keys", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--keep", default=None, help="directory to keep the exported vector sets in")
     ap.add_argument("--skip-subset", action="store_true")
     ap.add_argument("--only-trace", action="store_true")
     ap.add_argument("--only-narrow", action="store_true")
+    ap.add_argument("--only-tables", action="store_true")
     args = ap.parse_args()
     torch, common, intref = import_reference()
+    if args.only_tables:
+        tables_golden(intref)
+        return
     if args.only_trace:
         trace_golden(torch, common, intref)
         return
@@ -250,6 +276,7 @@ def main():
         print("subset done", round(time.time() - t0, 1), "s")
     trace_golden(torch, common, intref)
     narrow_golden(torch, common, intref)
+    tables_golden(intref)
     print("vector sets in", out_root)
 
 
