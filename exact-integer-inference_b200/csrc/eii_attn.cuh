@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     const int64_t row0 = static_cast<int64_t>(seq) * T;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int quad = warp & 3, kb = warp >> 2;  // rows 32 quad .. +31, key block / dim block kb
-    const int i = quad * 32 + lane;             // query row of this thread (TMEM lane)
+    const int i = quad * 32 + lane;             // tile row of this thread (TMEM lane)
 
     if (warp == 0) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
     if (tid == 0) { mbar_init(bar, 1); *abort = 0; fence_mbar_init(); }
@@ -107,9 +107,16 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
 #pragma unroll
             for (int u = 0; u < 16; ++u) lo[u] = hi[u] = 0;
         }
-        uint8_t* tile = which < 3 ? Qs + which * ATTN_TC_TILE : Ks;
-        *reinterpret_cast<uint4*>(tile + sw128(r, c * 16)) = *reinterpret_cast<uint4*>(lo);
-        *reinterpret_cast<uint4*>(tile + sw128(r, 64 + c * 16)) = *reinterpret_cast<uint4*>(hi);
+        // q rows go to their packed tile slot (see pack_slot below); k rows to the K tile
+        uint8_t* tile = Ks;
+        int tr = r;
+        if (which < 3) {
+            const int sl = 3 * (3 - r / 32) + which;
+            tile = Qs + (sl / 4) * ATTN_TC_TILE;
+            tr = (sl % 4) * 32 + r % 32;
+        }
+        *reinterpret_cast<uint4*>(tile + sw128(tr, c * 16)) = *reinterpret_cast<uint4*>(lo);
+        *reinterpret_cast<uint4*>(tile + sw128(tr, 64 + c * 16)) = *reinterpret_cast<uint4*>(hi);
     }
     {   // V^T: thread (j, dim quarter) scatters key j's 16 values into column j of both planes
         const int j = tid & 127, dq = tid >> 7;
@@ -138,11 +145,19 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     const uint32_t sK = smem_u32(Ks), sV0 = smem_u32(VT), sV1 = smem_u32(VT + 8192);
     const uint32_t sP0 = smem_u32(Ps), sP1 = smem_u32(Ps + ATTN_TC_TILE);
     // key block kb holds keys 32 kb .. 32 kb + 31; it has unmasked keys for this quadrant iff kb <= quad
-    const bool active = kb <= quad;
+    // Packed query tiles: the three heads' 32-row query blocks (head h, block b: positions 32 b ..
+    // 32 b + 31) fill the twelve (tile, lane quadrant) slots s = 4 t + q in order of decreasing b:
+    // s -> head s % 3, block 3 - s / 3.  A quadrant holding block b has b + 1 live key blocks under
+    // the causal mask, and each tile waits for its slowest quadrant, so the three tiles cost 4, 3
+    // and 2 key blocks instead of 4 each with one head per tile.
+    bool active = false;
     const bool fast = ap.shift_s >= 1 && ap.shift_s <= 31;
     const int64_t srnd = fast ? (int64_t(1) << (ap.shift_s - 1)) : 0;
 
-    for (int h = 0; h < 3; ++h) {
+    for (int h = 0; h < 3; ++h) {  // h = packed tile
+        const int slot = 4 * h + quad, hq = slot % 3, bq = 3 - slot / 3;
+        const int pos = 32 * bq + lane;  // sequence position of this thread's query row
+        active = kb <= bq;
         // ---- S = Q_h K^T (M = 128 queries, N = 128 keys, K = 64 dims per plane pair)
         if (tid == 0) {
             const uint32_t sQ = smem_u32(Qs + h * ATTN_TC_TILE);
@@ -197,7 +212,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                                               static_cast<int64_t>(static_cast<int32_t>(d0[q + u]));
                             s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
                         }
-                        if (col + q + u <= i) lmax = max(lmax, s2[u]);
+                        if (col + q + u <= pos) lmax = max(lmax, s2[u]);
                     }
                     sp[(c * 16 + q) / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
                 }
@@ -217,7 +232,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                 const int j = kb * 32 + q;
                 const int32_t s = static_cast<int16_t>((q & 1) ? (sp[q / 2] >> 16) : (sp[q / 2] & 0xFFFF));
                 const int32_t dd = rowmax - s;
-                if (j <= i && dd <= DMAX) lz += E[dd];
+                if (j <= pos && dd <= DMAX) lz += E[dd];
             }
         }
         red_z[kb * 128 + i] = lz;
@@ -236,10 +251,10 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                     const int qq = c * 16 + q;
                     const int j = kb * 32 + qq;
                     int64_t p = 0;
-                    if (active && i < T) {
+                    if (active && pos < T) {
                         const int32_t s = static_cast<int16_t>((qq & 1) ? (sp[qq / 2] >> 16) : (sp[qq / 2] & 0xFFFF));
                         const int32_t dd = rowmax - s;
-                        if (j <= i && dd <= DMAX) p = prob_q16_f32(E[dd], Z, halfZ, scale);
+                        if (j <= pos && dd <= DMAX) p = prob_q16_f32(E[dd], Z, halfZ, scale);
                     }
                     if (p == 65536) jstar_s[i] = j;
                     b0[q] = static_cast<uint8_t>(p & 0xFF);
@@ -273,7 +288,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
         phase ^= 1;
         tc_fence_after();
         {   // epilogue: rows of my quadrant, dims 16 kb .. 16 kb + 15
-            const int hh = g * 3 + h;
+            const int hh = g * 3 + hq;
             const int col = kb * 16;
             uint32_t c0[16], c1[16], c2[16];
             tmem_ld16(tq + col, c0);
@@ -281,7 +296,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
             tmem_ld16(tq + 128 + col, c2);
             tmem_wait_ld();
             tmem_launder(c0); tmem_launder(c1); tmem_launder(c2);
-            if (i < T) {
+            if (pos < T) {
                 const int js = jstar_s[i];
                 int32_t out[16];
                 const bool cfast = ap.shift_c >= 1 && ap.shift_c <= 31;
@@ -308,7 +323,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                 }
                 // row-blocked planes: this warp's 32 rows x 16 dims are 512 contiguous bytes per plane
                 const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
-                uint8_t* dst = ap.ctx_planes + blocked_off(row0 + i, hh * 64 + col, D_MODEL);
+                uint8_t* dst = ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL);
                 for (int p = 0; p < ap.P; ++p) {
                     uint8_t b[16];
 #pragma unroll
