@@ -87,6 +87,7 @@ struct LayerDev {
     int silu_lo, silu_count, silu_wide, silu_d;
     int fast_qkv, fast_o, fast_gu, fast_d;  // fast requantisation path applies (see EpiParams::fast)
     int narrow_qkv, narrow_gu;              // requantised values provably fit int32 (EpiParams::narrow)
+    int gated_sd;                           // |gated| <= 2^30: signed-digit planes (EpiParams::sd_flags)
     int8_t *w_qkv, *w_o, *w_gu, *w_d;
     int2 *msh_qkv, *msh_o, *msh_gu, *msh_d;
     CUtensorMap tm_qkv, tm_o, tm_gu, tm_d, tm_o64, tm_d64;  // *64: boxes of BN_P4 rows for 4-plane GEMMs
@@ -214,6 +215,7 @@ struct eii_engine {
     int16_t *q = nullptr, *k = nullptr, *v = nullptr;
     uint8_t* ctx_planes = nullptr;
     uint8_t* gated_planes = nullptr;
+    uint32_t* sd_flags = nullptr;  // [N_LAYERS][ceil(cap_rows / 128)]: top signed digit needed per row block
     int32_t* logits_ws = nullptr;
     int64_t logits_ws_rows = 0;
     int64_t* ids_dev = nullptr;
@@ -307,6 +309,7 @@ int free_workspace(eii_engine* e) {
     e->cap_rows = 0;
     e->x = nullptr;
     e->h_planes = e->ctx_planes = e->gated_planes = nullptr;
+    e->sd_flags = nullptr;
     e->q = e->k = e->v = nullptr;
     e->logits_ws = nullptr;
     e->logits_ws_rows = 0;
@@ -327,6 +330,7 @@ int ensure_rows(eii_engine* e, int rows) {
     TRY(dalloc(W, &e->v, (size_t)rows * 192));
     TRY(dalloc(W, &e->ctx_planes, (size_t)4 * ((rows + 127) / 128) * 128 * D_MODEL));  // row-blocked
     TRY(dalloc(W, &e->gated_planes, (size_t)4 * ((rows + 127) / 128) * 128 * D_FF));  // row-blocked
+    TRY(dalloc(W, &e->sd_flags, (size_t)N_LAYERS * ((rows + 127) / 128)));
     e->cap_rows = rows;
     return EII_OK;
 }
@@ -435,11 +439,11 @@ int launch_gemm_p(eii_engine* e, int P, const CUtensorMap& A, const CUtensorMap&
 
 int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, int shift, int bits,
                 uint8_t* planes, int P, int64_t* out64, cudaStream_t st, int64_t* u_out = nullptr,
-                int64_t* z_out = nullptr) {
+                int64_t* z_out = nullptr, uint32_t* zero_ptr = nullptr, int zero_n = 0) {
     const int rows_per_block = 16;  // 8 warps, two rows each
     ProfScope ps(e, EII_K_NORM, st);
     CK(launch_k(k_rmsnorm, dim3((rows + rows_per_block - 1) / rows_per_block), dim3(256), 0, st, x, rows, gain, shift,
-                bits, planes, P, out64, u_out, z_out));
+                bits, planes, P, out64, u_out, z_out, zero_ptr, zero_n));
     return EII_OK;
 }
 
@@ -472,12 +476,13 @@ struct TraceHook {
 };
 
 int trace_linear(eii_engine* e, int P, const CUtensorMap& A, bool a_blocked, const int8_t* W, int K, int N,
-                 const int2* msh, int bits_out, int64_t* out, int rows, cudaStream_t st) {
+                 const int2* msh, int bits_out, int64_t* out, int rows, cudaStream_t st, bool a_sd = false) {
     CUtensorMap tmB;
     TRY(map_2d(&tmB, W, K, N, P == 4 ? BN_P4 : 128));
     EpiParams ep{};
     ep.M = rows; ep.N = N; ep.K = K; ep.msh = msh; ep.err = e->err_dev; ep.out64 = out; ep.bits_out = bits_out;
     ep.a_blocked = a_blocked ? 1 : 0;
+    ep.a_sd = a_sd ? 1 : 0;
     return launch_gemm_p<EPI_LINEAR>(e, P, A, tmB, ep, st, EII_K_GEMM_LINEAR);
 }
 
@@ -553,7 +558,9 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
                                  EII_K_GEMM_O, &am->x32, &am->x16));
     if (trh) CK(cudaMemcpyAsync(trh->xmid, e->x, sizeof(int32_t) * rows * D_MODEL, cudaMemcpyDeviceToDevice, st));
 
-    TRY(launch_norm(e, e->x, rows, L.ln2, L.norm2_shift, L.h2.bits, e->h_planes, 2, nullptr, st));
+    uint32_t* sd_flags = L.gated_sd ? e->sd_flags + (size_t)l * ((e->cap_rows + 127) / 128) : nullptr;
+    TRY(launch_norm(e, e->x, rows, L.ln2, L.norm2_shift, L.h2.bits, e->h_planes, 2, nullptr, st, nullptr, nullptr,
+                    sd_flags, (rows + 127) / 128));
     if (trh) {
         TRY(launch_norm(e, e->x, rows, L.ln2, L.norm2_shift, L.h2.bits, nullptr, 0, trh->n2, st, trh->u2, trh->z2));
         // gate and up columns interleaved per 128-column tile, as W_gu is stored
@@ -566,15 +573,15 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     ep.silu_neg = L.silu_neg; ep.silu_smem = L.silu_neg != nullptr; ep.silu_lo = L.silu_lo;
     ep.silu_count = L.silu_count; ep.silu_wide = L.silu_wide; ep.silu_d = L.silu_d; ep.bits_s = L.s.bits;
     ep.fast = L.fast_gu; ep.narrow = L.narrow_gu;
-    ep.bits_m = L.m.bits; ep.gated_P = L.Pm; ep.gated_planes = e->gated_planes;
+    ep.bits_m = L.m.bits; ep.gated_P = L.Pm; ep.gated_planes = e->gated_planes; ep.sd_flags = sd_flags;
     TRY(launch_gemm<2, EPI_GATEUP>(e, am->h, L.tm_gu, ep, st, EII_K_GEMM_GATEUP));
     if (trh)
         TRY(trace_linear(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, true, L.w_d, D_FF, D_MODEL, L.msh_d, 64, trh->dres,
-                         rows, st));
+                         rows, st, L.gated_sd != 0));
 
     ep = EpiParams{};
     ep.M = rows; ep.N = D_MODEL; ep.K = D_FF; ep.msh = L.msh_d; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_d;
-    ep.a_blocked = 1;
+    ep.a_blocked = 1; ep.sd_flags = sd_flags; ep.a_sd = sd_flags != nullptr;
     TRY(launch_gemm_p<EPI_RESID>(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, L.Pm == 2 ? L.tm_d : L.tm_d64, ep, st,
                                  EII_K_GEMM_DOWN, &am->x32, &am->x16));
     if (e->grid_on && !trh) TRY(launch_grid(e, rows, e->grid_out[l], st));
@@ -877,6 +884,8 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
             TRY(check_col_shifts(msh, "gate/up", l));
             L.fast_gu = cols_fast(msh) && L.gated_shift >= 0 && L.gated_shift <= 31;
             L.narrow_gu = L.fast_gu && cols_narrow(w.data(), 2 * D_FF, D_MODEL, msh, 32768);
+            // |SAT32(RS(silu * up, gs))| <= |silu * up| <= 2^15 * 2^15 when both are INT16 and gs >= 0
+            L.gated_sd = L.m.bits == 32 && L.s.bits == 16 && L.u.bits == 16 && L.gated_shift >= 0 && !getenv("EII_NO_SD");
             TRY(upload(e, &L.w_gu, w.data(), w.size()));
             TRY(upload(e, &L.msh_gu, msh.data(), 2 * D_FF));
             TRY(map_2d(&L.tm_gu, L.w_gu, D_MODEL, 2 * D_FF));
@@ -1376,14 +1385,14 @@ int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_tr
     free_list(tmp);
     if (rc != EII_OK) return rc;
     // planes -> values (row-blocked layout; low planes unsigned, top plane signed)
-    auto unblock = [&](const std::vector<uint8_t>& buf, int P, int K, int64_t stride, int64_t* out) {
+    auto unblock = [&](const std::vector<uint8_t>& buf, int P, int K, int64_t stride, int64_t* out, bool all_signed) {
         for (int r = 0; r < rows; ++r)
             for (int c = 0; c < K; ++c) {
                 const int64_t off = blocked_off(r, c, K);
                 int64_t val = 0;
                 for (int p = 0; p < P; ++p) {
                     const uint8_t b = buf[p * stride + off];
-                    val += (p == P - 1 ? (int64_t)(int8_t)b : (int64_t)b) * ((int64_t)1 << (8 * p));
+                    val += (p == P - 1 || all_signed ? (int64_t)(int8_t)b : (int64_t)b) * ((int64_t)1 << (8 * p));
                 }
                 out[(size_t)r * K + c] = val;
             }
@@ -1395,7 +1404,7 @@ int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_tr
     put(tr->norm1_U, u1); put(tr->norm1_z, z1); put(tr->norm1_out, n1);
     put(tr->q_proj, q); put(tr->k_proj, k); put(tr->v_proj, v); put(tr->q_rope, qr); put(tr->k_rope, kr);
     put(tr->attn_score, score); put(tr->attn_prob, prob);
-    if (tr->attn_ctx) unblock(ctxp, L.Pc, D_MODEL, cstride, tr->attn_ctx);
+    if (tr->attn_ctx) unblock(ctxp, L.Pc, D_MODEL, cstride, tr->attn_ctx, false);
     put(tr->o_res, ores); put(tr->resid_mid, xmid);
     put(tr->norm2_U, u2); put(tr->norm2_z, z2); put(tr->norm2_out, n2);
     for (int r = 0; r < rows; ++r)
@@ -1406,7 +1415,7 @@ int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_tr
             if (tr->up_proj) tr->up_proj[(size_t)r * D_FF + j] = u;
             if (tr->silu_gate) tr->silu_gate[(size_t)r * D_FF + j] = silu[(size_t)(g + 32768)];
         }
-    if (tr->mlp_gated) unblock(gatedp, L.Pm, D_FF, gstride, tr->mlp_gated);
+    if (tr->mlp_gated) unblock(gatedp, L.Pm, D_FF, gstride, tr->mlp_gated, L.gated_sd != 0);
     put(tr->down_res, dres); put(tr->resid_out, xout);
     return EII_OK;
 }

@@ -77,6 +77,14 @@ struct EpiParams {
     uint8_t* gated_planes;
     // A operand in that row-blocked layout (4-D map, no swizzle) instead of [P][M][K] with 128-byte swizzle
     int a_blocked;
+    // Signed-digit gated planes (host-proven |gated| <= 2^30): gated = sum_p 2^(8p) d_p with every digit
+    // d_p in [-128, 127]; the digit bytes are the bytes of (gated + 0x808080) ^ 0x808080, and the top
+    // digit (byte 3 of gated + 0x808080) is 0 for gated in [-0x808080, 0x7F7F7F].  sd_flags[m_blk]
+    // != 0 marks a 128-row block where some top digit is not 0.  EPI_GATEUP writes the digits and
+    // the flags; the down GEMM (EPI_RESID, P = 4) skips the top plane (loads and MMAs) in blocks
+    // whose flag is 0.  a_sd: the A planes are signed digits (every plane multiplied as s8).
+    uint32_t* sd_flags;
+    int a_sd;
     // EPI_LOGITS: int32 out[row * ld + col] = RS(acc m, shift) (low 32 bits, no SAT)
     int32_t* logits;
     int64_t ld_logits;
@@ -401,6 +409,8 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
         uint8_t* gdst = ep.gated_planes + static_cast<int64_t>(m_blk) * 64 * ep.N + (n_blk * 4 + cg) * 2048 +
                         (quad * 32 + lane) * 16;
         uint32_t keep[4][2];  // packed planes of features 0..7, stored with 8..15 as one 16-byte word
+        const bool sd = ep.sd_flags != nullptr && ep.gated_P == 4;
+        bool big = false;     // some value of this warp needs the top signed digit
         const int gs = ep.gated_shift;
         const int64_t grnd = gs >= 1 ? (int64_t(1) << (gs - 1)) : 0;
         const bool lean = MODE >= 1 && ep.silu_smem && !ep.silu_wide && ep.bits_s == 16 && ep.silu_d <= 15 &&
@@ -443,6 +453,16 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                     }
                 }
             }
+            if (sd) {  // signed digits: the bytes of (gated + 0x808080) ^ 0x808080
+                uint32_t any = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t w = static_cast<uint32_t>(gm[i]) + 0x808080u;
+                    any |= w;
+                    gm[i] = static_cast<int32_t>(w ^ 0x808080u);
+                }
+                big |= (any >> 24) != 0;
+            }
             if (h8 == 0) {
                 pack_plane<0, 8>(gm, keep[0]);
                 pack_plane<1, 8>(gm, keep[1]);
@@ -464,12 +484,14 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 }
             }
         }
+        if (sd && __any_sync(0xffffffffu, big) && lane == 0) atomicOr(ep.sd_flags + m_blk, 1u);
     } else if constexpr (KIND == EPI_RESID) {
         // x = SAT32(x + RS(acc m, shift)) on this warp's 32 rows x NCOL columns.  The residual tile is
         // in the staging buffer (TMA load issued before the accumulator wait); with one resident
         // 16-column chunk (XCH == 1) the second chunk is loaded after the first is stored.
         constexpr int NCOL = BN / 4, NCH = NCOL / 16;
         constexpr int XCH = GemmCfg<P, KIND>::STG_BYTES / 2048;
+        const bool top4 = P != 4 || !ep.sd_flags || __ldg(ep.sd_flags + m_blk) != 0;
         constexpr int S = XCH * 64;  // staging row bytes
         const int row0 = m_blk * 128 + quad * 32;
         const bool live = row0 < ep.M;
@@ -490,6 +512,12 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
             }
             uint32_t v[P][16];
             load_planes<P, 16>(tacc + tc, v);
+            if constexpr (P == 4) {
+                if (!top4) {  // top signed-digit plane not computed for this row block
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) v[3][q] = 0;
+                }
+            }
             if (row_ok) {
                 int32_t xo[16];
 #pragma unroll
@@ -662,15 +690,19 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             bool ok = true;
             for (int t = t_first; t < t_end && ok; t += t_step) {
                 const int m_blk = t / num_n, n_blk = t % num_n;
+                // planes of this tile's A operand (3 when the signed-digit top plane is all zero)
+                int np = P;
+                if constexpr (KIND == EPI_RESID && P == 4)
+                    if (ep.sd_flags && __ldg(ep.sd_flags + m_blk) == 0) np = 3;
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort, ep.err, ERR_TIMEOUT_PRODUCER)) { ok = false; break; }
                     uint8_t* sA = smem + stage * C::STAGE_BYTES;
                     uint8_t* sB = sA + P * C::A_BYTES;
-                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    mbar_arrive_expect_tx(&full[stage], np * C::A_BYTES + C::B_BYTES);
                     if (ep.a_blocked) {
 #pragma unroll
                         for (int p = 0; p < P; ++p)
-                            tma_load_4d(sA + p * C::A_BYTES, &tmA, &full[stage], 0, kb * 8, m_blk, p);
+                            if (p < np) tma_load_4d(sA + p * C::A_BYTES, &tmA, &full[stage], 0, kb * 8, m_blk, p);
                     } else {
 #pragma unroll
                         for (int p = 0; p < P; ++p)
@@ -699,14 +731,19 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             int acc_iter = 0;
             bool ok = true;
             bool issued = false;
+            griddep_wait();  // the signed-digit flags below are the previous kernel's output
             for (int t = t_first; t < t_end && ok; t += t_step, ++acc_iter) {
                 const int n_blk = t % num_n;
+                // planes of this tile (the producer loads the same: 3 when the signed-digit top plane is 0)
+                int np = P;
+                if constexpr (KIND == EPI_RESID && P == 4)
+                    if (ep.sd_flags && __ldg(ep.sd_flags + t / num_n) == 0) np = 3;
                 const int buf = acc_iter % C::NB;
                 const uint32_t acc_phase = (acc_iter / C::NB) & 1;
                 if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort, ep.err, ERR_TIMEOUT_MMA_ACC)) { ok = false; break; }
                 tc_fence_after();
                 const int n_valid = min(C::BN, ep.N - n_blk * C::BN);
-                const uint32_t id_lo = idesc_i8(false, true, n_valid);
+                const uint32_t id_lo = idesc_i8(ep.a_sd != 0, true, n_valid);  // low planes u8, or signed digits
                 const uint32_t id_hi = idesc_i8(true, true, n_valid);
                 const uint32_t dbase = tmem_base + buf * C::ACC_COLS;
                 for (int kb = 0; kb < KB; ++kb) {
@@ -719,6 +756,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
                         const uint64_t bdesc = smem_desc_sw128(sB + ks * 32);
 #pragma unroll
                         for (int p = 0; p < P; ++p) {
+                            if (p >= np) continue;
                             // row-blocked A: 16-byte K chunks 2 KB apart, 8-row groups 128 bytes apart
                             const uint64_t adesc = ep.a_blocked ? smem_desc_noswz(sA + p * C::A_BYTES + ks * 4096, 2048, 128)
                                                                 : smem_desc_sw128(sA + p * C::A_BYTES + ks * 32);

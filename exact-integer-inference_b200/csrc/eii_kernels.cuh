@@ -107,12 +107,15 @@ __device__ __forceinline__ int64_t half_sum64(int64_t v) {
 
 __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain, int shift_out,
                           int bits_out, uint8_t* __restrict__ planes, int P, int64_t* __restrict__ out64,
-                          int64_t* __restrict__ u_out, int64_t* __restrict__ z_out) {
+                          int64_t* __restrict__ u_out, int64_t* __restrict__ z_out, uint32_t* __restrict__ zero_ptr,
+                          int zero_n) {
     const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
     const int l = threadIdx.x & 15;
     const bool live = row < M;
     griddep_wait();
     griddep_launch();
+    if (zero_ptr && blockIdx.x == 0)  // flag words the next kernels fill (signed-digit gated planes)
+        for (int i = threadIdx.x; i < zero_n; i += blockDim.x) zero_ptr[i] = 0;
     const int4* xr = reinterpret_cast<const int4*>(x + static_cast<int64_t>(live ? row : 0) * D_MODEL);
     int4 v[9];
     int64_t A = 0, B = 0, C = 0;

@@ -345,3 +345,15 @@ def test_narrow_modes_match_reference(base_model_path, wide, nres):
         M.close()
     assert lg[0, :8].tolist() == want["logits_row0_first8"]
     assert sha256_arr(lg, np.int64) == want["logits_int64_sha256"]
+
+
+def test_forward_t24_unsigned_gated_planes(base_model, base_model_path, monkeypatch):
+    """The down GEMM on the plain gated byte planes (EII_NO_SD: no signed digits, all four planes
+    every tile) gives the same integers as the signed-digit planes with the top plane skipped."""
+    import _eii
+    monkeypatch.setenv("EII_NO_SD", "1")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        _check_set(e, base_model, "t24")
+    finally:
+        e.close()
