@@ -277,11 +277,12 @@ __device__ __forceinline__ void gateup_lean(const uint32_t (&vg)[P][N], const ui
         const int32_t a = min(g, -g);
         int32_t sg = a >= lo_g ? static_cast<int32_t>(tab[a - lo_g]) : 0;
         if (g > 0) sg = min(max(sg + (g << d), -32768), 32767);
+        // |sg u| <= 2^30 and 2^(gs-1) <= 2^30, so RS(sg u, gs) lies in [-2^30, 2^30]: it fits int32 and
+        // SAT32 never applies; SAT16 is a clamp of that int32
         const int64_t prod = static_cast<int64_t>(sg) * u + grnd;
-        int32_t hi;
-        uint32_t lo;
-        shr31(prod, gs, hi, lo);  // also right for gs == 0 (a funnel shift by 0 returns the low word)
-        gm[i] = sat_hl(hi, lo, BITS_M);
+        const int32_t r = static_cast<int32_t>(
+            __funnelshift_r(static_cast<uint32_t>(prod), static_cast<uint32_t>(static_cast<uint64_t>(prod) >> 32), gs));
+        gm[i] = BITS_M == 32 ? r : clamp16(r);
     }
 }
 

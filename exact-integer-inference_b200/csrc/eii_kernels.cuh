@@ -81,7 +81,11 @@ __host__ __device__ __forceinline__ int64_t norm_recip_root(int64_t A, int64_t B
     const __int128 S = static_cast<__int128>(A) * (static_cast<__int128>(1) << 32) +
                        static_cast<__int128>(B) * (static_cast<__int128>(1) << 17) + static_cast<__int128>(C);
     const unsigned __int128 Tt = static_cast<unsigned __int128>(S) + static_cast<unsigned __int128>(EPS_S);
-    double est = 1099511627776.0 / sqrt(static_cast<double>(Tt));  // 2^40 / sqrt(Tt)
+#ifdef __CUDA_ARCH__
+    double est = 1099511627776.0 * rsqrt(static_cast<double>(Tt));  // 2^40 / sqrt(Tt); the loops fix U
+#else
+    double est = 1099511627776.0 / sqrt(static_cast<double>(Tt));
+#endif
     if (est > 2147483647.0) est = 2147483647.0;
     uint64_t u = static_cast<uint64_t>(est);
     while (u > 0 && !sq_times_le_2p80(u, Tt)) --u;
