@@ -225,6 +225,7 @@ struct eii_engine {
     std::vector<void*> weights;
     std::vector<void*> workspace;
     // optional per-kernel timing (eii_profile_enable): event pairs around each launch
+    bool generic_norm = false;  // EII_NORM=generic: always the generic RMSNorm kernel
     bool force_cuda_core_attention = false;  // EII_ATTENTION=cuda_core selects the CUDA-core kernel for T <= 128
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_pool;
@@ -442,6 +443,12 @@ int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, 
                 int64_t* z_out = nullptr, uint32_t* zero_ptr = nullptr, int zero_n = 0) {
     const int rows_per_block = 16;  // 8 warps, two rows each
     ProfScope ps(e, EII_K_NORM, st);
+    // the forward pass's own case (two INT16 planes, output shift in [10, 31]) has a lean kernel
+    if (planes && P == 2 && bits == 16 && !out64 && !u_out && !z_out && shift >= 10 && shift <= 31 && !e->generic_norm) {
+        CK(launch_k(k_rmsnorm_p16, dim3((rows + rows_per_block - 1) / rows_per_block), dim3(256), 0, st, x, rows, gain,
+                    shift, planes, zero_ptr, zero_n));
+        return EII_OK;
+    }
     CK(launch_k(k_rmsnorm, dim3((rows + rows_per_block - 1) / rows_per_block), dim3(256), 0, st, x, rows, gain, shift,
                 bits, planes, P, out64, u_out, z_out, zero_ptr, zero_n));
     return EII_OK;
@@ -937,6 +944,7 @@ int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
                                               ATTN_TC_SMEM) != cudaSuccess))
         rc = fail(EII_ERR_CUDA, "attention smem attribute failed");
     if (const char* a = getenv("EII_ATTENTION")) e->force_cuda_core_attention = strcmp(a, "cuda_core") == 0;
+    if (const char* a = getenv("EII_NORM")) e->generic_norm = strcmp(a, "generic") == 0;
     if (rc != EII_OK) {
         eii_close(e);
         return rc;

@@ -227,6 +227,18 @@ def test_forward_t24_generic_requant(base_model, base_model_path, monkeypatch):
         e.close()
 
 
+def test_forward_t24_generic_norm(base_model, base_model_path, monkeypatch):
+    """The generic RMSNorm kernel (int64 outputs, any plane count and shift) and the lean two-plane
+    kernel the forward pass uses give the same integers."""
+    import _eii
+    monkeypatch.setenv("EII_NORM", "generic")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        _check_set(e, base_model, "t24")
+    finally:
+        e.close()
+
+
 def test_forward_t24_without_narrow_requant(base_model, base_model_path, monkeypatch):
     """The 32-bit requantisation with explicit 64-bit saturation tests (used when a column's bound
     does not prove that the shifted value fits int32) gives the same integers."""
