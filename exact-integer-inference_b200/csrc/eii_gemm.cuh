@@ -339,12 +339,9 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
 #pragma unroll 1
         for (int h8 = 0; h8 < 16; h8 += 8) {  // 8 dims at a time keeps the pass free of spills
             const int d0 = sub + h8;
-            uint32_t va[P][8], vb[P][8];
-            load_planes<P, 8>(tacc + 64 * hl + d0, va);
-            load_planes<P, 8>(tacc + 64 * hl + 32 + d0, vb);
-            if (!row_ok) continue;
+            // RoPE table rows first, so their load latency overlaps the TMEM loads
             int32_t rc[8], rsn[8];
-            if (region < 2) {
+            if (region < 2 && row_ok) {
                 const int4* cpp = reinterpret_cast<const int4*>(ep.rope_c + pos * 32 + d0);
                 const int4* spp = reinterpret_cast<const int4*>(ep.rope_s + pos * 32 + d0);
                 reinterpret_cast<int4*>(rc)[0] = __ldg(cpp);
@@ -352,6 +349,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 reinterpret_cast<int4*>(rsn)[0] = __ldg(spp);
                 reinterpret_cast<int4*>(rsn)[1] = __ldg(spp + 1);
             }
+            uint32_t va[P][8], vb[P][8];
+            load_planes<P, 8>(tacc + 64 * hl + d0, va);
+            load_planes<P, 8>(tacc + 64 * hl + 32 + d0, vb);
+            if (!row_ok) continue;
             int16_t oa[8], ob[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
