@@ -209,15 +209,21 @@ def cpu_baseline_from_gpu(eng, model_bin, workdir, seconds_hint=30):
 
 
 # ------------------------------------------------------------------------------------ roofline
-def roofline(prof, rows_per_launch, peaks):
-    """Dominant kernel (most device time in the profiled step) against its roofline."""
+def roofline(prof, rows_total, peaks):
+    """Dominant kernel (most device time in the profiled step) against its roofline.  The work per
+    launch is the step's total work of that kernel over its launch count (chunks may differ in size)."""
     name, (ms, n) = max(prof.items(), key=lambda kv: kv[1][0])
     per_launch_s = ms / n / 1e3
-    r = rows_per_launch
-    macs = {"gemm_gateup_silu": r * 3072 * 576, "gemm_qkv_rope": r * 960 * 576, "gemm_o_resid": r * 576 * 576,
-            "gemm_down_resid": r * 576 * 1536, "gemm_logits": r * VOCAB * 576,
-            "attention": (r // T) * 9 * 64 * 2 * (T * (T + 1) // 2)}
-    bytes_ = {"rmsnorm": r * D * 4 + r * D * 2, "embed": r * D * 5}
+    L = 30  # layers: one launch of each layer kernel per layer and chunk; norms 2 per layer + final
+    rows = rows_total
+    macs_total = {"gemm_gateup_silu": L * rows * 3072 * 576, "gemm_qkv_rope": L * rows * 960 * 576,
+                  "gemm_o_resid": L * rows * 576 * 576, "gemm_down_resid": L * rows * 576 * 1536,
+                  "gemm_logits": rows * VOCAB * 576,
+                  "attention": L * (rows // T) * 9 * 64 * 2 * (T * (T + 1) // 2)}
+    bytes_total = {"rmsnorm": (2 * L + 1) * rows * (D * 4 + D * 2), "embed": rows * D * 5}
+    macs = {k: v // n for k, v in macs_total.items()}
+    bytes_ = {k: v // n for k, v in bytes_total.items()}
+    r = rows * (1 if name in ("gemm_logits", "embed") else (2 * L + 1 if name == "rmsnorm" else L)) // n
     int8_peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
     if name in macs:
         achieved = 2.0 * macs[name] / per_launch_s / 1e12
@@ -230,7 +236,8 @@ def roofline(prof, rows_per_launch, peaks):
         out = {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks.get("hbm_gbs", 6650.0),
                "unit": "GB/s", "frac": round(achieved / peaks.get("hbm_gbs", 6650.0), 4), "peak_note": "of measured"}
     out["launch_us"] = round(per_launch_s * 1e6, 1)
-    out["traffic"] = traffic_for(name, rows_per_launch)
+    out["rows_per_launch"] = r
+    out["traffic"] = traffic_for(name, r)
     return out
 
 
@@ -378,7 +385,7 @@ def run_ours(args):
     prof = {k: v for k, v in eng.profile_read().items() if v[1] > 0}
     eng.profile_enable(False)
     launches_per_step = sum(v[1] for v in prof.values())
-    chunk_rows = max(1, int(os.environ.get("EII_CHUNK_ROWS", "16384")) // T) * T
+    chunk_rows = eng.chunk_sequences(ns, T) * T
     decode = decode_bench(eng, ids_host, ids_dev, ns, digests, stream, barrier, max_over_ranks)
     counts = torch.tensor([checked, exact, digest_match], dtype=torch.int64, device="cuda")
     all_dig = torch.from_numpy(dig_host.view(np.int64).copy()).cuda()
@@ -405,7 +412,7 @@ def run_ours(args):
                     "d2h_bytes_per_step": int(N_SEQ * 8),
                     "path": "eii_forward (C ABI) with pinned host ids, per-sequence digests read back"},
             "gpu_launches": int(launches_per_step * args.steps),
-            "roofline": roofline(prof, min(chunk_rows, rows), peaks),
+            "roofline": roofline(prof, rows, peaks),
             "clocks": clocks,
             "check": {"subset_sequences": int(counts[0]), "subset_exact": int(counts[1]),
                       "digests_device_eq_host_ranks": int(counts[2]),

@@ -42,6 +42,7 @@ _SIGS = {
     "eii_logits": ([_P, _P, ctypes.c_int, _P], ctypes.c_int),
     "eii_kernel_name": ([ctypes.c_int], ctypes.c_char_p),
     "eii_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
+    "eii_chunk_sequences": ([_P, ctypes.c_int, ctypes.c_int], ctypes.c_int),
     "eii_profile_read": ([_P, ctypes.c_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)],
                          ctypes.c_int),
     "eii_linear": ([_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
@@ -154,6 +155,13 @@ class Engine:
                                        ctypes.c_void_p(logits_ptr) if logits_ptr else None, ld,
                                        ctypes.c_void_p(digests_ptr) if digests_ptr else None,
                                        ctypes.c_void_p(stream) if stream else None))
+
+    def chunk_sequences(self, n_seq, T):
+        """Sequences per chunk of the engine's workspace for a forward of n_seq x T tokens."""
+        cs = lib().eii_chunk_sequences(self.h, n_seq, T)
+        if cs < 0:
+            check(-cs)
+        return cs
 
     def profile_enable(self, on=True):
         check(lib().eii_profile_enable(self.h, 1 if on else 0))

@@ -625,15 +625,17 @@ int check_device_error(eii_engine* e, cudaStream_t st) {
     return EII_OK;
 }
 
-int default_chunk_rows() {
+// Sequences per chunk: about EII_CHUNK_ROWS rows (default 16384).  Without the variable the count is
+// rounded to a multiple of the SM count once it reaches half of it: the attention runs one CTA per
+// (sequence, KV group) at one CTA per SM, so 3 x 148 k CTAs fill whole waves (128 sequences of 128
+// tokens took three waves for 2.6 waves of work), and the persistent GEMMs get 148 k row blocks.
+int chunk_seqs_for(const eii_engine* e, int n_seq, int T) {
     const char* s = getenv("EII_CHUNK_ROWS");
-    int v = s ? atoi(s) : 0;
-    return v > 0 ? v : 16384;
-}
-
-int chunk_seqs_for(int n_seq, int T) {
-    int cs = default_chunk_rows() / T;
+    const int v = s ? atoi(s) : 0;
+    int cs = (v > 0 ? v : 16384) / T;
     if (cs < 1) cs = 1;
+    const int sms = e->num_sms > 0 ? e->num_sms : 1;
+    if (v <= 0 && cs >= sms / 2) cs = ((cs + sms / 2) / sms) * sms;
     if (cs > n_seq) cs = n_seq;
     return cs;
 }
@@ -982,7 +984,7 @@ int forward_host(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* e
     TRY(check_ids_host(ids, (int64_t)n_seq * T));
     CK(cudaSetDevice(e->device));
     cudaStream_t st = e->stream;
-    const int cs = chunk_seqs_for(n_seq, T);
+    const int cs = chunk_seqs_for(e, n_seq, T);
     TRY(ensure_rows(e, cs * T));
     TRY(ensure_ids(e, (int64_t)cs * T));
     if (logits_out || digests) TRY(ensure_logits_ws(e, cs * T));
@@ -1040,7 +1042,7 @@ int forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int3
         return fail(EII_ERR_ARG, "logits_dev must be 16-byte aligned with ld >= %d, ld %% 4 == 0", VOCAB);
     CK(cudaSetDevice(e->device));
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
-    const int cs = chunk_seqs_for(n_seq, T);
+    const int cs = chunk_seqs_for(e, n_seq, T);
     TRY(ensure_rows(e, cs * T));
     if (!logits_dev && digests_dev) TRY(ensure_logits_ws(e, cs * T));
     if (digests_dev) CK(cudaMemsetAsync(digests_dev, 0, sizeof(uint64_t) * n_seq, st));
@@ -1076,6 +1078,12 @@ const char* eii_kernel_name(int kind) {
                                                      "gemm_gateup_silu", "gemm_down_resid", "gemm_logits", "digest",
                                                      "gemm_linear"};
     return (kind >= 0 && kind < EII_NUM_KERNEL_KINDS) ? names[kind] : "";
+}
+
+int eii_chunk_sequences(const eii_engine* e, int n_seq, int T) {
+    if (!e) return -fail(EII_ERR_ARG, "engine is null");
+    if (n_seq < 1 || T < 1) return -fail(EII_ERR_ARG, "n_seq and T must be positive");
+    return chunk_seqs_for(e, n_seq, T);
 }
 
 int eii_profile_enable(eii_engine* e, int on) {
