@@ -6,10 +6,15 @@
 //   S  = Q K^T  as three int32 TMEM accumulators over the 64-dim head:
 //        D0 = q0.k0, D1 = q1.k0 + q0.k1, D2 = q1.k1      (q0,k0 u8 low bytes, q1,k1 s8 top bytes)
 //        S = 65536 D2 + 256 D1 + D0 exactly (|partial sums| <= 64 * 255 * 255 < 2^31).
-//   softmax per query row (one thread per row), exactly as python/intref.py:239-246:
-//        s = SAT16(RS(S, shift_s)) for j <= i, rowmax, e = E[rowmax - s] (0 beyond DMAX),
-//        Z = sum e, P = floor((e 65536 + floor(Z/2)) / Z) in [0, 65536]; the division by the
-//        row-invariant Z is a double estimate corrected with integer remainders.
+//   scores: each warp reads its TMEM lane quadrant (32 query rows) and 32-key block and writes
+//        s = SAT16(RS(S, shift_s)) as int16 into a shared score tile (rows padded to 288 bytes);
+//   softmax per query row, four threads per row (exactly as python/intref.py:239-246):
+//        rowmax over j <= i, e = E[rowmax - s] (0 beyond DMAX), Z = sum e, both reduced with two
+//        shuffles inside the row's thread quad, P = floor((e 65536 + floor(Z/2)) / Z) in [0, 65536]
+//        (an fp32 estimate of the quotient corrected with the integer remainder).  A row's keys
+//        are split into groups of four taken round-robin by its four threads, and warp w holds
+//        rows 8w .. 8w + 7, so every SM sub-partition (warps w = s mod 4) gets one warp of each
+//        32-row query block and the causal work is balanced without block-wide reductions.
 //        P = 65536 * [P == 65536] + 256 p1 + p0; the two low bytes are written as u8 planes and
 //        the (at most one) P == 65536 key of a row is added back in the epilogue.
 //   ctx = P V   as three TMEM accumulators over the T keys (V transposed, K-major):
@@ -28,9 +33,12 @@ namespace eii {
 
 constexpr int ATTN_TC_THREADS = 512;   // 16 warps: warp w owns TMEM lane quadrant w % 4 and key/dim block w / 4
 constexpr int ATTN_TC_TILE = 128 * 128;  // one 128 x 128-byte swizzled tile
-// smem: Q (3 tiles) | K (1) | V^T planes (2 x 64 rows x 128 B = 1 tile) | P planes (2 tiles) | E |
-//       row max [4][128] int32 | row sum [4][128] int64 | j* [128] int32 | barrier, TMEM slot, abort
-constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + (DMAX + 1 + 3) * 4 + 4 * 128 * 4 + 4 * 128 * 8 + 128 * 4 + 64;
+// Score tile row pitch: 144 int16 (288 bytes = 72 words, 8 mod 32), so the four rows a half-warp
+// reads with 8-byte loads start 8 banks apart.
+constexpr int ATTN_SS_PITCH = 144;
+// smem: Q (3 tiles) | K (1) | V^T planes (2 x 64 rows x 128 B = 1 tile) | P planes (2 tiles) |
+//       scores [128][144] int16 | E | j* [128] int32 | barrier, TMEM slot, abort
+constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + 128 * ATTN_SS_PITCH * 2 + (DMAX + 1 + 3) * 4 + 128 * 4 + 64;
 
 // Byte offset of byte b of row r inside a 128-byte-row tile with the 128-byte swizzle.
 __device__ __forceinline__ int sw128(int r, int b) { return r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15); }
@@ -67,10 +75,9 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     uint8_t* Ks = sm + 3 * ATTN_TC_TILE;    // row j = [k0 | k1]
     uint8_t* VT = sm + 4 * ATTN_TC_TILE;    // plane p at VT + p * 8192: row d, byte j
     uint8_t* Ps = sm + 5 * ATTN_TC_TILE;    // plane p at Ps + p * ATTN_TC_TILE: row i, byte j
-    int32_t* E = reinterpret_cast<int32_t*>(sm + 7 * ATTN_TC_TILE);
-    int32_t* red_max = E + DMAX + 1 + 3;                                  // [4][128]
-    int64_t* red_z = reinterpret_cast<int64_t*>(red_max + 4 * 128);      // [4][128]
-    int32_t* jstar_s = reinterpret_cast<int32_t*>(red_z + 4 * 128);      // [128]
+    int16_t* Ss = reinterpret_cast<int16_t*>(sm + 7 * ATTN_TC_TILE);   // [128][ATTN_SS_PITCH]
+    int32_t* E = reinterpret_cast<int32_t*>(Ss + 128 * ATTN_SS_PITCH);
+    int32_t* jstar_s = E + DMAX + 1 + 3;                                  // [128]
     uint64_t* bar = reinterpret_cast<uint64_t*>(jstar_s + 128);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -151,7 +158,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     // the causal mask, and each tile waits for its slowest quadrant, so the three tiles cost 4, 3
     // and 2 key blocks instead of 4 each with one head per tile.
     bool active = false;
-    const bool fast = ap.shift_s >= 1 && ap.shift_s <= 31;
+    const bool fast = ap.shift_s >= 8 && ap.shift_s <= 31;  // 32-bit score path (see the score pass)
     const int64_t srnd = fast ? (int64_t(1) << (ap.shift_s - 1)) : 0;
 
     for (int h = 0; h < 3; ++h) {  // h = packed tile
@@ -177,9 +184,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
         phase ^= 1;
         tc_fence_after();
 
-        // ---- pass 1: scores of my 32 keys, partial row max
-        uint32_t sp[16];  // s_j as int16 pairs, j = 32 kb + 0..31
-        int32_t lmax = INT32_MIN;
+        // ---- scores of my 32-key block for my quadrant's rows -> the shared score tile
         if (active) {
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
@@ -190,79 +195,88 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                 tmem_ld16(tq + 256 + col, d2);
                 tmem_wait_ld();
                 tmem_launder(d0); tmem_launder(d1); tmem_launder(d2);
+                uint32_t sp[8];  // s as int16 pairs
 #pragma unroll
                 for (int q = 0; q < 16; q += 2) {
                     int32_t s2[2];
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
+                        const int32_t a0 = static_cast<int32_t>(d0[q + u]), a1 = static_cast<int32_t>(d1[q + u]),
+                                      a2 = static_cast<int32_t>(d2[q + u]);
                         if (fast) {
-                            // S + 2^(shift-1) from the three plane sums with 32x32 -> 64 multiply-adds
-                            const int64_t t = static_cast<int64_t>(static_cast<int32_t>(d2[q + u])) * 65536 +
-                                              (static_cast<int64_t>(static_cast<int32_t>(d1[q + u])) * 256 +
-                                               (static_cast<int64_t>(static_cast<int32_t>(d0[q + u])) + srnd));
-                            const uint32_t tl = static_cast<uint32_t>(t), th = static_cast<uint32_t>(static_cast<uint64_t>(t) >> 32);
-                            const uint32_t lo = __funnelshift_r(tl, th, ap.shift_s);
-                            const int32_t hi = static_cast<int32_t>(th) >> ap.shift_s;
-                            const int32_t w = hi == (static_cast<int32_t>(lo) >> 31) ? static_cast<int32_t>(lo)
-                                                                                     : (hi < 0 ? INT32_MIN : INT32_MAX);
-                            s2[u] = min(max(w, -32768), 32767);
+                            // S + 2^(sh-1) = 2^8 (2^8 a2 + a1 + ((a0 + 2^(sh-1)) >> 8)) + ((a0 + 2^(sh-1)) & 255),
+                            // so RS(S, sh) = (2^8 a2 + a1 + ((a0 + 2^(sh-1)) >> 8)) >> (sh - 8): every term
+                            // fits int32 (|a0| < 2^22, |a1| < 2^22, |a2| <= 2^20, 2^(sh-1) <= 2^30)
+                            const int32_t t = a2 * 256 + a1 + ((a0 + static_cast<int32_t>(srnd)) >> 8);
+                            s2[u] = min(max(t >> (ap.shift_s - 8), -32768), 32767);
                         } else {
-                            const int64_t S = static_cast<int64_t>(static_cast<int32_t>(d2[q + u])) * 65536 +
-                                              static_cast<int64_t>(static_cast<int32_t>(d1[q + u])) * 256 +
-                                              static_cast<int64_t>(static_cast<int32_t>(d0[q + u]));
+                            const int64_t S = static_cast<int64_t>(a2) * 65536 + static_cast<int64_t>(a1) * 256 +
+                                              static_cast<int64_t>(a0);
                             s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
                         }
-                        if (col + q + u <= pos) lmax = max(lmax, s2[u]);
                     }
-                    sp[(c * 16 + q) / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
+                    sp[q / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
                 }
+                uint4* dst = reinterpret_cast<uint4*>(Ss + i * ATTN_SS_PITCH + col);
+                dst[0] = make_uint4(sp[0], sp[1], sp[2], sp[3]);
+                dst[1] = make_uint4(sp[4], sp[5], sp[6], sp[7]);
             }
         }
-        red_max[kb * 128 + i] = lmax;
         __syncthreads();
-        int32_t rowmax = red_max[i];
-#pragma unroll
-        for (int b = 1; b < 4; ++b) rowmax = max(rowmax, red_max[b * 128 + i]);
 
-        // ---- pass 2: partial Z
-        int64_t lz = 0;
-        if (active) {
-#pragma unroll
-            for (int q = 0; q < 32; ++q) {
-                const int j = kb * 32 + q;
-                const int32_t s = static_cast<int16_t>((q & 1) ? (sp[q / 2] >> 16) : (sp[q / 2] & 0xFFFF));
-                const int32_t dd = rowmax - s;
-                if (j <= pos && dd <= DMAX) lz += E[dd];
-            }
-        }
-        red_z[kb * 128 + i] = lz;
-        __syncthreads();
-        const int64_t Z = red_z[i] + red_z[128 + i] + red_z[256 + i] + red_z[384 + i];
-
-        // ---- pass 3: probabilities of my keys -> u8 planes of P mod 65536 (+ the P == 65536 key)
+        // ---- softmax of tile row r by threads 4 r .. 4 r + 3: thread jq takes key groups g = jq + 4 m
+        // (keys 4 g .. 4 g + 3), m = 0 .. 7; rows past T or keys past the row's position get P = 0
         {
-            const int64_t halfZ = Z / 2;
-            const float scale = Z > 0 ? static_cast<float>(65536.0 / static_cast<double>(Z)) : 0.f;
+            const int r = tid >> 2, jq = tid & 3;
+            const int rslot = 4 * h + (r >> 5);
+            const int rpos = 32 * (3 - rslot / 3) + (r & 31);
+            const int nk = rpos < T ? rpos + 1 : 0;  // live keys of this row
+            const int16_t* srow = Ss + r * ATTN_SS_PITCH;
+            uint2 sv[8];
+            int32_t mx = -32768;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint8_t b0[16], b1[16];
+            for (int m = 0; m < 8; ++m) {
+                const int k0 = 4 * (jq + 4 * m);
+                sv[m] = k0 < nk ? *reinterpret_cast<const uint2*>(srow + k0) : make_uint2(0, 0);
 #pragma unroll
-                for (int q = 0; q < 16; ++q) {
-                    const int qq = c * 16 + q;
-                    const int j = kb * 32 + qq;
-                    int64_t p = 0;
-                    if (active && pos < T) {
-                        const int32_t s = static_cast<int16_t>((qq & 1) ? (sp[qq / 2] >> 16) : (sp[qq / 2] & 0xFFFF));
-                        const int32_t dd = rowmax - s;
-                        if (j <= pos && dd <= DMAX) p = prob_q16_f32(E[dd], Z, halfZ, scale);
-                    }
-                    if (p == 65536) jstar_s[i] = j;
-                    b0[q] = static_cast<uint8_t>(p & 0xFF);
-                    b1[q] = static_cast<uint8_t>((p >> 8) & 0xFF);
+                for (int u = 0; u < 4; ++u) {
+                    const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
+                    if (k0 + u < nk) mx = max(mx, sk);
                 }
-                const int byte = kb * 32 + c * 16;
-                *reinterpret_cast<uint4*>(Ps + sw128(i, byte)) = *reinterpret_cast<uint4*>(b0);
-                *reinterpret_cast<uint4*>(Ps + ATTN_TC_TILE + sw128(i, byte)) = *reinterpret_cast<uint4*>(b1);
+            }
+            mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            int64_t z = 0;
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int k0 = 4 * (jq + 4 * m);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
+                    const int32_t dd = mx - sk;
+                    if (k0 + u < nk && dd <= DMAX) z += E[dd];
+                }
+            }
+            z += __shfl_xor_sync(0xffffffffu, z, 1);
+            z += __shfl_xor_sync(0xffffffffu, z, 2);
+            const int64_t halfZ = z / 2;
+            const float scale = z > 0 ? static_cast<float>(65536.0 / static_cast<double>(z)) : 0.f;
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int g = jq + 4 * m, k0 = 4 * g;
+                uint32_t b0 = 0, b1 = 0;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
+                    const int32_t dd = mx - sk;
+                    int32_t p = 0;
+                    if (k0 + u < nk && dd <= DMAX) p = prob_q16_f32(E[dd], z, halfZ, scale);
+                    if (p == 65536) jstar_s[r] = k0 + u;
+                    b0 |= static_cast<uint32_t>(p & 0xFF) << (8 * u);
+                    b1 |= static_cast<uint32_t>((p >> 8) & 0xFF) << (8 * u);
+                }
+                *reinterpret_cast<uint32_t*>(Ps + sw128(r, k0)) = b0;
+                *reinterpret_cast<uint32_t*>(Ps + ATTN_TC_TILE + sw128(r, k0)) = b1;
             }
         }
         fence_async_smem();
