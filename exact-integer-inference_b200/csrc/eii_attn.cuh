@@ -95,26 +95,42 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     griddep_wait();  // q, k, v are the previous kernel's output
     griddep_launch();
 
-    // ---- stage K, Q (3 heads) and V^T as byte planes; rows/keys >= T are zero
-    for (int idx = tid; idx < 128 * 4 * 4; idx += ATTN_TC_THREADS) {
+    // ---- stage K, Q (3 heads) and V^T as byte planes; rows/keys >= T are zero.  Every global load of
+    // the staging is issued before the first shared-memory store, so their latencies overlap.
+    constexpr int QK_ITERS = 128 * 4 * 4 / ATTN_TC_THREADS;  // 32-byte pieces per thread
+    int4 qka[QK_ITERS], qkb[QK_ITERS], va = make_int4(0, 0, 0, 0), vb = make_int4(0, 0, 0, 0);
+#pragma unroll
+    for (int it = 0; it < QK_ITERS; ++it) {
+        const int idx = tid + it * ATTN_TC_THREADS;
         const int r = idx / 16, c = (idx / 4) % 4, which = idx % 4;  // which: 0..2 = q head, 3 = k
-        uint8_t lo[16], hi[16];
+        qka[it] = qkb[it] = make_int4(0, 0, 0, 0);
         if (r < T) {
             const int16_t* src = which < 3 ? ap.q + (row0 + r) * D_MODEL + (g * 3 + which) * 64 + c * 16
                                            : ap.k + (row0 + r) * 192 + g * 64 + c * 16;
-            const int4 a = reinterpret_cast<const int4*>(src)[0], b = reinterpret_cast<const int4*>(src)[1];
-            const int16_t* v = reinterpret_cast<const int16_t*>(&a);
-            const int16_t* w = reinterpret_cast<const int16_t*>(&b);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                lo[u] = static_cast<uint8_t>(v[u] & 0xFF); hi[u] = static_cast<uint8_t>((v[u] >> 8) & 0xFF);
-                lo[8 + u] = static_cast<uint8_t>(w[u] & 0xFF); hi[8 + u] = static_cast<uint8_t>((w[u] >> 8) & 0xFF);
-            }
-        } else {
-#pragma unroll
-            for (int u = 0; u < 16; ++u) lo[u] = hi[u] = 0;
+            qka[it] = reinterpret_cast<const int4*>(src)[0];
+            qkb[it] = reinterpret_cast<const int4*>(src)[1];
         }
-        // q rows go to their packed tile slot (see pack_slot below); k rows to the K tile
+    }
+    const int vj = tid & 127, vdq = tid >> 7;  // V^T: thread (key, dim quarter)
+    if (vj < T) {
+        const int4* src = reinterpret_cast<const int4*>(ap.v + (row0 + vj) * 192 + g * 64 + vdq * 16);
+        va = src[0];
+        vb = src[1];
+    }
+#pragma unroll
+    for (int it = 0; it < QK_ITERS; ++it) {
+        const int idx = tid + it * ATTN_TC_THREADS;
+        const int r = idx / 16, c = (idx / 4) % 4, which = idx % 4;
+        // low bytes of the 16 values (bytes 0 and 2 of each word) and high bytes (1 and 3)
+        const uint32_t w[8] = {static_cast<uint32_t>(qka[it].x), static_cast<uint32_t>(qka[it].y),
+                               static_cast<uint32_t>(qka[it].z), static_cast<uint32_t>(qka[it].w),
+                               static_cast<uint32_t>(qkb[it].x), static_cast<uint32_t>(qkb[it].y),
+                               static_cast<uint32_t>(qkb[it].z), static_cast<uint32_t>(qkb[it].w)};
+        const uint4 lo = make_uint4(__byte_perm(w[0], w[1], 0x6420), __byte_perm(w[2], w[3], 0x6420),
+                                    __byte_perm(w[4], w[5], 0x6420), __byte_perm(w[6], w[7], 0x6420));
+        const uint4 hi = make_uint4(__byte_perm(w[0], w[1], 0x7531), __byte_perm(w[2], w[3], 0x7531),
+                                    __byte_perm(w[4], w[5], 0x7531), __byte_perm(w[6], w[7], 0x7531));
+        // q rows go to their packed tile slot (see the tile loop); k rows to the K tile
         uint8_t* tile = Ks;
         int tr = r;
         if (which < 3) {
@@ -122,24 +138,17 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
             tile = Qs + (sl / 4) * ATTN_TC_TILE;
             tr = (sl % 4) * 32 + r % 32;
         }
-        *reinterpret_cast<uint4*>(tile + sw128(tr, c * 16)) = *reinterpret_cast<uint4*>(lo);
-        *reinterpret_cast<uint4*>(tile + sw128(tr, 64 + c * 16)) = *reinterpret_cast<uint4*>(hi);
+        *reinterpret_cast<uint4*>(tile + sw128(tr, c * 16)) = lo;
+        *reinterpret_cast<uint4*>(tile + sw128(tr, 64 + c * 16)) = hi;
     }
-    {   // V^T: thread (j, dim quarter) scatters key j's 16 values into column j of both planes
-        const int j = tid & 127, dq = tid >> 7;
-        int16_t v[16];
-        if (j < T) {
-            const int4* src = reinterpret_cast<const int4*>(ap.v + (row0 + j) * 192 + g * 64 + dq * 16);
-            *reinterpret_cast<int4*>(&v[0]) = src[0];
-            *reinterpret_cast<int4*>(&v[8]) = src[1];
-        } else {
-#pragma unroll
-            for (int d = 0; d < 16; ++d) v[d] = 0;
-        }
+    {   // V^T: key vj's 16 values go into column vj of both planes
+        const int16_t* v = reinterpret_cast<const int16_t*>(&va);
+        const int16_t* v2 = reinterpret_cast<const int16_t*>(&vb);
 #pragma unroll
         for (int d = 0; d < 16; ++d) {
-            VT[sw128(dq * 16 + d, j)] = static_cast<uint8_t>(v[d] & 0xFF);
-            VT[8192 + sw128(dq * 16 + d, j)] = static_cast<uint8_t>((v[d] >> 8) & 0xFF);
+            const int16_t x = d < 8 ? v[d] : v2[d - 8];
+            VT[sw128(vdq * 16 + d, vj)] = static_cast<uint8_t>(x & 0xFF);
+            VT[8192 + sw128(vdq * 16 + d, vj)] = static_cast<uint8_t>((x >> 8) & 0xFF);
         }
     }
     fence_async_smem();
