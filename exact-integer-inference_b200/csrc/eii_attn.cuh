@@ -241,12 +241,16 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
             const int rpos = 32 * (3 - rslot / 3) + (r & 31);
             const int nk = rpos < T ? rpos + 1 : 0;  // live keys of this row
             const int16_t* srow = Ss + r * ATTN_SS_PITCH;
+            // a thread's key groups ascend with m, so the live ones are m < nm (branches, not predicates:
+            // the unrolled division would otherwise run for every key of the row's 128)
+            const int nm = nk > 4 * jq ? (nk - 4 * jq + 15) / 16 : 0;
             uint2 sv[8];
             int32_t mx = -32768;
 #pragma unroll
             for (int m = 0; m < 8; ++m) {
+                if (m >= nm) break;
                 const int k0 = 4 * (jq + 4 * m);
-                sv[m] = k0 < nk ? *reinterpret_cast<const uint2*>(srow + k0) : make_uint2(0, 0);
+                sv[m] = *reinterpret_cast<const uint2*>(srow + k0);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
@@ -258,6 +262,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
             int64_t z = 0;
 #pragma unroll
             for (int m = 0; m < 8; ++m) {
+                if (m >= nm) break;
                 const int k0 = 4 * (jq + 4 * m);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
@@ -272,17 +277,19 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
             const float scale = z > 0 ? static_cast<float>(65536.0 / static_cast<double>(z)) : 0.f;
 #pragma unroll
             for (int m = 0; m < 8; ++m) {
-                const int g = jq + 4 * m, k0 = 4 * g;
+                const int k0 = 4 * (jq + 4 * m);
                 uint32_t b0 = 0, b1 = 0;
+                if (m < nm) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
-                    const int32_t dd = mx - sk;
-                    int32_t p = 0;
-                    if (k0 + u < nk && dd <= DMAX) p = prob_q16_f32(E[dd], z, halfZ, scale);
-                    if (p == 65536) jstar_s[r] = k0 + u;
-                    b0 |= static_cast<uint32_t>(p & 0xFF) << (8 * u);
-                    b1 |= static_cast<uint32_t>((p >> 8) & 0xFF) << (8 * u);
+                    for (int u = 0; u < 4; ++u) {
+                        const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
+                        const int32_t dd = mx - sk;
+                        int32_t p = 0;
+                        if (k0 + u < nk && dd <= DMAX) p = prob_q16_f32(E[dd], z, halfZ, scale);
+                        if (p == 65536) jstar_s[r] = k0 + u;
+                        b0 |= static_cast<uint32_t>(p & 0xFF) << (8 * u);
+                        b1 |= static_cast<uint32_t>((p >> 8) & 0xFF) << (8 * u);
+                    }
                 }
                 *reinterpret_cast<uint32_t*>(Ps + sw128(r, k0)) = b0;
                 *reinterpret_cast<uint32_t*>(Ps + ATTN_TC_TILE + sw128(r, k0)) = b1;
