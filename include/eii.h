@@ -199,7 +199,7 @@ int eii_profile_read(eii_engine* e, int kind, double* total_ms, int64_t* launche
 
 /* Sequences per chunk that eii_forward / eii_forward_device use for n_seq sequences of T tokens
  * (the engine works through the sequences in chunks of its device workspace).  A chunk holds about
- * EII_CHUNK_ROWS rows (environment, default 16384); unless that variable is set, the sequence count
+ * EII_CHUNK_ROWS rows (environment, default 65536); unless that variable is set, the sequence count
  * is rounded to a multiple of the device's SM count when it is at least half of it, so that the
  * attention (one CTA per sequence and KV group) runs in whole waves and the persistent GEMMs give
  * every SM the same number of tiles.  Returns the count, or minus an error code for a null engine
