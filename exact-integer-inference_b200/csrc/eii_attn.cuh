@@ -78,8 +78,8 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     int16_t* Ss = reinterpret_cast<int16_t*>(sm + 7 * ATTN_TC_TILE);   // [128][ATTN_SS_PITCH]
     int32_t* E = reinterpret_cast<int32_t*>(Ss + 128 * ATTN_SS_PITCH);
     int32_t* jstar_s = E + DMAX + 1 + 3;                                  // [128]
-    uint64_t* bar = reinterpret_cast<uint64_t*>(jstar_s + 128);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(jstar_s + 128);  // [0]: S = Q K^T, [1]: P V
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int T = ap.T;
@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     const int i = quad * 32 + lane;             // tile row of this thread (TMEM lane)
 
     if (warp == 0) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
-    if (tid == 0) { mbar_init(bar, 1); *abort = 0; fence_mbar_init(); }
+    if (tid == 0) { mbar_init(bar, 1); mbar_init(bar + 1, 1); *abort = 0; fence_mbar_init(); }
     for (int u = tid; u <= DMAX; u += ATTN_TC_THREADS) E[u] = ap.exp_tab[u];  // model table
     griddep_wait();  // q, k, v are the previous kernel's output
     griddep_launch();
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    uint32_t phase = 0;
+    uint32_t phase_s = 0, phase_p = 0;
     const uint32_t sK = smem_u32(Ks), sV0 = smem_u32(VT), sV1 = smem_u32(VT + 8192);
     const uint32_t sP0 = smem_u32(Ps), sP1 = smem_u32(Ps + ATTN_TC_TILE);
     // key block kb holds keys 32 kb .. 32 kb + 31; it has unmasked keys for this quadrant iff kb <= quad
@@ -170,27 +170,36 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     const bool fast = ap.shift_s >= 8 && ap.shift_s <= 31;  // 32-bit score path (see the score pass)
     const int64_t srnd = fast ? (int64_t(1) << (ap.shift_s - 1)) : 0;
 
+    // S of packed tile t covers its live key blocks only: nt = 128, 96, 64 keys for t = 0, 1, 2, with
+    // the three accumulators at TMEM columns 0, nt and 2 nt (at most 288 columns after tile 0).  P V
+    // goes to columns 320 .. 511, so the next tile's S can be computed while this tile's softmax,
+    // P V and epilogue run: it is issued as soon as this tile's scores have left TMEM.
+    constexpr uint32_t PV_COL = 320;
+    auto issue_s = [&](int t) {
+        const int nt = 128 - 32 * t;
+        const uint32_t sQ = smem_u32(Qs + t * ATTN_TC_TILE);
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+            const uint32_t qlo = sQ + ks * 32, qhi = sQ + 64 + ks * 32, klo = sK + ks * 32, khi = sK + 64 + ks * 32;
+            const uint32_t acc = ks > 0 ? 1u : 0u;
+            mma_i8(tmem + 0, smem_desc_sw128(qlo), smem_desc_sw128(klo), idesc_i8(false, false, nt), acc);
+            mma_i8(tmem + nt, smem_desc_sw128(qhi), smem_desc_sw128(klo), idesc_i8(true, false, nt), acc);
+            mma_i8(tmem + nt, smem_desc_sw128(qlo), smem_desc_sw128(khi), idesc_i8(false, true, nt), 1u);
+            mma_i8(tmem + 2 * nt, smem_desc_sw128(qhi), smem_desc_sw128(khi), idesc_i8(true, true, nt), acc);
+        }
+        tc_commit(bar);
+    };
+    if (tid == 0) issue_s(0);
+
     for (int h = 0; h < 3; ++h) {  // h = packed tile
         const int slot = 4 * h + quad, hq = slot % 3, bq = 3 - slot / 3;
         const int pos = 32 * bq + lane;  // sequence position of this thread's query row
+        const int nt = 128 - 32 * h;
         active = kb <= bq;
-        // ---- S = Q_h K^T (M = 128 queries, N = 128 keys, K = 64 dims per plane pair)
-        if (tid == 0) {
-            const uint32_t sQ = smem_u32(Qs + h * ATTN_TC_TILE);
-#pragma unroll
-            for (int ks = 0; ks < 2; ++ks) {
-                const uint32_t qlo = sQ + ks * 32, qhi = sQ + 64 + ks * 32, klo = sK + ks * 32, khi = sK + 64 + ks * 32;
-                const uint32_t acc = ks > 0 ? 1u : 0u;
-                mma_i8(tmem + 0, smem_desc_sw128(qlo), smem_desc_sw128(klo), idesc_i8(false, false, 128), acc);
-                mma_i8(tmem + 128, smem_desc_sw128(qhi), smem_desc_sw128(klo), idesc_i8(true, false, 128), acc);
-                mma_i8(tmem + 128, smem_desc_sw128(qlo), smem_desc_sw128(khi), idesc_i8(false, true, 128), 1u);
-                mma_i8(tmem + 256, smem_desc_sw128(qhi), smem_desc_sw128(khi), idesc_i8(true, true, 128), acc);
-            }
-            tc_commit(bar);
-        }
         if (tid < 128) jstar_s[tid] = -1;
-        if (!__syncthreads_and(mbar_wait(bar, phase, abort, err, ERR_TIMEOUT_ATTN))) break;
-        phase ^= 1;
+        // ---- S = Q_h K^T (M = 128 queries, N = nt keys, K = 64 dims per plane pair), issued earlier
+        if (!__syncthreads_and(mbar_wait(bar, phase_s, abort, err, ERR_TIMEOUT_ATTN))) break;
+        phase_s ^= 1;
         tc_fence_after();
 
         // ---- scores of my 32-key block for my quadrant's rows -> the shared score tile
@@ -200,8 +209,8 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                 const int col = kb * 32 + c * 16;
                 uint32_t d0[16], d1[16], d2[16];
                 tmem_ld16(tq + col, d0);
-                tmem_ld16(tq + 128 + col, d1);
-                tmem_ld16(tq + 256 + col, d2);
+                tmem_ld16(tq + nt + col, d1);
+                tmem_ld16(tq + 2 * nt + col, d2);
                 tmem_wait_ld();
                 tmem_launder(d0); tmem_launder(d1); tmem_launder(d2);
                 uint32_t sp[8];  // s as int16 pairs
@@ -231,7 +240,10 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                 dst[1] = make_uint4(sp[4], sp[5], sp[6], sp[7]);
             }
         }
+        tc_fence_before();
         __syncthreads();
+        tc_fence_after();
+        if (tid == 0 && h < 2) issue_s(h + 1);  // S columns are free again
 
         // ---- softmax of tile row r by threads 4 r .. 4 r + 3: thread jq takes key groups g = jq + 4 m
         // (keys 4 g .. 4 g + 3), m = 0 .. 7; rows past T or keys past the row's position get P = 0
@@ -300,30 +312,30 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
         __syncthreads();
         tc_fence_after();
 
-        // ---- ctx = P V (M = 128 queries, N = 64 dims, K = 128 keys); reuses the S columns
+        // ---- ctx = P V (M = 128 queries, N = 64 dims, K = 128 keys) into columns PV_COL ..
         if (tid == 0) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
                 const uint32_t acc = ks > 0 ? 1u : 0u;
                 const uint64_t p0 = smem_desc_sw128(sP0 + ks * 32), p1 = smem_desc_sw128(sP1 + ks * 32);
                 const uint64_t v0 = smem_desc_sw128(sV0 + ks * 32), v1 = smem_desc_sw128(sV1 + ks * 32);
-                mma_i8(tmem + 0, p0, v0, idesc_i8(false, false, 64), acc);
-                mma_i8(tmem + 64, p1, v0, idesc_i8(false, false, 64), acc);
-                mma_i8(tmem + 64, p0, v1, idesc_i8(false, true, 64), 1u);
-                mma_i8(tmem + 128, p1, v1, idesc_i8(false, true, 64), acc);
+                mma_i8(tmem + PV_COL, p0, v0, idesc_i8(false, false, 64), acc);
+                mma_i8(tmem + PV_COL + 64, p1, v0, idesc_i8(false, false, 64), acc);
+                mma_i8(tmem + PV_COL + 64, p0, v1, idesc_i8(false, true, 64), 1u);
+                mma_i8(tmem + PV_COL + 128, p1, v1, idesc_i8(false, true, 64), acc);
             }
-            tc_commit(bar);
+            tc_commit(bar + 1);
         }
-        if (!__syncthreads_and(mbar_wait(bar, phase, abort, err, ERR_TIMEOUT_ATTN))) break;
-        phase ^= 1;
+        if (!__syncthreads_and(mbar_wait(bar + 1, phase_p, abort, err, ERR_TIMEOUT_ATTN))) break;
+        phase_p ^= 1;
         tc_fence_after();
         {   // epilogue: rows of my quadrant, dims 16 kb .. 16 kb + 15
             const int hh = g * 3 + hq;
             const int col = kb * 16;
             uint32_t c0[16], c1[16], c2[16];
-            tmem_ld16(tq + col, c0);
-            tmem_ld16(tq + 64 + col, c1);
-            tmem_ld16(tq + 128 + col, c2);
+            tmem_ld16(tq + PV_COL + col, c0);
+            tmem_ld16(tq + PV_COL + 64 + col, c1);
+            tmem_ld16(tq + PV_COL + 128 + col, c2);
             tmem_wait_ld();
             tmem_launder(c0); tmem_launder(c1); tmem_launder(c2);
             if (pos < T) {
