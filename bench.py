@@ -466,6 +466,22 @@ def run_reference(args):
         "check": f"{exact}/{len(verdicts)} reference runs ALL STATES EXACT"}), flush=True)
 
 
+def run_probe(ns):
+    """One forward of the first `ns` config-4 sequences through eii_forward_device (logits and
+    digests on the device), for ncu captures of single launches; prints the first digest."""
+    import torch
+    import _eii
+    eng = _eii.Engine(ensure_model(), 0)
+    ids = torch.from_numpy(np.ascontiguousarray(token_table()[:ns, :T])).cuda()
+    logits = torch.empty((ns * T, VOCAB), dtype=torch.int32, device="cuda")
+    digests = torch.zeros(ns, dtype=torch.int64, device="cuda")
+    eng.forward_device(ids.data_ptr(), ns, T, logits.data_ptr(), VOCAB, digests.data_ptr(),
+                       torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    eng.close()
+    print(f"[probe] {ns} x {T} tokens, digest[0] = {int(digests[0].item()) & ((1 << 64) - 1):016x}")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -473,7 +489,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--probe", type=int, default=0, metavar="NSEQ",
+                    help="profiling target: one untimed forward of NSEQ x 128 tokens on cuda:0, then exit")
     args = ap.parse_args()
+    if args.probe:
+        run_probe(args.probe)
+        return
     if args.warmup < 3:
         log("[bench] note: fewer than 3 warm-up steps")
     if args.impl == "reference":
