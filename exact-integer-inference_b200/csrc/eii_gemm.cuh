@@ -101,6 +101,9 @@ struct EpiParams {
 };
 
 constexpr int SILU_SMEM_BYTES = 48 * 1024;  // compact SiLU table capacity (int16 x 24576 or int32 x 12288)
+// RoPE rows staged by the QKV GEMM: up to 128 positions; a 36-word pitch puts the 16-byte loads of
+// eight consecutive positions (one per lane) on distinct banks.
+constexpr int ROPE_SMEM_ROWS = 128, ROPE_SMEM_PITCH = 36;
 constexpr int SMEM_LIMIT = 227 * 1024;
 // N-tile width of the 4-plane GEMMs (down, and O at INT32 attn_ctx layers).  128 keeps their
 // operand traffic from L2 at the level of the 2-plane GEMMs (the mainloops are L2-bound) at the
@@ -131,9 +134,11 @@ struct GemmCfg {
     static constexpr int COLP_BYTES = 2 * BN * 16;  // per-tile column (m, shift, 2^(shift-1), m << 8), x2
     static constexpr int DIGW_BYTES = KIND == EPI_LOGITS ? 2 * BN * 8 : 0;  // per-tile digest column weights, x2
     static constexpr int SILU_BYTES = KIND == EPI_GATEUP ? SILU_SMEM_BYTES : 0;
+    // QKV: the RoPE cos/sin rows of positions pos0 .. pos0 + T - 1 (T <= 128), rows padded to 36 words
+    static constexpr int ROPE_BYTES = KIND == EPI_QKV ? 2 * ROPE_SMEM_ROWS * ROPE_SMEM_PITCH * 4 : 0;
     static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;  // 1024-aligned
     static constexpr int BAR_OFFSET = STG_OFFSET + EPI_WARPS * STG_BYTES;
-    static constexpr int SMEM = BAR_OFFSET + 1024 + BAR_BYTES + COLP_BYTES + DIGW_BYTES + SILU_BYTES;
+    static constexpr int SMEM = BAR_OFFSET + 1024 + BAR_BYTES + COLP_BYTES + DIGW_BYTES + SILU_BYTES + ROPE_BYTES;
     static_assert(NB >= 1, "accumulators must fit in TMEM");
     static_assert(STG_BYTES % 1024 == 0, "staging buffers are 1024-byte aligned");
     static_assert(SMEM <= SMEM_LIMIT, "shared memory budget");
@@ -330,6 +335,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
         const int rshift = region == 0 ? ep.rope_shift_q : ep.rope_shift_k;
         const CUtensorMap* omap = region == 0 ? maps.c0 : (region == 1 ? maps.c1 : maps.c2);
         const int pos = row_ok ? ep.pos0 + row % ep.T : 0;
+        const bool rope_sm = ep.T <= ROPE_SMEM_ROWS && ep.pos0 + ep.T <= 512;
         const int64_t rrnd = rshift >= 1 ? (int64_t(1) << (rshift - 1)) : 0;
         // staging: dims [sub, sub + 16) and [32 + sub, 32 + sub + 16) of the head, 32 rows each (SW32)
         uint8_t* sa = stg;
@@ -339,15 +345,25 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
 #pragma unroll 1
         for (int h8 = 0; h8 < 16; h8 += 8) {  // 8 dims at a time keeps the pass free of spills
             const int d0 = sub + h8;
-            // RoPE table rows first, so their load latency overlaps the TMEM loads
+            // RoPE table rows first, so their load latency overlaps the TMEM loads; from the rows the
+            // CTA staged in shared memory (silu_tab holds them for QKV) when T <= 128
             int32_t rc[8], rsn[8];
             if (region < 2 && row_ok) {
-                const int4* cpp = reinterpret_cast<const int4*>(ep.rope_c + pos * 32 + d0);
-                const int4* spp = reinterpret_cast<const int4*>(ep.rope_s + pos * 32 + d0);
-                reinterpret_cast<int4*>(rc)[0] = __ldg(cpp);
-                reinterpret_cast<int4*>(rc)[1] = __ldg(cpp + 1);
-                reinterpret_cast<int4*>(rsn)[0] = __ldg(spp);
-                reinterpret_cast<int4*>(rsn)[1] = __ldg(spp + 1);
+                if (rope_sm) {
+                    const int32_t* rs = static_cast<const int32_t*>(silu_tab) + (row % ep.T) * ROPE_SMEM_PITCH + d0;
+                    reinterpret_cast<int4*>(rc)[0] = reinterpret_cast<const int4*>(rs)[0];
+                    reinterpret_cast<int4*>(rc)[1] = reinterpret_cast<const int4*>(rs)[1];
+                    rs += ROPE_SMEM_ROWS * ROPE_SMEM_PITCH;
+                    reinterpret_cast<int4*>(rsn)[0] = reinterpret_cast<const int4*>(rs)[0];
+                    reinterpret_cast<int4*>(rsn)[1] = reinterpret_cast<const int4*>(rs)[1];
+                } else {
+                    const int4* cpp = reinterpret_cast<const int4*>(ep.rope_c + pos * 32 + d0);
+                    const int4* spp = reinterpret_cast<const int4*>(ep.rope_s + pos * 32 + d0);
+                    reinterpret_cast<int4*>(rc)[0] = __ldg(cpp);
+                    reinterpret_cast<int4*>(rc)[1] = __ldg(cpp + 1);
+                    reinterpret_cast<int4*>(rsn)[0] = __ldg(spp);
+                    reinterpret_cast<int4*>(rsn)[1] = __ldg(spp + 1);
+                }
             }
             uint32_t va[P][8], vb[P][8];
             load_planes<P, 8>(tacc + 64 * hl + d0, va);
@@ -788,6 +804,17 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
         uint8_t* stg = staging + e * C::STG_BYTES;
         const EpiMaps maps{&tmC0, &tmC1, &tmC2};
         uint32_t xphase = 0;
+        if constexpr (KIND == EPI_QKV) {
+            if (ep.T <= ROPE_SMEM_ROWS && ep.pos0 + ep.T <= 512) {  // stage the RoPE rows of this launch's positions
+                int32_t* rs = static_cast<int32_t*>(silu_tab);
+                for (int q = et; q < 2 * ep.T * 8; q += C::EPI_THREADS) {
+                    const int tab = q / (ep.T * 8), r = (q / 8) % ep.T, c4 = q % 8;
+                    const int32_t* src = (tab ? ep.rope_s : ep.rope_c) + (ep.pos0 + r) * 32 + c4 * 4;
+                    *reinterpret_cast<int4*>(rs + (tab * ROPE_SMEM_ROWS + r) * ROPE_SMEM_PITCH + c4 * 4) =
+                        __ldg(reinterpret_cast<const int4*>(src));
+                }
+            }
+        }
         if constexpr (KIND == EPI_GATEUP) {
             if (ep.silu_smem) {  // stage the compact SiLU table once per CTA
                 const int nbytes = ep.silu_count * (ep.silu_wide ? 4 : 2);
