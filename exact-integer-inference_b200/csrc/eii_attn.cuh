@@ -341,36 +341,54 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
             if (pos < T) {
                 const int js = jstar_s[i];
                 int32_t out[16];
-                const bool cfast = ap.shift_c >= 1 && ap.shift_c <= 31;
-                const int64_t crnd = cfast ? (int64_t(1) << (ap.shift_c - 1)) : 0;
+                if (ap.shift_c >= 8 && ap.shift_c <= 31) {
+                    // ctx + 2^(sh-1) = 2^8 (2^8 C2 + C1 + 2^8 v_j* + ((C0 + 2^(sh-1)) >> 8)) + ((C0 + 2^(sh-1)) & 255),
+                    // so RS(ctx, sh) = (...) >> (sh - 8), every term in int32: |2^8 C2| <= 2^8 * 128 * 255 * 128
+                    // < 2^30, |C1| < 2^24, |2^8 v_j*| <= 2^23, |C0| < 2^23, 2^(sh-1) <= 2^30
+                    const int32_t crnd = 1 << (ap.shift_c - 1);
+                    const int32_t lim = ap.bits_c < 32 ? (1 << (ap.bits_c - 1)) : 0;
 #pragma unroll
-                for (int q = 0; q < 16; ++q) {
-                    const int d = col + q;
-                    int64_t a = static_cast<int64_t>(static_cast<int32_t>(c2[q])) * 65536 +
-                                (static_cast<int64_t>(static_cast<int32_t>(c1[q])) * 256 +
-                                 static_cast<int64_t>(static_cast<int32_t>(c0[q])));
-                    if (js >= 0) {
-                        const int32_t vj = static_cast<int32_t>(VT[sw128(d, js)]) |
-                                           (static_cast<int32_t>(static_cast<int8_t>(VT[8192 + sw128(d, js)])) << 8);
-                        a += static_cast<int64_t>(vj) * 65536;
+                    for (int q = 0; q < 16; ++q) {
+                        const int d = col + q;
+                        int32_t t = static_cast<int32_t>(c2[q]) * 256 + static_cast<int32_t>(c1[q]) +
+                                    ((static_cast<int32_t>(c0[q]) + crnd) >> 8);
+                        if (js >= 0) {
+                            const int32_t vj = static_cast<int32_t>(VT[sw128(d, js)]) |
+                                               (static_cast<int32_t>(static_cast<int8_t>(VT[8192 + sw128(d, js)])) * 256);
+                            t += vj * 256;
+                        }
+                        int32_t r = t >> (ap.shift_c - 8);
+                        if (lim) r = min(max(r, -lim), lim - 1);
+                        out[q] = r;
                     }
-                    if (cfast) {
-                        int32_t hi;
-                        uint32_t lo;
-                        shr31(a + crnd, ap.shift_c, hi, lo);
-                        out[q] = sat_hl(hi, lo, ap.bits_c);
-                    } else {
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) {
+                        const int d = col + q;
+                        int64_t a = static_cast<int64_t>(static_cast<int32_t>(c2[q])) * 65536 +
+                                    (static_cast<int64_t>(static_cast<int32_t>(c1[q])) * 256 +
+                                     static_cast<int64_t>(static_cast<int32_t>(c0[q])));
+                        if (js >= 0) {
+                            const int32_t vj = static_cast<int32_t>(VT[sw128(d, js)]) |
+                                               (static_cast<int32_t>(static_cast<int8_t>(VT[8192 + sw128(d, js)])) << 8);
+                            a += static_cast<int64_t>(vj) * 65536;
+                        }
                         out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
                     }
                 }
                 // row-blocked planes: this warp's 32 rows x 16 dims are 512 contiguous bytes per plane
                 const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
-                uint8_t* dst = ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL);
-                for (int p = 0; p < ap.P; ++p) {
-                    uint8_t b[16];
-#pragma unroll
-                    for (int q = 0; q < 16; ++q) b[q] = static_cast<uint8_t>(static_cast<uint32_t>(out[q]) >> (8 * p));
-                    *reinterpret_cast<uint4*>(dst + p * pstride) = *reinterpret_cast<uint4*>(b);
+                uint4* dst = reinterpret_cast<uint4*>(ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL));
+                uint32_t w[4];
+                pack_plane<0, 16>(out, w);
+                dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                pack_plane<1, 16>(out, w);
+                dst[pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                if (ap.P == 4) {
+                    pack_plane<2, 16>(out, w);
+                    dst[2 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                    pack_plane<3, 16>(out, w);
+                    dst[3 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
                 }
             }
         }
