@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     // the causal mask, and each tile waits for its slowest quadrant, so the three tiles cost 4, 3
     // and 2 key blocks instead of 4 each with one head per tile.
     bool active = false;
-    const bool fast = ap.shift_s >= 8 && ap.shift_s <= 31;  // 32-bit score path (see the score pass)
+    const bool fast = !ap.generic && ap.shift_s >= 8 && ap.shift_s <= 31;  // 32-bit score path (see the score pass)
     const int64_t srnd = fast ? (int64_t(1) << (ap.shift_s - 1)) : 0;
 
     // S of packed tile t covers its live key blocks only: nt = 128, 96, 64 keys for t = 0, 1, 2, with
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
             if (pos < T) {
                 const int js = jstar_s[i];
                 int32_t out[16];
-                if (ap.shift_c >= 8 && ap.shift_c <= 31) {
+                if (!ap.generic && ap.shift_c >= 8 && ap.shift_c <= 31) {
                     // ctx + 2^(sh-1) = 2^8 (2^8 C2 + C1 + 2^8 v_j* + ((C0 + 2^(sh-1)) >> 8)) + ((C0 + 2^(sh-1)) & 255),
                     // so RS(ctx, sh) = (...) >> (sh - 8), every term in int32: |2^8 C2| <= 2^8 * 128 * 255 * 128
                     // < 2^30, |C1| < 2^24, |2^8 v_j*| <= 2^23, |C0| < 2^23, 2^(sh-1) <= 2^30

@@ -226,6 +226,7 @@ struct eii_engine {
     std::vector<void*> workspace;
     // optional per-kernel timing (eii_profile_enable): event pairs around each launch
     bool generic_norm = false;  // EII_NORM=generic: always the generic RMSNorm kernel
+    int generic_attention = 0;  // EII_ATTENTION=generic: 64-bit requantisation in the tensor-core attention
     bool force_cuda_core_attention = false;  // EII_ATTENTION=cuda_core selects the CUDA-core kernel for T <= 128
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_pool;
@@ -543,6 +544,7 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     AttnParams ap{};
     ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;
     ap.M = rows; ap.T = T; ap.shift_s = L.shift_s; ap.shift_c = L.shift_c; ap.bits_c = L.c.bits;
+    ap.generic = e->generic_attention;
     if (trh) {
         ap.score_out = trh->score;
         ap.prob_out = trh->prob;
@@ -946,7 +948,10 @@ int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
                          cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               ATTN_TC_SMEM) != cudaSuccess))
         rc = fail(EII_ERR_CUDA, "attention smem attribute failed");
-    if (const char* a = getenv("EII_ATTENTION")) e->force_cuda_core_attention = strcmp(a, "cuda_core") == 0;
+    if (const char* a = getenv("EII_ATTENTION")) {
+        e->force_cuda_core_attention = strcmp(a, "cuda_core") == 0;
+        e->generic_attention = strcmp(a, "generic") == 0;
+    }
     if (const char* a = getenv("EII_NORM")) e->generic_norm = strcmp(a, "generic") == 0;
     if (rc != EII_OK) {
         eii_close(e);

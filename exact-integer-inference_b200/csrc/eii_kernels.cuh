@@ -314,6 +314,7 @@ struct AttnParams {
     int P;
     int M, T;
     int shift_s, shift_c, bits_c;
+    int generic;  // k_attention_tc: take the 64-bit score and context requantisation for every shift (test switch)
     // optional trace outputs of k_attention (python/intref.py:249-250): [M/T][9][T][T] scores (s for
     // j <= i) and probabilities P; entries above the diagonal are left to the caller (zeroed)
     int32_t* score_out;

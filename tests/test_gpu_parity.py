@@ -227,6 +227,18 @@ def test_forward_t24_generic_requant(base_model, base_model_path, monkeypatch):
         e.close()
 
 
+def test_forward_t128_generic_attention_requant(base_model, base_model_path, monkeypatch):
+    """The tensor-core attention's 64-bit score and context requantisation (taken for shifts outside
+    [8, 31]) and its 32-bit forms give the same integers."""
+    import _eii
+    monkeypatch.setenv("EII_ATTENTION", "generic")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        _check_set(e, base_model, "t128")
+    finally:
+        e.close()
+
+
 def test_forward_t24_generic_norm(base_model, base_model_path, monkeypatch):
     """The generic RMSNorm kernel (int64 outputs, any plane count and shift) and the lean two-plane
     kernel the forward pass uses give the same integers."""
