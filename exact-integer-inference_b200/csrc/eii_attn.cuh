@@ -83,8 +83,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int T = ap.T;
-    const int seq = blockIdx.x / N_KV, g = blockIdx.x % N_KV;
-    const int64_t row0 = static_cast<int64_t>(seq) * T;
+    const int items = (ap.M / T) * N_KV;  // (sequence, KV group) pairs; CTA b takes b, b + grid, ...
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int quad = warp & 3, kb = warp >> 2;  // rows 32 quad .. +31, key block / dim block kb
     const int i = quad * 32 + lane;             // tile row of this thread (TMEM lane)
@@ -94,64 +93,6 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     for (int u = tid; u <= DMAX; u += ATTN_TC_THREADS) E[u] = ap.exp_tab[u];  // model table
     griddep_wait();  // q, k, v are the previous kernel's output
     griddep_launch();
-
-    // ---- stage K, Q (3 heads) and V^T as byte planes; rows/keys >= T are zero.  Every global load of
-    // the staging is issued before the first shared-memory store, so their latencies overlap.
-    constexpr int QK_ITERS = 128 * 4 * 4 / ATTN_TC_THREADS;  // 32-byte pieces per thread
-    int4 qka[QK_ITERS], qkb[QK_ITERS], va = make_int4(0, 0, 0, 0), vb = make_int4(0, 0, 0, 0);
-#pragma unroll
-    for (int it = 0; it < QK_ITERS; ++it) {
-        const int idx = tid + it * ATTN_TC_THREADS;
-        const int r = idx / 16, c = (idx / 4) % 4, which = idx % 4;  // which: 0..2 = q head, 3 = k
-        qka[it] = qkb[it] = make_int4(0, 0, 0, 0);
-        if (r < T) {
-            const int16_t* src = which < 3 ? ap.q + (row0 + r) * D_MODEL + (g * 3 + which) * 64 + c * 16
-                                           : ap.k + (row0 + r) * 192 + g * 64 + c * 16;
-            qka[it] = reinterpret_cast<const int4*>(src)[0];
-            qkb[it] = reinterpret_cast<const int4*>(src)[1];
-        }
-    }
-    const int vj = tid & 127, vdq = tid >> 7;  // V^T: thread (key, dim quarter)
-    if (vj < T) {
-        const int4* src = reinterpret_cast<const int4*>(ap.v + (row0 + vj) * 192 + g * 64 + vdq * 16);
-        va = src[0];
-        vb = src[1];
-    }
-#pragma unroll
-    for (int it = 0; it < QK_ITERS; ++it) {
-        const int idx = tid + it * ATTN_TC_THREADS;
-        const int r = idx / 16, c = (idx / 4) % 4, which = idx % 4;
-        // low bytes of the 16 values (bytes 0 and 2 of each word) and high bytes (1 and 3)
-        const uint32_t w[8] = {static_cast<uint32_t>(qka[it].x), static_cast<uint32_t>(qka[it].y),
-                               static_cast<uint32_t>(qka[it].z), static_cast<uint32_t>(qka[it].w),
-                               static_cast<uint32_t>(qkb[it].x), static_cast<uint32_t>(qkb[it].y),
-                               static_cast<uint32_t>(qkb[it].z), static_cast<uint32_t>(qkb[it].w)};
-        const uint4 lo = make_uint4(__byte_perm(w[0], w[1], 0x6420), __byte_perm(w[2], w[3], 0x6420),
-                                    __byte_perm(w[4], w[5], 0x6420), __byte_perm(w[6], w[7], 0x6420));
-        const uint4 hi = make_uint4(__byte_perm(w[0], w[1], 0x7531), __byte_perm(w[2], w[3], 0x7531),
-                                    __byte_perm(w[4], w[5], 0x7531), __byte_perm(w[6], w[7], 0x7531));
-        // q rows go to their packed tile slot (see the tile loop); k rows to the K tile
-        uint8_t* tile = Ks;
-        int tr = r;
-        if (which < 3) {
-            const int sl = 3 * (3 - r / 32) + which;
-            tile = Qs + (sl / 4) * ATTN_TC_TILE;
-            tr = (sl % 4) * 32 + r % 32;
-        }
-        *reinterpret_cast<uint4*>(tile + sw128(tr, c * 16)) = lo;
-        *reinterpret_cast<uint4*>(tile + sw128(tr, 64 + c * 16)) = hi;
-    }
-    {   // V^T: key vj's 16 values go into column vj of both planes
-        const int16_t* v = reinterpret_cast<const int16_t*>(&va);
-        const int16_t* v2 = reinterpret_cast<const int16_t*>(&vb);
-#pragma unroll
-        for (int d = 0; d < 16; ++d) {
-            const int16_t x = d < 8 ? v[d] : v2[d - 8];
-            VT[sw128(vdq * 16 + d, vj)] = static_cast<uint8_t>(x & 0xFF);
-            VT[8192 + sw128(vdq * 16 + d, vj)] = static_cast<uint8_t>((x >> 8) & 0xFF);
-        }
-    }
-    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -169,7 +110,6 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     bool active = false;
     const bool fast = !ap.generic && ap.shift_s >= 8 && ap.shift_s <= 31;  // 32-bit score path (see the score pass)
     const int64_t srnd = fast ? (int64_t(1) << (ap.shift_s - 1)) : 0;
-
     // S of packed tile t covers its live key blocks only: nt = 128, 96, 64 keys for t = 0, 1, 2, with
     // the three accumulators at TMEM columns 0, nt and 2 nt (at most 288 columns after tile 0).  P V
     // goes to columns 320 .. 511, so the next tile's S can be computed while this tile's softmax,
@@ -189,213 +129,283 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
         }
         tc_commit(bar);
     };
-    if (tid == 0) issue_s(0);
 
-    for (int h = 0; h < 3; ++h) {  // h = packed tile
-        const int slot = 4 * h + quad, hq = slot % 3, bq = 3 - slot / 3;
-        const int pos = 32 * bq + lane;  // sequence position of this thread's query row
-        const int nt = 128 - 32 * h;
-        active = kb <= bq;
-        if (tid < 128) jstar_s[tid] = -1;
-        // ---- S = Q_h K^T (M = 128 queries, N = nt keys, K = 64 dims per plane pair), issued earlier
-        if (!__syncthreads_and(mbar_wait(bar, phase_s, abort, err, ERR_TIMEOUT_ATTN))) break;
-        phase_s ^= 1;
-        tc_fence_after();
+    // Persistent over (sequence, KV group) items: the TMEM allocation, barriers and exp table above are
+    // set up once per CTA.  Between items every MMA has completed (the last P V was waited for) and the
+    // end-of-tile barrier has passed, so the staging below may overwrite Q, K, V^T and the P planes.
+    bool ok = true;
+    for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const int seq = item / N_KV, g = item % N_KV;
+        const int64_t row0 = static_cast<int64_t>(seq) * T;
 
-        // ---- scores of my 32-key block for my quadrant's rows -> the shared score tile
-        if (active) {
+        // ---- stage K, Q (3 heads) and V^T as byte planes; rows/keys >= T are zero.  Every global load of
+        // the staging is issued before the first shared-memory store, so their latencies overlap.
+        constexpr int QK_ITERS = 128 * 4 * 4 / ATTN_TC_THREADS;  // 32-byte pieces per thread
+        int4 qka[QK_ITERS], qkb[QK_ITERS], va = make_int4(0, 0, 0, 0), vb = make_int4(0, 0, 0, 0);
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                const int col = kb * 32 + c * 16;
-                uint32_t d0[16], d1[16], d2[16];
-                tmem_ld16(tq + col, d0);
-                tmem_ld16(tq + nt + col, d1);
-                tmem_ld16(tq + 2 * nt + col, d2);
-                tmem_wait_ld();
-                tmem_launder(d0); tmem_launder(d1); tmem_launder(d2);
-                uint32_t sp[8];  // s as int16 pairs
-#pragma unroll
-                for (int q = 0; q < 16; q += 2) {
-                    int32_t s2[2];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int32_t a0 = static_cast<int32_t>(d0[q + u]), a1 = static_cast<int32_t>(d1[q + u]),
-                                      a2 = static_cast<int32_t>(d2[q + u]);
-                        if (fast) {
-                            // S + 2^(sh-1) = 2^8 (2^8 a2 + a1 + ((a0 + 2^(sh-1)) >> 8)) + ((a0 + 2^(sh-1)) & 255),
-                            // so RS(S, sh) = (2^8 a2 + a1 + ((a0 + 2^(sh-1)) >> 8)) >> (sh - 8): every term
-                            // fits int32 (|a0| < 2^22, |a1| < 2^22, |a2| <= 2^20, 2^(sh-1) <= 2^30)
-                            const int32_t t = a2 * 256 + a1 + ((a0 + static_cast<int32_t>(srnd)) >> 8);
-                            s2[u] = min(max(t >> (ap.shift_s - 8), -32768), 32767);
-                        } else {
-                            const int64_t S = static_cast<int64_t>(a2) * 65536 + static_cast<int64_t>(a1) * 256 +
-                                              static_cast<int64_t>(a0);
-                            s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
-                        }
-                    }
-                    sp[q / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
-                }
-                uint4* dst = reinterpret_cast<uint4*>(Ss + i * ATTN_SS_PITCH + col);
-                dst[0] = make_uint4(sp[0], sp[1], sp[2], sp[3]);
-                dst[1] = make_uint4(sp[4], sp[5], sp[6], sp[7]);
+        for (int it = 0; it < QK_ITERS; ++it) {
+            const int idx = tid + it * ATTN_TC_THREADS;
+            const int r = idx / 16, c = (idx / 4) % 4, which = idx % 4;  // which: 0..2 = q head, 3 = k
+            qka[it] = qkb[it] = make_int4(0, 0, 0, 0);
+            if (r < T) {
+                const int16_t* src = which < 3 ? ap.q + (row0 + r) * D_MODEL + (g * 3 + which) * 64 + c * 16
+                                               : ap.k + (row0 + r) * 192 + g * 64 + c * 16;
+                qka[it] = reinterpret_cast<const int4*>(src)[0];
+                qkb[it] = reinterpret_cast<const int4*>(src)[1];
             }
         }
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        if (tid == 0 && h < 2) issue_s(h + 1);  // S columns are free again
-
-        // ---- softmax of tile row r by threads 4 r .. 4 r + 3: thread jq takes key groups g = jq + 4 m
-        // (keys 4 g .. 4 g + 3), m = 0 .. 7; rows past T or keys past the row's position get P = 0
-        {
-            const int r = tid >> 2, jq = tid & 3;
-            const int rslot = 4 * h + (r >> 5);
-            const int rpos = 32 * (3 - rslot / 3) + (r & 31);
-            const int nk = rpos < T ? rpos + 1 : 0;  // live keys of this row
-            const int16_t* srow = Ss + r * ATTN_SS_PITCH;
-            // a thread's key groups ascend with m, so the live ones are m < nm (branches, not predicates:
-            // the unrolled division would otherwise run for every key of the row's 128)
-            const int nm = nk > 4 * jq ? (nk - 4 * jq + 15) / 16 : 0;
-            uint2 sv[8];
-            int32_t mx = -32768;
+        const int vj = tid & 127, vdq = tid >> 7;  // V^T: thread (key, dim quarter)
+        if (vj < T) {
+            const int4* src = reinterpret_cast<const int4*>(ap.v + (row0 + vj) * 192 + g * 64 + vdq * 16);
+            va = src[0];
+            vb = src[1];
+        }
 #pragma unroll
-            for (int m = 0; m < 8; ++m) {
-                if (m >= nm) break;
-                const int k0 = 4 * (jq + 4 * m);
-                sv[m] = *reinterpret_cast<const uint2*>(srow + k0);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
-                    if (k0 + u < nk) mx = max(mx, sk);
-                }
+        for (int it = 0; it < QK_ITERS; ++it) {
+            const int idx = tid + it * ATTN_TC_THREADS;
+            const int r = idx / 16, c = (idx / 4) % 4, which = idx % 4;
+            // low bytes of the 16 values (bytes 0 and 2 of each word) and high bytes (1 and 3)
+            const uint32_t w[8] = {static_cast<uint32_t>(qka[it].x), static_cast<uint32_t>(qka[it].y),
+                                   static_cast<uint32_t>(qka[it].z), static_cast<uint32_t>(qka[it].w),
+                                   static_cast<uint32_t>(qkb[it].x), static_cast<uint32_t>(qkb[it].y),
+                                   static_cast<uint32_t>(qkb[it].z), static_cast<uint32_t>(qkb[it].w)};
+            const uint4 lo = make_uint4(__byte_perm(w[0], w[1], 0x6420), __byte_perm(w[2], w[3], 0x6420),
+                                        __byte_perm(w[4], w[5], 0x6420), __byte_perm(w[6], w[7], 0x6420));
+            const uint4 hi = make_uint4(__byte_perm(w[0], w[1], 0x7531), __byte_perm(w[2], w[3], 0x7531),
+                                        __byte_perm(w[4], w[5], 0x7531), __byte_perm(w[6], w[7], 0x7531));
+            // q rows go to their packed tile slot (see the tile loop); k rows to the K tile
+            uint8_t* tile = Ks;
+            int tr = r;
+            if (which < 3) {
+                const int sl = 3 * (3 - r / 32) + which;
+                tile = Qs + (sl / 4) * ATTN_TC_TILE;
+                tr = (sl % 4) * 32 + r % 32;
             }
-            mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            int64_t z = 0;
+            *reinterpret_cast<uint4*>(tile + sw128(tr, c * 16)) = lo;
+            *reinterpret_cast<uint4*>(tile + sw128(tr, 64 + c * 16)) = hi;
+        }
+        {   // V^T: key vj's 16 values go into column vj of both planes
+            const int16_t* v = reinterpret_cast<const int16_t*>(&va);
+            const int16_t* v2 = reinterpret_cast<const int16_t*>(&vb);
 #pragma unroll
-            for (int m = 0; m < 8; ++m) {
-                if (m >= nm) break;
-                const int k0 = 4 * (jq + 4 * m);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
-                    const int32_t dd = mx - sk;
-                    if (k0 + u < nk && dd <= DMAX) z += E[dd];
-                }
-            }
-            z += __shfl_xor_sync(0xffffffffu, z, 1);
-            z += __shfl_xor_sync(0xffffffffu, z, 2);
-            const int64_t halfZ = z / 2;
-            const float scale = z > 0 ? static_cast<float>(65536.0 / static_cast<double>(z)) : 0.f;
-#pragma unroll
-            for (int m = 0; m < 8; ++m) {
-                const int k0 = 4 * (jq + 4 * m);
-                uint32_t b0 = 0, b1 = 0;
-                if (m < nm) {
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
-                        const int32_t dd = mx - sk;
-                        int32_t p = 0;
-                        if (k0 + u < nk && dd <= DMAX) p = prob_q16_f32(E[dd], z, halfZ, scale);
-                        if (p == 65536) jstar_s[r] = k0 + u;
-                        b0 |= static_cast<uint32_t>(p & 0xFF) << (8 * u);
-                        b1 |= static_cast<uint32_t>((p >> 8) & 0xFF) << (8 * u);
-                    }
-                }
-                *reinterpret_cast<uint32_t*>(Ps + sw128(r, k0)) = b0;
-                *reinterpret_cast<uint32_t*>(Ps + ATTN_TC_TILE + sw128(r, k0)) = b1;
+            for (int d = 0; d < 16; ++d) {
+                const int16_t x = d < 8 ? v[d] : v2[d - 8];
+                VT[sw128(vdq * 16 + d, vj)] = static_cast<uint8_t>(x & 0xFF);
+                VT[8192 + sw128(vdq * 16 + d, vj)] = static_cast<uint8_t>((x >> 8) & 0xFF);
             }
         }
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
+        if (tid == 0) issue_s(0);
 
-        // ---- ctx = P V (M = 128 queries, N = 64 dims, K = 128 keys) into columns PV_COL ..
-        if (tid == 0) {
+        for (int h = 0; h < 3; ++h) {  // h = packed tile
+            const int slot = 4 * h + quad, hq = slot % 3, bq = 3 - slot / 3;
+            const int pos = 32 * bq + lane;  // sequence position of this thread's query row
+            const int nt = 128 - 32 * h;
+            active = kb <= bq;
+            if (tid < 128) jstar_s[tid] = -1;
+            // ---- S = Q_h K^T (M = 128 queries, N = nt keys, K = 64 dims per plane pair), issued earlier
+            if (!__syncthreads_and(mbar_wait(bar, phase_s, abort, err, ERR_TIMEOUT_ATTN))) { ok = false; break; }
+            phase_s ^= 1;
+            tc_fence_after();
+
+            // ---- scores of my 32-key block for my quadrant's rows -> the shared score tile
+            if (active) {
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                const uint32_t acc = ks > 0 ? 1u : 0u;
-                const uint64_t p0 = smem_desc_sw128(sP0 + ks * 32), p1 = smem_desc_sw128(sP1 + ks * 32);
-                const uint64_t v0 = smem_desc_sw128(sV0 + ks * 32), v1 = smem_desc_sw128(sV1 + ks * 32);
-                mma_i8(tmem + PV_COL, p0, v0, idesc_i8(false, false, 64), acc);
-                mma_i8(tmem + PV_COL + 64, p1, v0, idesc_i8(false, false, 64), acc);
-                mma_i8(tmem + PV_COL + 64, p0, v1, idesc_i8(false, true, 64), 1u);
-                mma_i8(tmem + PV_COL + 128, p1, v1, idesc_i8(false, true, 64), acc);
-            }
-            tc_commit(bar + 1);
-        }
-        if (!__syncthreads_and(mbar_wait(bar + 1, phase_p, abort, err, ERR_TIMEOUT_ATTN))) break;
-        phase_p ^= 1;
-        tc_fence_after();
-        {   // epilogue: rows of my quadrant, dims 16 kb .. 16 kb + 15
-            const int hh = g * 3 + hq;
-            const int col = kb * 16;
-            uint32_t c0[16], c1[16], c2[16];
-            tmem_ld16(tq + PV_COL + col, c0);
-            tmem_ld16(tq + PV_COL + 64 + col, c1);
-            tmem_ld16(tq + PV_COL + 128 + col, c2);
-            tmem_wait_ld();
-            tmem_launder(c0); tmem_launder(c1); tmem_launder(c2);
-            if (pos < T) {
-                const int js = jstar_s[i];
-                int32_t out[16];
-                if (!ap.generic && ap.shift_c >= 8 && ap.shift_c <= 31) {
-                    // ctx + 2^(sh-1) = 2^8 (2^8 C2 + C1 + 2^8 v_j* + ((C0 + 2^(sh-1)) >> 8)) + ((C0 + 2^(sh-1)) & 255),
-                    // so RS(ctx, sh) = (...) >> (sh - 8), every term in int32: |2^8 C2| <= 2^8 * 128 * 255 * 128
-                    // < 2^30, |C1| < 2^24, |2^8 v_j*| <= 2^23, |C0| < 2^23, 2^(sh-1) <= 2^30
-                    const int32_t crnd = 1 << (ap.shift_c - 1);
-                    const int32_t lim = ap.bits_c < 32 ? (1 << (ap.bits_c - 1)) : 0;
+                for (int c = 0; c < 2; ++c) {
+                    const int col = kb * 32 + c * 16;
+                    uint32_t d0[16], d1[16], d2[16];
+                    tmem_ld16(tq + col, d0);
+                    tmem_ld16(tq + nt + col, d1);
+                    tmem_ld16(tq + 2 * nt + col, d2);
+                    tmem_wait_ld();
+                    tmem_launder(d0); tmem_launder(d1); tmem_launder(d2);
+                    uint32_t sp[8];  // s as int16 pairs
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) {
-                        const int d = col + q;
-                        int32_t t = static_cast<int32_t>(c2[q]) * 256 + static_cast<int32_t>(c1[q]) +
-                                    ((static_cast<int32_t>(c0[q]) + crnd) >> 8);
-                        if (js >= 0) {
-                            const int32_t vj = static_cast<int32_t>(VT[sw128(d, js)]) |
-                                               (static_cast<int32_t>(static_cast<int8_t>(VT[8192 + sw128(d, js)])) * 256);
-                            t += vj * 256;
+                    for (int q = 0; q < 16; q += 2) {
+                        int32_t s2[2];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const int32_t a0 = static_cast<int32_t>(d0[q + u]), a1 = static_cast<int32_t>(d1[q + u]),
+                                          a2 = static_cast<int32_t>(d2[q + u]);
+                            if (fast) {
+                                // S + 2^(sh-1) = 2^8 (2^8 a2 + a1 + ((a0 + 2^(sh-1)) >> 8)) + ((a0 + 2^(sh-1)) & 255),
+                                // so RS(S, sh) = (2^8 a2 + a1 + ((a0 + 2^(sh-1)) >> 8)) >> (sh - 8): every term
+                                // fits int32 (|a0| < 2^22, |a1| < 2^22, |a2| <= 2^20, 2^(sh-1) <= 2^30)
+                                const int32_t t = a2 * 256 + a1 + ((a0 + static_cast<int32_t>(srnd)) >> 8);
+                                s2[u] = min(max(t >> (ap.shift_s - 8), -32768), 32767);
+                            } else {
+                                const int64_t S = static_cast<int64_t>(a2) * 65536 + static_cast<int64_t>(a1) * 256 +
+                                                  static_cast<int64_t>(a0);
+                                s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
+                            }
                         }
-                        int32_t r = t >> (ap.shift_c - 8);
-                        if (lim) r = min(max(r, -lim), lim - 1);
-                        out[q] = r;
+                        sp[q / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
                     }
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 16; ++q) {
-                        const int d = col + q;
-                        int64_t a = static_cast<int64_t>(static_cast<int32_t>(c2[q])) * 65536 +
-                                    (static_cast<int64_t>(static_cast<int32_t>(c1[q])) * 256 +
-                                     static_cast<int64_t>(static_cast<int32_t>(c0[q])));
-                        if (js >= 0) {
-                            const int32_t vj = static_cast<int32_t>(VT[sw128(d, js)]) |
-                                               (static_cast<int32_t>(static_cast<int8_t>(VT[8192 + sw128(d, js)])) << 8);
-                            a += static_cast<int64_t>(vj) * 65536;
-                        }
-                        out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
-                    }
-                }
-                // row-blocked planes: this warp's 32 rows x 16 dims are 512 contiguous bytes per plane
-                const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
-                uint4* dst = reinterpret_cast<uint4*>(ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL));
-                uint32_t w[4];
-                pack_plane<0, 16>(out, w);
-                dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                pack_plane<1, 16>(out, w);
-                dst[pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
-                if (ap.P == 4) {
-                    pack_plane<2, 16>(out, w);
-                    dst[2 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
-                    pack_plane<3, 16>(out, w);
-                    dst[3 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                    uint4* dst = reinterpret_cast<uint4*>(Ss + i * ATTN_SS_PITCH + col);
+                    dst[0] = make_uint4(sp[0], sp[1], sp[2], sp[3]);
+                    dst[1] = make_uint4(sp[4], sp[5], sp[6], sp[7]);
                 }
             }
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0 && h < 2) issue_s(h + 1);  // S columns are free again
+
+            // ---- softmax of tile row r by threads 4 r .. 4 r + 3: thread jq takes key groups g = jq + 4 m
+            // (keys 4 g .. 4 g + 3), m = 0 .. 7; rows past T or keys past the row's position get P = 0
+            {
+                const int r = tid >> 2, jq = tid & 3;
+                const int rslot = 4 * h + (r >> 5);
+                const int rpos = 32 * (3 - rslot / 3) + (r & 31);
+                const int nk = rpos < T ? rpos + 1 : 0;  // live keys of this row
+                const int16_t* srow = Ss + r * ATTN_SS_PITCH;
+                // a thread's key groups ascend with m, so the live ones are m < nm (branches, not predicates:
+                // the unrolled division would otherwise run for every key of the row's 128)
+                const int nm = nk > 4 * jq ? (nk - 4 * jq + 15) / 16 : 0;
+                uint2 sv[8];
+                int32_t mx = -32768;
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    if (m >= nm) break;
+                    const int k0 = 4 * (jq + 4 * m);
+                    sv[m] = *reinterpret_cast<const uint2*>(srow + k0);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
+                        if (k0 + u < nk) mx = max(mx, sk);
+                    }
+                }
+                mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                int64_t z = 0;
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    if (m >= nm) break;
+                    const int k0 = 4 * (jq + 4 * m);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
+                        const int32_t dd = mx - sk;
+                        if (k0 + u < nk && dd <= DMAX) z += E[dd];
+                    }
+                }
+                z += __shfl_xor_sync(0xffffffffu, z, 1);
+                z += __shfl_xor_sync(0xffffffffu, z, 2);
+                const int64_t halfZ = z / 2;
+                const float scale = z > 0 ? static_cast<float>(65536.0 / static_cast<double>(z)) : 0.f;
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const int k0 = 4 * (jq + 4 * m);
+                    uint32_t b0 = 0, b1 = 0;
+                    if (m < nm) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
+                            const int32_t dd = mx - sk;
+                            int32_t p = 0;
+                            if (k0 + u < nk && dd <= DMAX) p = prob_q16_f32(E[dd], z, halfZ, scale);
+                            if (p == 65536) jstar_s[r] = k0 + u;
+                            b0 |= static_cast<uint32_t>(p & 0xFF) << (8 * u);
+                            b1 |= static_cast<uint32_t>((p >> 8) & 0xFF) << (8 * u);
+                        }
+                    }
+                    *reinterpret_cast<uint32_t*>(Ps + sw128(r, k0)) = b0;
+                    *reinterpret_cast<uint32_t*>(Ps + ATTN_TC_TILE + sw128(r, k0)) = b1;
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+
+            // ---- ctx = P V (M = 128 queries, N = 64 dims, K = 128 keys) into columns PV_COL ..
+            if (tid == 0) {
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint32_t acc = ks > 0 ? 1u : 0u;
+                    const uint64_t p0 = smem_desc_sw128(sP0 + ks * 32), p1 = smem_desc_sw128(sP1 + ks * 32);
+                    const uint64_t v0 = smem_desc_sw128(sV0 + ks * 32), v1 = smem_desc_sw128(sV1 + ks * 32);
+                    mma_i8(tmem + PV_COL, p0, v0, idesc_i8(false, false, 64), acc);
+                    mma_i8(tmem + PV_COL + 64, p1, v0, idesc_i8(false, false, 64), acc);
+                    mma_i8(tmem + PV_COL + 64, p0, v1, idesc_i8(false, true, 64), 1u);
+                    mma_i8(tmem + PV_COL + 128, p1, v1, idesc_i8(false, true, 64), acc);
+                }
+                tc_commit(bar + 1);
+            }
+            if (!__syncthreads_and(mbar_wait(bar + 1, phase_p, abort, err, ERR_TIMEOUT_ATTN))) { ok = false; break; }
+            phase_p ^= 1;
+            tc_fence_after();
+            {   // epilogue: rows of my quadrant, dims 16 kb .. 16 kb + 15
+                const int hh = g * 3 + hq;
+                const int col = kb * 16;
+                uint32_t c0[16], c1[16], c2[16];
+                tmem_ld16(tq + PV_COL + col, c0);
+                tmem_ld16(tq + PV_COL + 64 + col, c1);
+                tmem_ld16(tq + PV_COL + 128 + col, c2);
+                tmem_wait_ld();
+                tmem_launder(c0); tmem_launder(c1); tmem_launder(c2);
+                if (pos < T) {
+                    const int js = jstar_s[i];
+                    int32_t out[16];
+                    if (!ap.generic && ap.shift_c >= 8 && ap.shift_c <= 31) {
+                        // ctx + 2^(sh-1) = 2^8 (2^8 C2 + C1 + 2^8 v_j* + ((C0 + 2^(sh-1)) >> 8)) + ((C0 + 2^(sh-1)) & 255),
+                        // so RS(ctx, sh) = (...) >> (sh - 8), every term in int32: |2^8 C2| <= 2^8 * 128 * 255 * 128
+                        // < 2^30, |C1| < 2^24, |2^8 v_j*| <= 2^23, |C0| < 2^23, 2^(sh-1) <= 2^30
+                        const int32_t crnd = 1 << (ap.shift_c - 1);
+                        const int32_t lim = ap.bits_c < 32 ? (1 << (ap.bits_c - 1)) : 0;
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const int d = col + q;
+                            int32_t t = static_cast<int32_t>(c2[q]) * 256 + static_cast<int32_t>(c1[q]) +
+                                        ((static_cast<int32_t>(c0[q]) + crnd) >> 8);
+                            if (js >= 0) {
+                                const int32_t vj = static_cast<int32_t>(VT[sw128(d, js)]) |
+                                                   (static_cast<int32_t>(static_cast<int8_t>(VT[8192 + sw128(d, js)])) * 256);
+                                t += vj * 256;
+                            }
+                            int32_t r = t >> (ap.shift_c - 8);
+                            if (lim) r = min(max(r, -lim), lim - 1);
+                            out[q] = r;
+                        }
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const int d = col + q;
+                            int64_t a = static_cast<int64_t>(static_cast<int32_t>(c2[q])) * 65536 +
+                                        (static_cast<int64_t>(static_cast<int32_t>(c1[q])) * 256 +
+                                         static_cast<int64_t>(static_cast<int32_t>(c0[q])));
+                            if (js >= 0) {
+                                const int32_t vj = static_cast<int32_t>(VT[sw128(d, js)]) |
+                                                   (static_cast<int32_t>(static_cast<int8_t>(VT[8192 + sw128(d, js)])) << 8);
+                                a += static_cast<int64_t>(vj) * 65536;
+                            }
+                            out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
+                        }
+                    }
+                    // row-blocked planes: this warp's 32 rows x 16 dims are 512 contiguous bytes per plane
+                    const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
+                    uint4* dst = reinterpret_cast<uint4*>(ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL));
+                    uint32_t w[4];
+                    pack_plane<0, 16>(out, w);
+                    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    pack_plane<1, 16>(out, w);
+                    dst[pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                    if (ap.P == 4) {
+                        pack_plane<2, 16>(out, w);
+                        dst[2 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                        pack_plane<3, 16>(out, w);
+                        dst[3 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
         }
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-    }
+    }  // item
     tc_fence_before();
     __syncthreads();
     tc_fence_after();

@@ -551,9 +551,12 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     }
     if (!decode) {
         ProfScope ps(e, EII_K_ATTENTION, st);
-        if (T <= 128 && !e->force_cuda_core_attention && !trh)
-            CK(launch_k(k_attention_tc, dim3(nseq * N_KV), dim3(ATTN_TC_THREADS), ATTN_TC_SMEM, st, ap, e->err_dev));
-        else
+        if (T <= 128 && !e->force_cuda_core_attention && !trh) {
+            // persistent: one CTA per SM (its resources allow one), each looping over (sequence, KV group) items
+            const int items = nseq * N_KV;
+            CK(launch_k(k_attention_tc, dim3(items < e->num_sms ? items : e->num_sms), dim3(ATTN_TC_THREADS), ATTN_TC_SMEM,
+                        st, ap, e->err_dev));
+        } else
             CK(launch_k(k_attention, dim3(nseq * N_KV), dim3(ATTN_WARPS * 32), attn_smem_bytes(T), st, ap));
     }
 
