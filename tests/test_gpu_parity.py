@@ -381,3 +381,21 @@ def test_forward_t24_unsigned_gated_planes(base_model, base_model_path, monkeypa
         _check_set(e, base_model, "t24")
     finally:
         e.close()
+
+
+def test_chunk_sequences_fill_whole_waves(eng, monkeypatch):
+    """Without EII_CHUNK_ROWS the sequences per chunk are a multiple of the SM count (about 65536
+    rows), so the attention's (sequence, KV group) items and the GEMM row blocks spread evenly over
+    the SMs; the variable sets the chunk exactly; the count never exceeds the request."""
+    import torch
+    import _eii
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    monkeypatch.delenv("EII_CHUNK_ROWS", raising=False)
+    cs = eng.chunk_sequences(4096, 128)
+    assert cs % sms == 0 and abs(cs * 128 - 65536) <= sms * 128 // 2
+    assert eng.chunk_sequences(3, 128) == 3
+    assert eng.chunk_sequences(100000, 1) % sms == 0
+    monkeypatch.setenv("EII_CHUNK_ROWS", "16384")
+    assert eng.chunk_sequences(4096, 128) == 128
+    with pytest.raises(_eii.EiiError):
+        eng.chunk_sequences(0, 128)
