@@ -222,7 +222,8 @@ __device__ __forceinline__ void add96(uint32_t& a0, uint32_t& a1, uint32_t& a2, 
         : "r"(b0), "r"(b1), "r"(b2));
 }
 
-__global__ void __launch_bounds__(256) k_rmsnorm_p16(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain,
+// Four 256-thread blocks per SM (at most 64 registers): more loads in flight on the HBM-bound path.
+__global__ void __launch_bounds__(256, 4) k_rmsnorm_p16(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain,
                                                       int shift_out, uint8_t* __restrict__ planes,
                                                       uint32_t* __restrict__ zero_ptr, int zero_n) {
     const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
