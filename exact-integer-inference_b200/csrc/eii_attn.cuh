@@ -36,9 +36,12 @@ constexpr int ATTN_TC_TILE = 128 * 128;  // one 128 x 128-byte swizzled tile
 // Score tile row pitch: 144 int16 (288 bytes = 72 words, 8 mod 32), so the four rows a half-warp
 // reads with 8-byte loads start 8 banks apart.
 constexpr int ATTN_SS_PITCH = 144;
+// e values of the softmax, private to each thread: [8 key groups][512 threads] int4 (a warp's 16-byte
+// accesses are 512 contiguous bytes, so conflict-free)
+constexpr int ATTN_ET_BYTES = 8 * 512 * 16;
 // smem: Q (3 tiles) | K (1) | V^T planes (2 x 64 rows x 128 B = 1 tile) | P planes (2 tiles) |
-//       scores [128][144] int16 | E | j* [128] int32 | barrier, TMEM slot, abort
-constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + 128 * ATTN_SS_PITCH * 2 + (DMAX + 1 + 3) * 4 + 128 * 4 + 64;
+//       e values | scores [128][144] int16 | E | j* [128] int32 | barrier, TMEM slot, abort
+constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + ATTN_ET_BYTES + 128 * ATTN_SS_PITCH * 2 + (DMAX + 1 + 3) * 4 + 128 * 4 + 64;
 
 // Byte offset of byte b of row r inside a 128-byte-row tile with the 128-byte swizzle.
 __device__ __forceinline__ int sw128(int r, int b) { return r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15); }
@@ -75,7 +78,8 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     uint8_t* Ks = sm + 3 * ATTN_TC_TILE;    // row j = [k0 | k1]
     uint8_t* VT = sm + 4 * ATTN_TC_TILE;    // plane p at VT + p * 8192: row d, byte j
     uint8_t* Ps = sm + 5 * ATTN_TC_TILE;    // plane p at Ps + p * ATTN_TC_TILE: row i, byte j
-    int16_t* Ss = reinterpret_cast<int16_t*>(sm + 7 * ATTN_TC_TILE);   // [128][ATTN_SS_PITCH]
+    int4* Et = reinterpret_cast<int4*>(sm + 7 * ATTN_TC_TILE);        // [8][512]: e of key group m of thread tid
+    int16_t* Ss = reinterpret_cast<int16_t*>(sm + 7 * ATTN_TC_TILE + ATTN_ET_BYTES);  // [128][ATTN_SS_PITCH]
     int32_t* E = reinterpret_cast<int32_t*>(Ss + 128 * ATTN_SS_PITCH);
     int32_t* jstar_s = E + DMAX + 1 + 3;                                  // [128]
     uint64_t* bar = reinterpret_cast<uint64_t*>(jstar_s + 128);  // [0]: S = Q K^T, [1]: P V
@@ -280,17 +284,22 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                 }
                 mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
                 mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                // e of each live key (0 past the row's position or beyond DMAX, which makes P = 0 below),
+                // kept in this thread's shared-memory slots for the division pass
                 int64_t z = 0;
 #pragma unroll
                 for (int m = 0; m < 8; ++m) {
                     if (m >= nm) break;
                     const int k0 = 4 * (jq + 4 * m);
+                    int32_t ev[4];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
                         const int32_t dd = mx - sk;
-                        if (k0 + u < nk && dd <= DMAX) z += E[dd];
+                        ev[u] = (k0 + u < nk && dd <= DMAX) ? E[dd] : 0;
+                        z += ev[u];
                     }
+                    Et[m * ATTN_TC_THREADS + tid] = make_int4(ev[0], ev[1], ev[2], ev[3]);
                 }
                 z += __shfl_xor_sync(0xffffffffu, z, 1);
                 z += __shfl_xor_sync(0xffffffffu, z, 2);
@@ -301,16 +310,17 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                     const int k0 = 4 * (jq + 4 * m);
                     uint32_t b0 = 0, b1 = 0;
                     if (m < nm) {
+                        const int4 e4 = Et[m * ATTN_TC_THREADS + tid];
+                        const int32_t ev[4] = {e4.x, e4.y, e4.z, e4.w};
+                        uint32_t p[4];
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
-                            const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
-                            const int32_t dd = mx - sk;
-                            int32_t p = 0;
-                            if (k0 + u < nk && dd <= DMAX) p = prob_q16_f32(E[dd], z, halfZ, scale);
-                            if (p == 65536) jstar_s[r] = k0 + u;
-                            b0 |= static_cast<uint32_t>(p & 0xFF) << (8 * u);
-                            b1 |= static_cast<uint32_t>((p >> 8) & 0xFF) << (8 * u);
+                            p[u] = static_cast<uint32_t>(prob_q16_f32(ev[u], z, halfZ, scale));  // 0 for e = 0
+                            if (p[u] == 65536u) jstar_s[r] = k0 + u;
                         }
+                        // plane 0: byte 0 of each P, plane 1: byte 1 (the P = 65536 key is added back via j*)
+                        b0 = __byte_perm(__byte_perm(p[0], p[1], 0x0040), __byte_perm(p[2], p[3], 0x0040), 0x5410);
+                        b1 = __byte_perm(__byte_perm(p[0], p[1], 0x0051), __byte_perm(p[2], p[3], 0x0051), 0x5410);
                     }
                     *reinterpret_cast<uint32_t*>(Ps + sw128(r, k0)) = b0;
                     *reinterpret_cast<uint32_t*>(Ps + ATTN_TC_TILE + sw128(r, k0)) = b1;
