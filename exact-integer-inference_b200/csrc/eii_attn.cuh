@@ -46,7 +46,6 @@ constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + ATTN_ET_BYTES + 128 * ATT
 // Byte offset of byte b of row r inside a 128-byte-row tile with the 128-byte swizzle.
 __device__ __forceinline__ int sw128(int r, int b) { return r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15); }
 
-
 // floor((e * 65536 + floor(Z/2)) / Z) for 0 <= e <= 2^30, 2^30 <= Z < 2^40.
 // n / Z = e (65536 / Z) + floor(Z/2) / Z, the second term in (0.5 - 1/(2Z), 0.5]; in fp32 the
 // estimate e * (65536 / Z) + 0.5 has absolute error < 0.05 (quotient < 2^17), so its floor is within
@@ -58,17 +57,6 @@ __device__ __forceinline__ int32_t prob_q16_f32(int32_t e, int64_t Z, int64_t ha
     if (r < 0) --q;
     else if (r >= Z) ++q;
     return q;
-}
-
-__device__ __forceinline__ int64_t prob_q16(int64_t e, int64_t Z, int64_t halfZ, double rz) {
-    const int64_t n = e * 65536 + halfZ;
-    int64_t p = static_cast<int64_t>(static_cast<double>(n) * rz);
-    int64_t r = n - p * Z;
-    if (r < 0) { --p; r += Z; }
-    if (r < 0) { --p; r += Z; }
-    if (r >= Z) { ++p; r -= Z; }
-    if (r >= Z) { ++p; }
-    return p;
 }
 
 __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams ap, int* err) {
