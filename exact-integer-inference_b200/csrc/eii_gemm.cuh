@@ -14,10 +14,11 @@
 //               weight tile [128 x 128 B], 128-byte swizzle, into a STAGES-deep smem ring.
 //   warp 1      TMEM allocator + single-thread MMA issuer: 4 (or 2 for a half block) K=32 steps
 //               x P planes of tcgen05.mma.cta_group::1.kind::i8, M=128, N=n_valid.
-//   warps 2-9   epilogue: tcgen05.ld of the P accumulators, int64 plane combination, requantise
-//               RS/SAT, and the fused step of the caller (RoPE, residual add, SiLU-gated product,
-//               logits store), written straight to global memory.
-// TMEM: P*128 int32 columns per accumulator set; 2 sets (double buffered) for P = 2, one for P = 4.
+//   warps 2-17  16 epilogue warps (4 per TMEM lane quadrant): tcgen05.ld of the P accumulators,
+//               plane combination, requantise RS/SAT, and the fused step of the caller (RoPE,
+//               residual add, SiLU-gated product, logits and digest), stored through shared-memory
+//               staging and TMA (or straight to the row-blocked gated planes).
+// TMEM: P*BN int32 columns per accumulator set; 2 sets (double buffered) for P = 2, one for P = 4.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -112,8 +113,8 @@ constexpr int BN_P4 = 128;
 
 template <int P, int KIND>
 struct GemmCfg {
-    // P = 4 uses 64-wide N tiles so that two accumulator sets (2 x 4 x 64 columns) fit in TMEM and the
-    // epilogue of one tile overlaps the MMAs of the next.
+    // P = 4 uses BN_P4-wide N tiles (128: one accumulator set, so its epilogue does not overlap the
+    // next tile's MMAs; 64 would double-buffer them at twice the operand traffic, measured slower).
     static constexpr int BM = 128, BN = (P == 4) ? BN_P4 : 128, BK = 128;
     static constexpr int ACC_COLS = P * BN;
     static constexpr int NB = 512 / ACC_COLS;  // accumulator sets in TMEM
