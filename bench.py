@@ -208,6 +208,26 @@ def cpu_baseline_from_gpu(eng, model_bin, workdir, seconds_hint=30):
             "reference_checked_engine_output": f"{exact}/{procs} ALL STATES EXACT"}
 
 
+def cpu_baseline_numpy(eng, model_bin, n=24):
+    """The numpy path beside the scalar C one: oracle/forward.py (a numpy restatement of
+    python/intref.py; the reference's own module is not on the GPU box) timed on the host's cores
+    with all BLAS threads, on n sequences of config 4.  Its logits are compared with this engine's."""
+    sys.path.insert(0, REPO)
+    from oracle import forward as ofw
+    from oracle.modelbin import read_model_bin
+    mdl = read_model_bin(model_bin)
+    ids = token_table()[:n, :T]
+    t0 = time.time()
+    out = ofw.forward(mdl, ids, want_states=False)
+    dt = time.time() - t0
+    mine = eng.forward(ids, logits=True)["logits"]
+    same = sum(bool(np.array_equal(out["logits"][i], mine[i].astype(np.int64))) for i in range(n))
+    return {"value": round(n * T / dt, 2), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "sample": f"{n} sequences x {T} tokens of config 4 (rows 0..{n - 1}), one process: oracle/forward.py, "
+                      f"numpy with float64 BLAS on all host threads (exact under the bound python/intref.py:61 asserts)",
+            "seconds": round(dt, 2), "engine_logits_equal": f"{same}/{n}"}
+
+
 # ------------------------------------------------------------------------------------ roofline
 def roofline(prof, rows_total, peaks):
     """Dominant kernel (most device time in the profiled step) against its roofline.  The work per
@@ -434,6 +454,7 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             with tempfile.TemporaryDirectory() as td:
                 line["cpu_baseline"] = cpu_baseline_from_gpu(eng, model_path(), td)
+            line["cpu_baseline_numpy"] = cpu_baseline_numpy(eng, model_path())
         print(json.dumps(line), flush=True)
     eng.close()
     if dist:
