@@ -229,10 +229,11 @@ def cpu_baseline_numpy(eng, model_bin, n=24):
 
 
 # ------------------------------------------------------------------------------------ roofline
-def roofline(prof, rows_total, peaks):
-    """Dominant kernel (most device time in the profiled step) against its roofline.  The work per
-    launch is the step's total work of that kernel over its launch count (chunks may differ in size)."""
-    name, (ms, n) = max(prof.items(), key=lambda kv: kv[1][0])
+def roofline(prof, rows_total, peaks, kernel=None):
+    """Dominant kernel (most device time in the profiled step), or the named one, against its
+    roofline.  The work per launch is the step's total work of that kernel over its launch count
+    (chunks may differ in size)."""
+    name, (ms, n) = max(prof.items(), key=lambda kv: kv[1][0]) if kernel is None else (kernel, prof[kernel])
     per_launch_s = ms / n / 1e3
     L = 30  # layers: one launch of each layer kernel per layer and chunk; norms 2 per layer + final
     rows = rows_total
@@ -258,7 +259,20 @@ def roofline(prof, rows_total, peaks):
     out["launch_us"] = round(per_launch_s * 1e6, 1)
     out["rows_per_launch"] = r
     out["traffic"] = traffic_for(name, r)
+    act = tensor_active_for(name)
+    if act is not None:
+        out["tensor_pipe_active_ncu"] = act
     return out
+
+
+def tensor_active_for(kernel):
+    """Tensor-pipe active fraction of the kernel in the committed ncu capture (profiles/traffic.json;
+    sm__pipe_tensor_subpipe_imma_cycles_active), byte planes included."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            return json.load(f)[kernel]["tensor_active_pct"] / 100.0
+    except Exception:
+        return None
 
 
 def traffic_for(kernel, rows):
@@ -444,6 +458,7 @@ def run_ours(args):
                     "path": "eii_forward (C ABI) with pinned host ids, per-sequence digests read back"},
             "gpu_launches": int(launches_per_step * args.steps),
             "roofline": roofline(prof, rows, peaks),
+            "roofline_hbm": roofline(prof, rows, peaks, kernel="rmsnorm") if "rmsnorm" in prof else None,
             "clocks": clocks,
             "check": {"subset_sequences": int(counts[0]), "subset_exact": int(counts[1]),
                       "digests_device_eq_host_ranks": int(counts[2]),

@@ -53,3 +53,12 @@ def test_traffic_scales_with_rows(bench):
     assert bench.traffic_for("gemm_gateup_silu", e["rows"]) == e["dram_bytes"]
     assert bench.traffic_for("gemm_gateup_silu", 2 * e["rows"]) == 2 * e["dram_bytes"]
     assert bench.traffic_for("no_such_kernel", 128) is None
+
+
+def test_roofline_named_kernel_and_tensor_activity(bench):
+    rows = 4096 * 128
+    prof = {"gemm_gateup_silu": (300 * 0.330, 300), "rmsnorm": (610 * 0.042, 610)}
+    r = bench.roofline(prof, rows, PEAKS, kernel="rmsnorm")
+    assert r["kernel"] == "rmsnorm" and r["bound"] == "hbm"
+    d = bench.roofline(prof, rows, PEAKS)
+    assert 0.0 < d["tensor_pipe_active_ncu"] < 1.0
