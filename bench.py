@@ -329,6 +329,72 @@ def decode_bench(eng, ids_host, ids_dev, ns, fwd_digests, stream, barrier, max_o
             "exact_vs_forward_digests": exact}
 
 
+def gemm_sweep_bench(eng, peaks, reps=5):
+    """The stand-alone contraction sweep (shapes, formats and activations of
+    sweep.py): per (shape, M) the device time of the GEMM kernel (engine profile events on its stream,
+    L2 flushed between launches), logical int8-weight x wide-activation ops per second against the
+    int8 dense peak, the plane-expanded tensor work (planes x logical ops) against the same peak, and
+    exactness: block digests of out and of the exact acc against the reference's own Model.linear
+    (tests/golden/gemm_sweep_large.json)."""
+    import torch
+    import _eii
+    import sweep
+    with open(os.path.join(REPO, "tests", "golden", "gemm_sweep_large.json")) as f:
+        gold = {(c["case"], c["M"]): c for c in json.load(f)["cases"]}
+    int8_peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
+    flush = torch.empty(64 << 20, dtype=torch.int32, device="cuda")  # 256 MB > L2
+    out_rows = []
+    buf = open(model_path(), "rb").read()
+    for ci, case in enumerate(sweep.CASES):
+        W, m, n = sweep.weights(buf, ci)
+        bits_in, f_in, f_out, bits_out = sweep.case_formats(ci)
+        N, K = W.shape
+        P = bits_in // 8
+        plan = _eii.LinearPlan(eng, W, m, n, bits_in, f_in, f_out, bits_out)
+        try:
+            for M in sweep.MS:
+                a = torch.empty((M, K), dtype=torch.int32, device="cuda")
+                for b in range(sweep.blocks(M)):
+                    blk = sweep.activation_block(ci, M, b, K, bits_in)
+                    a[sweep.BLOCK * b:sweep.BLOCK * b + blk.shape[0]].copy_(torch.from_numpy(blk))
+                out = torch.empty((M, N), dtype=torch.int32, device="cuda")
+                d_out = torch.empty(M, dtype=torch.int64, device="cuda")
+                d_acc = torch.empty(M, dtype=torch.int64, device="cuda")
+                plan.run(a.data_ptr(), M, out.data_ptr(), N, d_out.data_ptr(), d_acc.data_ptr())
+                g = gold.get((ci, M))
+                exact = None
+                if g is not None:
+                    exact = (sweep.hexes(sweep.block_digests(d_acc.cpu().numpy().view(np.uint64), M)) == g["acc_blocks"]
+                             and sweep.hexes(sweep.block_digests(d_out.cpu().numpy().view(np.uint64), M)) == g["out_blocks"])
+                plan.run(a.data_ptr(), M, out.data_ptr(), N)  # warm-up without digests
+                eng.profile_enable(True)
+                for _ in range(reps):
+                    flush.zero_()
+                    plan.run(a.data_ptr(), M, out.data_ptr(), N)
+                prof = eng.profile_read()
+                eng.profile_enable(False)
+                ms, nl = prof["gemm_sweep"]
+                t = ms / nl / 1e3
+                ops = 2.0 * M * N * K
+                tops = ops / t / 1e12
+                hbm = (M * K * P + N * K + M * N * 4) / t / 1e9
+                out_rows.append({"shape": case[0], "M": M, "N": N, "K": K, "planes": P, "us": round(t * 1e6, 1),
+                                 "tops_logical": round(tops, 1), "frac": round(tops / int8_peak, 4),
+                                 "tensor_work_frac": round(P * tops / int8_peak, 4),
+                                 "hbm_gbs_algorithmic": round(hbm, 1), "exact_vs_reference": exact})
+                del a, out, d_out, d_acc
+                torch.cuda.empty_cache()
+        finally:
+            plan.close()
+    return {"peak_tops": round(int8_peak, 1),
+            "peak_note": "int8 dense = 2 x measured bf16 (MEASURED_PEAKS.json), of measured",
+            "ops_note": "tops_logical = 2 M N K / GEMM kernel time; tensor_work_frac counts the byte-plane MMAs "
+                        "(planes x logical) against the same peak",
+            "path": "eii_linear_plan_run (int32 activations -> byte planes -> tcgen05 kind::i8 GEMM, int32 out)",
+            "timing": f"CUDA events around the GEMM launch on the engine's stream, {reps} launches, L2 flushed "
+                      "between them", "cases": out_rows}
+
+
 def run_ours(args):
     import torch
     import _eii
@@ -470,6 +536,10 @@ def run_ours(args):
             with tempfile.TemporaryDirectory() as td:
                 line["cpu_baseline"] = cpu_baseline_from_gpu(eng, model_path(), td)
             line["cpu_baseline_numpy"] = cpu_baseline_numpy(eng, model_path())
+        if world == 1 and not args.no_gemm_sweep:
+            del logits
+            torch.cuda.empty_cache()
+            line["gemm_sweep"] = gemm_sweep_bench(eng, peaks)
         print(json.dumps(line), flush=True)
     eng.close()
     if dist:
@@ -536,6 +606,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm-sweep", action="store_true", help="skip the contraction sweep (config 5) at N=1")
     ap.add_argument("--probe", type=int, default=0, metavar="NSEQ",
                     help="profiling target: one untimed forward of NSEQ x 128 tokens on cuda:0, then exit")
     args = ap.parse_args()

@@ -16,7 +16,7 @@ STATUS_NAMES = {0: "EII_OK", 1: "EII_ERR_ARG", 2: "EII_ERR_IO", 3: "EII_ERR_CUDA
                 5: "EII_ERR_FORMAT"}
 
 VOCAB, D_MODEL, N_LAYERS = 49152, 576, 30
-NUM_KERNEL_KINDS = 10
+NUM_KERNEL_KINDS = 12
 
 
 class EiiError(RuntimeError):
@@ -60,6 +60,10 @@ _SIGS = {
     "eii_decoder_position": ([_P], ctypes.c_int),
     "eii_decoder_reset": ([_P], ctypes.c_int),
     "eii_decoder_close": ([_P], None),
+    "eii_linear_plan_open": ([_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                              ctypes.c_int, ctypes.POINTER(_P)], ctypes.c_int),
+    "eii_linear_plan_run": ([_P, _P, ctypes.c_int, _P, ctypes.c_int64, _P, _P, _P], ctypes.c_int),
+    "eii_linear_plan_close": ([_P], None),
 }
 
 
@@ -263,6 +267,40 @@ def verify_tables(model_bin):
             model_bin = f.read()
     buf = np.frombuffer(model_bin, dtype=np.uint8) if not isinstance(model_bin, np.ndarray) else model_bin
     check(lib().eii_verify_tables(ptr(buf), buf.nbytes))
+
+
+class LinearPlan:
+    """Device-resident Model.linear with bound weights (include/eii.h, eii_linear_plan_*):
+    out = SAT_bits_out(RS(a W^T m, n + f_in - f_out)) as int32 on device buffers, with optional
+    per-row digests of out and of the exact int64 accumulators."""
+
+    def __init__(self, engine, W, m, n, bits_in, f_in, f_out, bits_out):
+        W = _c(W, np.int8)
+        m = _c(m, np.int64)
+        n = _c(n, np.int64)
+        N, K = W.shape
+        h = ctypes.c_void_p()
+        check(lib().eii_linear_plan_open(engine.h, ptr(W), ptr(m), ptr(n), N, K, int(bits_in), int(f_in), int(f_out),
+                                         int(bits_out), ctypes.byref(h)))
+        self.h = h
+        self.engine = engine  # the engine must outlive the plan
+        self.N, self.K = N, K
+
+    def run(self, a_ptr, M, out_ptr, ld=None, dig_out_ptr=None, dig_acc_ptr=None, stream=None):
+        v = lambda p: ctypes.c_void_p(p) if p else None
+        check(lib().eii_linear_plan_run(self.h, ctypes.c_void_p(a_ptr), int(M), ctypes.c_void_p(out_ptr),
+                                        int(ld or self.N), v(dig_out_ptr), v(dig_acc_ptr), v(stream)))
+
+    def close(self):
+        if self.h:
+            lib().eii_linear_plan_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Decoder:

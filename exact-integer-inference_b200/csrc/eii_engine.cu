@@ -625,25 +625,28 @@ int check_device_error(eii_engine* e, cudaStream_t st) {
     if (code) {
         CK(cudaMemset(e->err_dev, 0, sizeof(int)));
         if (code == ERR_BAD_TOKEN) return fail(EII_ERR_ARG, "token id outside [0, %d)", VOCAB);
+        if (code == ERR_BAD_INPUT) return fail(EII_ERR_ARG, "an activation lies outside the signed range of its format");
         return fail(EII_ERR_DEVICE, "kernel reported error %d (bounded wait timed out)", code);
     }
     return EII_OK;
 }
 
-// Sequences per chunk: about EII_CHUNK_ROWS rows (default 65536; larger chunks amortise each
-// kernel's ramp: 592 x 128 rows ran a forward 3.7% faster than 148 x 128).  Without the variable the
-// count is rounded to a multiple of the SM count once it reaches half of it: the attention runs one
-// CTA per (sequence, KV group) at one CTA per SM, so 3 x 148 k CTAs fill whole waves (128 sequences
-// of 128 tokens took three waves for 2.6 waves of work), and the persistent GEMMs get 148 k row blocks.
+// Sequences per chunk.  The chunk workspace holds about 65536 rows (larger chunks amortise each
+// kernel's ramp: 592 x 128 rows ran a forward 3.7% faster than 148 x 128); the n_seq sequences are
+// split into the fewest chunks of at most that many rows, all of (nearly) equal size, so no chunk
+// is a small remainder: 4096 sequences of 128 tokens run as 8 x 512, and the 512-sequence shard of
+// one of 8 GPUs as one chunk of 512 (a remainder chunk of 68 sequences filled under half of the
+// SMs in every kernel).  EII_CHUNK_ROWS=R sets chunks of exactly R / T sequences instead.
 int chunk_seqs_for(const eii_engine* e, int n_seq, int T) {
+    (void)e;
     const char* s = getenv("EII_CHUNK_ROWS");
     const int v = s ? atoi(s) : 0;
-    int cs = (v > 0 ? v : 65536) / T;
-    if (cs < 1) cs = 1;
-    const int sms = e->num_sms > 0 ? e->num_sms : 1;
-    if (v <= 0 && cs >= sms / 2) cs = ((cs + sms / 2) / sms) * sms;
-    if (cs > n_seq) cs = n_seq;
-    return cs;
+    int cap = (v > 0 ? v : 65536) / T;
+    if (cap < 1) cap = 1;
+    if (cap >= n_seq) return n_seq;
+    if (v > 0) return cap;
+    const int chunks = (n_seq + cap - 1) / cap;
+    return (n_seq + chunks - 1) / chunks;
 }
 
 // ------------------------------------------------------------------------- model loading
@@ -1085,7 +1088,7 @@ int eii_version(void) { return 100; }
 const char* eii_kernel_name(int kind) {
     static const char* names[EII_NUM_KERNEL_KINDS] = {"embed", "rmsnorm", "gemm_qkv_rope", "attention", "gemm_o_resid",
                                                      "gemm_gateup_silu", "gemm_down_resid", "gemm_logits", "digest",
-                                                     "gemm_linear"};
+                                                     "gemm_linear", "split_planes", "gemm_sweep"};
     return (kind >= 0 && kind < EII_NUM_KERNEL_KINDS) ? names[kind] : "";
 }
 
@@ -1478,13 +1481,16 @@ static int linear_device(eii_engine* e, const int64_t* a_dev, int M, int K, int 
     const int P = bits_in / 8;
     uint8_t* planes;
     TRY(dalloc(tmp, &planes, (size_t)P * M * K));
-    k_split_planes<<<1184, 256, 0, e->stream>>>(a_dev, (int64_t)M * K, P, (int64_t)M * K, planes);
+    k_split_planes<<<1184, 256, 0, e->stream>>>(a_dev, (int64_t)M * K, P, (int64_t)M * K, planes, e->err_dev);
     CK(cudaGetLastError());
     CUtensorMap tmA;
     TRY(map_planes(&tmA, planes, K, M, P));
     EpiParams ep{};
     ep.M = M; ep.N = N; ep.K = K; ep.msh = msh_dev; ep.err = e->err_dev; ep.out64 = out_dev; ep.acc64 = acc_dev;
     ep.bits_out = bits_out;
+    // tests only: EII_TEST_STALL_NS=t makes the epilogue's first wait run out after t ns (bounded-wait
+    // abort path; the call then reports EII_ERR_DEVICE and the handle stays usable)
+    if (const char* st = getenv("EII_TEST_STALL_NS")) ep.test_stall_ns = strtoull(st, nullptr, 10);
     return launch_gemm_p<EPI_LINEAR>(e, P, tmA, tmB, ep, e->stream, EII_K_GEMM_LINEAR);
 }
 
@@ -1544,6 +1550,110 @@ int eii_logits(eii_engine* e, const int64_t* x, int rows, int64_t* logits) {
     if (rc == EII_OK) rc = check_device_error(e, e->stream);
     free_list(tmp);
     return rc;
+}
+
+}  // extern "C"
+
+// =========================================================================== device-resident linear
+// A contraction with fixed int8 weights (Model.linear, python/intref.py:186-190, with W, f_in,
+// f_out and bits_out bound once) run on device-resident activations: the weights and the per-column
+// (m, shift) table are uploaded once at plan creation, like the model's own weights; each run splits
+// the int32 activation values into byte planes (a plan-owned workspace) and runs the tcgen05 GEMM
+// with the EPI_SWEEP epilogue (int32 outputs, optional per-row digests of out and of the exact acc).
+struct eii_linear_plan {
+    eii_engine* e = nullptr;
+    int N = 0, K = 0, P = 0, bits_in = 0, bits_out = 0, fast = 0;
+    int8_t* w = nullptr;
+    int2* msh = nullptr;
+    CUtensorMap tmB;
+    std::vector<void*> mem;
+    uint8_t* planes = nullptr;
+    size_t planes_cap = 0;
+};
+
+extern "C" {
+
+int eii_linear_plan_open(eii_engine* e, const int8_t* W, const int64_t* m, const int64_t* n, int N, int K,
+                         int bits_in, int f_in, int f_out, int bits_out, eii_linear_plan** out) {
+    if (!e || !W || !m || !n || !out) return fail(EII_ERR_ARG, "null argument to eii_linear_plan_open");
+    if (K < 32 || K > 1536 || K % 32 != 0) return fail(EII_ERR_ARG, "K must be a multiple of 32 in [32, 1536] (got %d)", K);
+    if (N < 16 || N % 16 != 0 || N > VOCAB) return fail(EII_ERR_ARG, "N must be a multiple of 16 in [16, %d] (got %d)", VOCAB, N);
+    if (bits_in != 16 && bits_in != 32) return fail(EII_ERR_ARG, "bits_in must be 16 or 32 (got %d)", bits_in);
+    if (bits_out < 2 || bits_out > 32) return fail(EII_ERR_ARG, "bits_out must be in [2, 32] for int32 outputs (got %d)", bits_out);
+    std::vector<int2> msh(N);
+    for (int j = 0; j < N; ++j) {
+        if (m[j] < 0 || m[j] > INT32_MAX) return fail(EII_ERR_ARG, "m[%d] = %lld outside [0, 2^31)", j, (long long)m[j]);
+        msh[j] = make_int2((int)m[j], (int)(n[j] + f_in - f_out));
+    }
+    TRY(check_col_shifts(msh, "linear plan", -1));
+    CK(cudaSetDevice(e->device));
+    eii_linear_plan* p = new eii_linear_plan;
+    p->e = e; p->N = N; p->K = K; p->P = bits_in / 8; p->bits_in = bits_in; p->bits_out = bits_out;
+    p->fast = cols_fast(msh) ? 1 : 0;
+    int rc = dalloc(p->mem, &p->w, (size_t)N * K);
+    if (rc == EII_OK) rc = dalloc(p->mem, &p->msh, (size_t)N);
+    if (rc == EII_OK && (cudaMemcpy(p->w, W, (size_t)N * K, cudaMemcpyHostToDevice) != cudaSuccess ||
+                         cudaMemcpy(p->msh, msh.data(), (size_t)N * sizeof(int2), cudaMemcpyHostToDevice) != cudaSuccess))
+        rc = fail(EII_ERR_CUDA, "weight upload failed");
+    if (rc == EII_OK) rc = map_2d(&p->tmB, p->w, K, N, p->P == 4 ? BN_P4 : 128);
+    if (rc != EII_OK) {
+        free_list(p->mem);
+        delete p;
+        return rc;
+    }
+    *out = p;
+    return EII_OK;
+}
+
+int eii_linear_plan_run(eii_linear_plan* p, const int32_t* a_dev, int M, int32_t* out_dev, int64_t ld_out,
+                        uint64_t* dig_out_dev, uint64_t* dig_acc_dev, void* stream) {
+    if (!p || !a_dev || !out_dev) return fail(EII_ERR_ARG, "null argument to eii_linear_plan_run");
+    if (M < 1) return fail(EII_ERR_ARG, "M must be >= 1 (got %d)", M);
+    if ((reinterpret_cast<uintptr_t>(a_dev) & 15) || (reinterpret_cast<uintptr_t>(out_dev) & 15))
+        return fail(EII_ERR_ARG, "a_dev and out_dev must be 16-byte aligned");
+    if (ld_out < p->N || ld_out % 4 != 0) return fail(EII_ERR_ARG, "ld_out must be >= N (%d) and a multiple of 4", p->N);
+    eii_engine* e = p->e;
+    CK(cudaSetDevice(e->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+    const size_t need = (size_t)p->P * M * p->K;
+    if (need > p->planes_cap) {
+        for (auto it = p->mem.begin(); it != p->mem.end(); ++it)
+            if (*it == p->planes) { CK(cudaFree(*it)); p->mem.erase(it); break; }
+        p->planes = nullptr;
+        p->planes_cap = 0;
+        TRY(dalloc(p->mem, &p->planes, need));
+        p->planes_cap = need;
+    }
+    if (dig_out_dev) CK(cudaMemsetAsync(dig_out_dev, 0, sizeof(uint64_t) * M, st));
+    if (dig_acc_dev) CK(cudaMemsetAsync(dig_acc_dev, 0, sizeof(uint64_t) * M, st));
+    const int64_t count = (int64_t)M * p->K;
+    {
+        ProfScope ps(e, EII_K_SPLIT_PLANES, st);
+        const int64_t n16 = count / 16;
+        const int64_t want = (n16 + 255) / 256, cap = (int64_t)e->num_sms * 8;
+        CK(launch_k(k_split_i32, dim3((unsigned)(want < cap ? want : cap)), dim3(256), 0, st, a_dev, count, p->P,
+                    count, p->planes, e->err_dev));
+    }
+    CUtensorMap tmA, om;
+    TRY(map_planes(&tmA, p->planes, p->K, M, p->P));
+    // output boxes: 32 rows x 32 int32 (128-byte rows) with two planes, 32 x 16 (64-byte rows) with four
+    TRY(map_out(&om, out_dev, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, p->N, M, (uint64_t)ld_out * 4, p->P == 2 ? 32 : 16, 32));
+    EpiParams ep{};
+    ep.M = M; ep.N = p->N; ep.K = p->K; ep.msh = p->msh; ep.err = e->err_dev; ep.fast = p->fast;
+    ep.logits = out_dev; ep.ld_logits = ld_out; ep.bits_out = p->bits_out;
+    ep.dig = reinterpret_cast<unsigned long long*>(dig_out_dev);
+    ep.dig_acc = reinterpret_cast<unsigned long long*>(dig_acc_dev);
+    ep.dig_b = e->dig_b;
+    TRY(launch_gemm_p<EPI_SWEEP>(e, p->P, tmA, p->tmB, ep, st, EII_K_GEMM_SWEEP, &om, &om));
+    return check_device_error(e, st);
+}
+
+void eii_linear_plan_close(eii_linear_plan* p) {
+    if (!p) return;
+    cudaSetDevice(p->e->device);
+    if (p->e->stream) cudaStreamSynchronize(p->e->stream);
+    free_list(p->mem);
+    delete p;
 }
 
 }  // extern "C"
@@ -1633,7 +1743,7 @@ extern "C" int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_i
     CK(cudaGetLastError());
     const int64_t count = (int64_t)M * K;
     k_split_planes<<<(unsigned)((count + 255) / 256 < 4096 ? (count + 255) / 256 : 4096), 256, 0, st>>>(a_dev, count, P,
-                                                                                                        count, d->planes);
+                                                                                                        count, d->planes, d->err);
     CK(cudaGetLastError());
     CUtensorMap tmA, tmB;
     TRY(map_planes(&tmA, d->planes, K, M, P));
@@ -1647,6 +1757,7 @@ extern "C" int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_i
     CK(cudaMemcpyAsync(&code, d->err, sizeof(int), cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     if (code == ERR_BAD_SHIFT) return fail(EII_ERR_ARG, "n + f_in - f_out outside [1, 62] (python/intref.py:49)");
+    if (code == ERR_BAD_INPUT) return fail(EII_ERR_ARG, "a_dev holds a value outside the signed %d-bit range", bits_in);
     if (code) return fail(EII_ERR_DEVICE, "kernel reported error %d (bounded wait timed out)", code);
     return EII_OK;
 }

@@ -28,7 +28,7 @@
 
 namespace eii {
 
-enum EpiKind : int { EPI_QKV = 0, EPI_RESID = 1, EPI_GATEUP = 2, EPI_LOGITS = 3, EPI_LINEAR = 4 };
+enum EpiKind : int { EPI_QKV = 0, EPI_RESID = 1, EPI_GATEUP = 2, EPI_LOGITS = 3, EPI_LINEAR = 4, EPI_SWEEP = 5 };
 
 // Error codes written to the engine's device error word.
 enum : int {
@@ -99,6 +99,15 @@ struct EpiParams {
     int64_t* out64;
     int64_t* acc64;
     int bits_out;
+    // EPI_SWEEP (the stand-alone contraction, python/intref.py:186-190, on device buffers):
+    //   int32 logits[row * ld_logits + col] = SAT_bits_out(RS(acc m, shift)), bits_out <= 32; optional
+    //   per-row digests  dig[row] += sum_col uint32(out) * dig_b[col]  and
+    //   dig_acc[row] += sum_col uint64(acc) * dig_b[col]  (mod 2^64, acc the exact int64 contraction).
+    unsigned long long* dig_acc;
+    // EPI_LINEAR, tests only: when non-zero, each epilogue warp first waits this many ns on a barrier
+    // that nothing arrives on, so the bounded wait runs out and the CTA takes its abort-and-drain path
+    // (error ERR_TIMEOUT_EPI); the engine sets it from EII_TEST_STALL_NS in eii_linear.
+    unsigned long long test_stall_ns;
 };
 
 constexpr int SILU_SMEM_BYTES = 48 * 1024;  // compact SiLU table capacity (int16 x 24576 or int32 x 12288)
@@ -124,8 +133,9 @@ struct GemmCfg {
     // Per-warp staging buffer for TMA tile stores (and the residual tile load): 32 rows x the warp's
     // columns.  LOGITS/RESID: int32, BN/4 columns; QKV: two 32-row x 16 int16 boxes.
     // RESID with 4 planes and 128-wide tiles keeps one 16-column chunk resident (2 KB) to fit.
+    // SWEEP: as LOGITS with two planes; with four (and 128-wide tiles) one 16-column chunk (2 KB) to fit.
     static constexpr int STG_BYTES = KIND == EPI_LOGITS ? (BN / 4) * 4 * 32
-                                     : KIND == EPI_RESID ? ((P == 4 && BN == 128) ? 2048 : (BN / 4) * 4 * 32)
+                                     : (KIND == EPI_RESID || KIND == EPI_SWEEP) ? ((P == 4 && BN == 128) ? 2048 : (BN / 4) * 4 * 32)
                                      : (KIND == EPI_QKV ? 2048 : 0);
     static constexpr int STAGES = (P == 2) ? (KIND == EPI_LINEAR ? 4 : 3) : (BN == 128 ? 2 : 3);
     static constexpr int EPI_WARPS = 16;  // 4 per TMEM lane quadrant, each owns 32 tile columns
@@ -133,7 +143,7 @@ struct GemmCfg {
     static constexpr int THREADS = 64 + EPI_THREADS;
     static constexpr int BAR_BYTES = 512;
     static constexpr int COLP_BYTES = 2 * BN * 16;  // per-tile column (m, shift, 2^(shift-1), m << 8), x2
-    static constexpr int DIGW_BYTES = KIND == EPI_LOGITS ? 2 * BN * 8 : 0;  // per-tile digest column weights, x2
+    static constexpr int DIGW_BYTES = (KIND == EPI_LOGITS || KIND == EPI_SWEEP) ? 2 * BN * 8 : 0;  // per-tile digest column weights, x2
     static constexpr int SILU_BYTES = KIND == EPI_GATEUP ? SILU_SMEM_BYTES : 0;
     // QKV: the RoPE cos/sin rows of positions pos0 .. pos0 + T - 1 (T <= 128), rows padded to 36 words
     static constexpr int ROPE_BYTES = KIND == EPI_QKV ? 2 * ROPE_SMEM_ROWS * ROPE_SMEM_PITCH * 4 : 0;
@@ -317,7 +327,8 @@ template <int P, int KIND, int MODE>
 __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc, int m_blk, int n_blk, int cg,
                                               int quad, int lane, const int4* colp, const void* silu_tab,
                                               uint8_t* stg, const EpiMaps& maps, uint64_t* xbar, uint32_t& xphase,
-                                              volatile int* abort, const uint64_t* digw, uint64_t& dsum) {
+                                              volatile int* abort, const uint64_t* digw, uint64_t& dsum,
+                                              uint64_t& asum) {
     constexpr int BN = (P == 4) ? BN_P4 : 128;
     const int row = m_blk * 128 + quad * 32 + lane;
     const bool row_ok = row < ep.M;
@@ -579,6 +590,79 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 bulk_commit();
             }
         }
+    } else if constexpr (KIND == EPI_SWEEP) {
+        // out = SAT_bits_out(RS(acc m, shift)) on this warp's 32 rows x NCOL columns, int32 TMA tile
+        // stores; digests of out and of the exact acc per row in registers (dsum, asum).  With one
+        // resident 16-column chunk (SCH == 1) each chunk is stored before the next is staged.
+        constexpr int NCOL = BN / 4, NCH = NCOL / 16;
+        constexpr int SCH = GemmCfg<P, KIND>::STG_BYTES / 2048;
+        constexpr int S = 64 * SCH;  // staging row bytes
+        const int row0 = m_blk * 128 + quad * 32;
+        if (lane == 0) bulk_wait_read0();  // the previous tile's store has read the staging buffer
+        __syncwarp();
+#pragma unroll 1
+        for (int ch = 0; ch < NCH; ++ch) {
+            const int tc = NCOL * cg + 16 * ch;
+            const int gc = n0 + tc;
+            if (gc >= ep.N) break;
+            const int slot = SCH == 1 ? 0 : ch;
+            if (SCH == 1 && ch > 0) {
+                if (lane == 0) bulk_wait_read0();
+                __syncwarp();
+            }
+            // 16 columns in sub-rounds of SW (8 with four planes: the accumulators stay in registers)
+            constexpr int SW = P == 4 ? 8 : 16;
+            int32_t o[16];
+#pragma unroll
+            for (int h = 0; h < 16; h += SW) {
+                uint32_t v[P][SW];
+                load_planes<P, SW>(tacc + tc + h, v);
+                if (row_ok) {
+#pragma unroll
+                    for (int i = 0; i < SW; ++i) {
+                        const int4 cp = colp[tc + h + i];
+                        if constexpr (MODE >= 1) {
+                            int32_t hi;
+                            uint32_t lo;
+                            shr31(mulround<P, SW>(v, i, cp), cp.y, hi, lo);
+                            o[h + i] = sat_hl(hi, lo, ep.bits_out);
+                        } else {
+                            o[h + i] = static_cast<int32_t>(requant_gen<P, SW>(v, i, cp, ep.bits_out));
+                        }
+                    }
+                    if (ep.dig_acc) {
+#pragma unroll
+                        for (int i = 0; i < SW; ++i) asum += static_cast<uint64_t>(combine<P, SW>(v, i)) * digw[tc + h + i];
+                    }
+                }
+            }
+            if (row_ok) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<int4*>(stg + stg_off<S>(lane, 4 * slot + q)) = *reinterpret_cast<int4*>(&o[4 * q]);
+                if (ep.dig) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) dsum += static_cast<uint64_t>(static_cast<uint32_t>(o[i])) * digw[tc + i];
+                }
+            }
+            if (SCH == 1) {
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0 && row0 < ep.M) {
+                    tma_store_2d(maps.c0, stg, gc, row0);
+                    bulk_commit();
+                }
+            }
+        }
+        if (SCH > 1) {
+            fence_async_smem();
+            __syncwarp();
+            const int gc0 = n0 + NCOL * cg;
+            if (lane == 0 && row0 < ep.M && gc0 < ep.N) {
+                tma_store_2d(maps.c0, stg, gc0, row0);
+                bulk_commit();
+            }
+        }
     } else {
         constexpr int NCOL = BN / 4;  // columns of this warp: 32 (P = 2) or 16 (P = 4)
         if constexpr (KIND == EPI_LOGITS) {
@@ -677,7 +761,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
     // Tile schedule shared by the three roles: LOGITS walks a contiguous run of tiles (rows stay on
     // one CTA for many N tiles, so the digest sums stay in registers); the others stride by the grid.
     int t_first = blockIdx.x, t_end = tiles, t_step = gridDim.x;
-    if constexpr (KIND == EPI_LOGITS) {
+    if constexpr (KIND == EPI_LOGITS || KIND == EPI_SWEEP) {
         t_first = static_cast<int>(static_cast<int64_t>(blockIdx.x) * tiles / gridDim.x);
         t_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * tiles / gridDim.x);
         t_step = 1;
@@ -826,17 +910,27 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
         }
         griddep_wait();  // outputs (and RESID's residual input) are shared with earlier kernels
         int acc_iter = 0;
-        int dig_m = -1;     // LOGITS digest: row block whose sums this lane holds
-        uint64_t dsum = 0;  //   sum over the columns seen so far of uint32(logit) * dig_b[col]
+        // LOGITS / SWEEP digests: row block whose sums this lane holds, and the sums over the columns
+        // seen so far of uint32(out) * dig_b[col] (dsum) and, SWEEP only, of uint64(acc) * dig_b[col] (asum)
+        int dig_m = -1;
+        uint64_t dsum = 0, asum = 0;
+        const bool digs = (KIND == EPI_LOGITS && ep.dig) || (KIND == EPI_SWEEP && (ep.dig || ep.dig_acc));
         auto dig_flush = [&]() {
             const int r = dig_m * 128 + quad * 32 + lane;
-            if (dig_m >= 0 && r < ep.M)
-                atomicAdd(ep.dig + r / ep.T, static_cast<unsigned long long>(dsum * __ldg(ep.dig_a + ep.pos0 + r % ep.T)));
+            if (dig_m >= 0 && r < ep.M) {
+                if constexpr (KIND == EPI_SWEEP) {
+                    if (ep.dig) atomicAdd(ep.dig + r, static_cast<unsigned long long>(dsum));
+                    if (ep.dig_acc) atomicAdd(ep.dig_acc + r, static_cast<unsigned long long>(asum));
+                } else {
+                    atomicAdd(ep.dig + r / ep.T, static_cast<unsigned long long>(dsum * __ldg(ep.dig_a + ep.pos0 + r % ep.T)));
+                }
+            }
             dsum = 0;
+            asum = 0;
         };
         for (int t = t_first; t < t_end; t += t_step, ++acc_iter) {
             const int m_blk = t / num_n, n_blk = t % num_n;
-            if (KIND == EPI_LOGITS && ep.dig && m_blk != dig_m) {
+            if (digs && m_blk != dig_m) {
                 dig_flush();
                 dig_m = m_blk;
             }
@@ -848,7 +942,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             int4* colp = colp_all + (acc_iter & 1) * C::BN;
             if (acc_iter == 0 && et < C::BN) {
                 colp[et] = col_params(ep, n_blk * C::BN + et);
-                if (KIND == EPI_LOGITS && ep.dig) digw_all[et] = dig_weight(ep, n_blk * C::BN + et);
+                if (digs) digw_all[et] = dig_weight(ep, n_blk * C::BN + et);
             }
             // RESID: the residual tile of this warp (32 rows x BN/4 int32) goes into its staging buffer by
             // TMA while the accumulators are being computed.
@@ -862,7 +956,12 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
                     tma_load_2d(stg, &tmC0, &xbar[e], gc0, row0);
                 }
             }
-            bool ok = mbar_wait(&acc_full[buf], acc_phase, abort, ep.err, ERR_TIMEOUT_EPI);
+            bool ok = true;
+            if constexpr (KIND == EPI_LINEAR) {
+                if (ep.test_stall_ns && acc_iter == 0)  // xbar is unused by this kind: its phase never completes
+                    ok = mbar_wait(&xbar[e], 0, abort, ep.err, ERR_TIMEOUT_EPI, ep.test_stall_ns);
+            }
+            ok = ok && mbar_wait(&acc_full[buf], acc_phase, abort, ep.err, ERR_TIMEOUT_EPI);
             if (xload) {
                 ok = ok && mbar_wait(&xbar[e], xphase, abort, ep.err, ERR_TIMEOUT_EPI);
                 xphase ^= 1;
@@ -874,24 +973,24 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             if (et < C::BN && t + t_step < t_end) {
                 const int nc = ((t + t_step) % num_n) * C::BN + et;
                 colp_all[((acc_iter + 1) & 1) * C::BN + et] = col_params(ep, nc);
-                if (KIND == EPI_LOGITS && ep.dig) digw_all[((acc_iter + 1) & 1) * C::BN + et] = dig_weight(ep, nc);
+                if (digs) digw_all[((acc_iter + 1) & 1) * C::BN + et] = dig_weight(ep, nc);
             }
             const uint64_t* digw = digw_all + (acc_iter & 1) * C::BN;
             const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
             if (KIND != EPI_LINEAR && ep.narrow && (KIND == EPI_QKV || KIND == EPI_GATEUP))
                 epilogue_tile<P, KIND, 2>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                          xphase, abort, digw, dsum);
+                                          xphase, abort, digw, dsum, asum);
             else if (KIND != EPI_LINEAR && KIND != EPI_QKV && ep.fast)
                 epilogue_tile<P, KIND, 1>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                          xphase, abort, digw, dsum);
+                                          xphase, abort, digw, dsum, asum);
             else
                 epilogue_tile<P, KIND, 0>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                          xphase, abort, digw, dsum);
+                                          xphase, abort, digw, dsum, asum);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
-        if (KIND == EPI_LOGITS && ep.dig) dig_flush();
+        if (digs) dig_flush();
         if (lane == 0) bulk_wait0();  // this warp's tile stores are complete before the CTA exits
     }
     tc_fence_before();

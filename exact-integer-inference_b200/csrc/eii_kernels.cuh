@@ -14,7 +14,7 @@ constexpr int N_HEADS = 9, N_KV = 3, HEAD_DIM = 64, ROPE_POS = 512, DMAX = 12 * 
 constexpr int F_RES = 15, F_SCORE = 7;
 constexpr int64_t EPS_S = 6184753;  // round(1e-5 * 576 * 2^30), python/intref.py:37
 
-enum : int { ERR_BAD_TOKEN = 201, ERR_BAD_SHIFT = 202 };
+enum : int { ERR_BAD_TOKEN = 201, ERR_BAD_SHIFT = 202, ERR_BAD_INPUT = 203 };
 
 // --------------------------------------------------------------------------- embedding
 // x[t,c] = RS(emb_q[id,c] * emb_m[id], emb_n[id] - 15)   (python/intref.py:163-166)
@@ -605,12 +605,49 @@ __global__ void __launch_bounds__(DECODE_THREADS) k_attention_decode(AttnDecodeP
 // --------------------------------------------------------------------------- plane split
 // int64 activations [M,K] (values within b = 8P bits) -> P byte planes [P][M][K].
 __global__ void k_split_planes(const int64_t* __restrict__ a, int64_t count, int P, int64_t plane_stride,
-                               uint8_t* __restrict__ planes) {
+                               uint8_t* __restrict__ planes, int* err) {
+    const int64_t lo = -(int64_t(1) << (8 * P - 1)), hi = (int64_t(1) << (8 * P - 1)) - 1;
+    bool bad = false;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t v = a[i];
+        bad |= v < lo || v > hi;
         for (int p = 0; p < P; ++p) planes[p * plane_stride + i] = plane_byte(v, p);
     }
+    if (bad && err) atomicCAS(err, 0, ERR_BAD_INPUT);
+}
+
+// int32 activations [M,K] (values within b = 8P bits; count a multiple of 16, 16-byte aligned) ->
+// P byte planes [P][M][K]: 16 values per thread and step (four 16-byte loads, one 16-byte store per
+// plane).  A value outside the signed b-bit range records ERR_BAD_INPUT.
+__global__ void k_split_i32(const int32_t* __restrict__ a, int64_t count, int P, int64_t plane_stride,
+                            uint8_t* __restrict__ planes, int* err) {
+    const int32_t lo = P == 2 ? -32768 : INT32_MIN, hi = P == 2 ? 32767 : INT32_MAX;
+    bool bad = false;
+    const int64_t n16 = count / 16;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int32_t v[16];
+        const int4* src = reinterpret_cast<const int4*>(a) + 4 * i;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) *reinterpret_cast<int4*>(&v[4 * q]) = __ldg(src + q);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) bad |= v[j] < lo || v[j] > hi;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            if (p >= P) break;
+            const uint32_t sel = p | ((4 + p) << 4);
+            uint32_t w[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t t01 = __byte_perm(static_cast<uint32_t>(v[4 * q]), static_cast<uint32_t>(v[4 * q + 1]), sel);
+                const uint32_t t23 = __byte_perm(static_cast<uint32_t>(v[4 * q + 2]), static_cast<uint32_t>(v[4 * q + 3]), sel);
+                w[q] = __byte_perm(t01, t23, 0x5410);
+            }
+            *reinterpret_cast<uint4*>(planes + p * plane_stride + 16 * i) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    if (bad && err) atomicCAS(err, 0, ERR_BAD_INPUT);
 }
 
 __global__ void k_i64_to_i32(const int64_t* __restrict__ a, int64_t n, int32_t* __restrict__ o) {

@@ -152,6 +152,30 @@ int eii_logits(eii_engine* e, const int64_t* x, int rows, int64_t* logits);
 int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const int8_t* W, const int64_t* m,
                const int64_t* n, int N, int f_in, int f_out, int bits_out, int64_t* out, int64_t* acc);
 
+/* Device-resident Model.linear (python/intref.py:186-190) with the weights bound once: the path of
+ * the stand-alone contraction sweep (int8 weights x wide activations at M up to 262144 rows).
+ * eii_linear_plan_open uploads W int8 [N][K] and the per-column (m, n + f_in - f_out) table (m, n
+ * host int64 [N]) to the handle's device; N a multiple of 16 up to 49152, K a multiple of 32 up to
+ * 1536, bits_in 16 or 32, bits_out <= 32.  eii_linear_plan_run then computes, on device buffers,
+ *   out_dev[r * ld_out + c] = SAT_bits_out(RS(acc[r][c] * m[c], n[c] + f_in - f_out)),  int32,
+ *   acc = a_dev W^T exact,  a_dev int32 [M][K] (values within signed bits_in, else EII_ERR_ARG),
+ * and, when the pointers are not null, per-row digests (uint64 [M], zeroed by the call)
+ *   dig_out_dev[r] = sum_c uint32(out[r][c]) * mix64(2^32 + c),
+ *   dig_acc_dev[r] = sum_c uint64(acc[r][c]) * mix64(2^32 + c)      (mod 2^64)
+ * with mix64 the digest weight of eii_forward, so a caller can check an M x N result (51.5 GB at
+ * M = 262144, N = 49152) and its exact int64 accumulators without copying them.  a_dev and out_dev
+ * must be 16-byte aligned and ld_out a multiple of 4.  `stream` is a cudaStream_t (null = the
+ * handle's stream); the call returns once the work is complete.  The plan owns a byte-plane
+ * workspace of (bits_in / 8) * M * K bytes, grown on demand; calls on a plan and its engine are
+ * serialised by the caller.  No reference counterpart as an API (the reference's linear is the
+ * numpy Model.linear on host arrays; eii_linear is its host-buffer drop-in). */
+typedef struct eii_linear_plan eii_linear_plan;
+int eii_linear_plan_open(eii_engine* e, const int8_t* W, const int64_t* m, const int64_t* n, int N, int K,
+                         int bits_in, int f_in, int f_out, int bits_out, eii_linear_plan** out);
+int eii_linear_plan_run(eii_linear_plan* p, const int32_t* a_dev, int M, int32_t* out_dev, int64_t ld_out,
+                        uint64_t* dig_out_dev, uint64_t* dig_acc_dev, void* stream);
+void eii_linear_plan_close(eii_linear_plan* p);
+
 /* Allocation-free linear: the same contraction and requantisation as eii_linear, for callers that
  * must not allocate device memory -- code whose device memory is owned by another allocator (a
  * framework or serving runtime that reserved the GPU up front) or that cannot afford the implicit
@@ -159,7 +183,9 @@ int eii_linear(eii_engine* e, const int64_t* a, int M, int K, int bits_in, const
  * cudaFree or other allocating routine and needs no engine handle.  No counterpart in the
  * reference.
  *   All pointers are device pointers on the CURRENT device: a_dev int64 [M][K] (values within
- *   signed bits_in, 16 or 32), w_dev int8 [N][K] (16-byte aligned), m_dev and n_dev int64 [N],
+ *   signed bits_in, 16 or 32; a value outside it, or a column shift n + f_in - f_out outside
+ *   [1, 62], is reported as EII_ERR_ARG after the call has run), w_dev int8 [N][K] (16-byte
+ *   aligned), m_dev and n_dev int64 [N],
  *   out_dev int64 [M][N], acc_dev int64 [M][N] or null.  `stream` is a cudaStream_t (null = the
  *   legacy default stream); the call returns after the work on it has finished.
  *   Scratch: the activation byte planes, the per-column multiplier/shift table and an error word
@@ -192,18 +218,19 @@ int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_in, const in
 #define EII_K_GEMM_LOGITS 7
 #define EII_K_DIGEST 8 /* no launches: the digest is fused into the logits GEMM */
 #define EII_K_GEMM_LINEAR 9
-#define EII_NUM_KERNEL_KINDS 10
+#define EII_K_SPLIT_PLANES 10 /* int32 activations -> byte planes (eii_linear_plan_run) */
+#define EII_K_GEMM_SWEEP 11   /* the contraction of eii_linear_plan_run */
+#define EII_NUM_KERNEL_KINDS 12
 const char* eii_kernel_name(int kind);
 int eii_profile_enable(eii_engine* e, int on);
 int eii_profile_read(eii_engine* e, int kind, double* total_ms, int64_t* launches);
 
 /* Sequences per chunk that eii_forward / eii_forward_device use for n_seq sequences of T tokens
- * (the engine works through the sequences in chunks of its device workspace).  A chunk holds about
- * EII_CHUNK_ROWS rows (environment, default 65536); unless that variable is set, the sequence count
- * is rounded to a multiple of the device's SM count when it is at least half of it, so that the
- * attention (one CTA per sequence and KV group) runs in whole waves and the persistent GEMMs give
- * every SM the same number of tiles.  Returns the count, or minus an error code for a null engine
- * or a non-positive size.  No reference counterpart (the reference runs one sequence at a time). */
+ * (the engine works through the sequences in chunks of its device workspace).  The sequences are
+ * split into the fewest chunks of at most 65536 rows, all of (nearly) equal size; the environment
+ * variable EII_CHUNK_ROWS=R sets chunks of exactly R / T sequences instead.  Returns the count, or
+ * minus an error code for a null engine or a non-positive size.  No reference counterpart (the
+ * reference runs one sequence at a time). */
 int eii_chunk_sequences(const eii_engine* e, int n_seq, int T);
 
 #ifdef __cplusplus

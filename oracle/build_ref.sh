@@ -3,10 +3,11 @@
 # reference checkout, into oracle/_ref/intref.  TEST INFRASTRUCTURE: the binary is the reference
 # implementation used as a parity cross-check and as bench.py's CPU baseline; nothing in the
 # shipped engine links or runs it.  Flags follow the reference's c/Makefile (-O2 -Wall -Wextra).
-#   sh oracle/build_ref.sh [REFERENCE_DIR]      (default: $EII_REFERENCE or /root/reference)
+#   sh oracle/build_ref.sh [REFERENCE_DIR]
+# (default: $EII_REFERENCE, else a directory named `reference` beside this repository)
 set -eu
-REF="${1:-${EII_REFERENCE:-/root/reference}}"
 HERE="$(cd "$(dirname "$0")" && pwd)"
+REF="${1:-${EII_REFERENCE:-$HERE/../../reference}}"
 SRC="$REF/c/intref.c"
 if [ ! -f "$SRC" ]; then
     echo "build_ref: $SRC not found; oracle/_ref/intref not rebuilt" >&2

@@ -1,12 +1,13 @@
 """Derive oracle/formats.json from the reference's format proposal (TEST INFRASTRUCTURE).
 
-Runs only where the reference checkout is present (default /root/reference, or the
-EII_REFERENCE environment variable).  It restates Model.fmt (python/intref.py:154-160):
+Runs only where the reference checkout is present ($EII_REFERENCE, or a directory named
+`reference` beside this repository).  It restates Model.fmt (python/intref.py:154-160):
 a site-layer whose class starts with "flagged" is INT32 with f = 31 - k in wide mode,
 every other site is INT16 with f = 15 - k; the final norm output uses f = 15 - k(final_out|30)
 (python/intref.py:296).  The 12 sites are written in model.bin's fmt[24] order
 (python/export_vectors.py:34).  Narrow mode (wide=False) and the residual grid exponents of
-Model._grid (python/intref.py:303-308) are kept too.
+Model._grid (python/intref.py:303-308) are kept too, and the class and k of every site-layer of the
+proposal (the `prop` table a Model subclass reads in its own fmt / _grid overrides).
 """
 import json, os, sys
 
@@ -15,7 +16,8 @@ SITES = ("norm1_out", "q_proj", "k_proj", "v_proj", "q_rope", "k_rope", "attn_ct
 
 
 def main():
-    ref = os.environ.get("EII_REFERENCE", "/root/reference")
+    here = os.path.dirname(os.path.abspath(__file__))
+    ref = os.environ.get("EII_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(here)), "reference")
     prop = json.load(open(os.path.join(ref, "results", "scaling_proposal.json")))["sites"]
     out = {"source": "results/scaling_proposal.json of the reference", "wide": [], "narrow": []}
     for l in range(30):
@@ -28,6 +30,8 @@ def main():
             out[mode].append(fm)
     out["f_y"] = 15 - prop["final_out|30"]["k"]
     out["resid_k"] = {s: [prop[f"{s}|{l}"]["k"] for l in range(30)] for s in ("resid_in", "resid_out")}
+    # the class and k of every site-layer: the drop-in Model's `prop` (python/intref.py:138-139)
+    out["sites"] = {name: {"class": e["class"], "k": int(e["k"])} for name, e in sorted(prop.items())}
     here = os.path.dirname(os.path.abspath(__file__))
     # one copy for the oracle, one for the engine package's synthetic-model writer
     for path in (os.path.join(here, "formats.json"),

@@ -1,7 +1,8 @@
 """Generate the golden fixtures in tests/golden/ by running the REFERENCE itself.
 
-Runs only in a container that has the reference checkout (default /root/reference, or
-$EII_REFERENCE); the fixtures it writes are committed so the tests never need the reference.
+Runs only where the reference checkout is present: $EII_REFERENCE, or a directory named
+`reference` beside this repository.  The fixtures it writes are committed so the tests never need
+the reference.
 
 What it does, for the seeded synthetic model of oracle/synth.py:
   1. imports the reference's python/intref.py and python/common.py, and patches the two loader
@@ -23,10 +24,14 @@ What it does, for the seeded synthetic model of oracle/synth.py:
   7. runs intref.Model(wide).forward(ids, narrow_residual) on the t24 tokens for the narrow comparison
      modes and records the logits digests (narrow_t24.json);
   8. records digests of the reference's exp, RoPE and SiLU tables for every format pair of its
-     format table (tables.json).
+     format table (tables.json);
+  9. runs intref.Model.linear on the contraction sweep of exact-integer-inference_b200/sweep.py
+     (four weight shapes, M = 512 ... 262144 rows, seeded activations over the full INT16 / INT32
+     ranges) and records the block digests of acc and of the requantised outputs
+     (gemm_sweep_large.json; about ten minutes of numpy).
 
     python tests/golden/make_golden.py [--keep DIR] [--skip-subset] [--only-trace] [--only-narrow]
-                                       [--only-tables]
+                                       [--only-tables] [--only-sweep]
 """
 import argparse
 import hashlib
@@ -45,7 +50,17 @@ sys.path.insert(0, REPO)
 from oracle import synth  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("EII_REFERENCE", "/root/reference")
+
+
+def reference_dir():
+    """The reference checkout: $EII_REFERENCE, else `reference` beside this repository."""
+    ref = os.environ.get("EII_REFERENCE") or os.path.join(os.path.dirname(REPO), "reference")
+    if not os.path.isdir(os.path.join(ref, "python")):
+        raise SystemExit(f"reference checkout not found at {ref} (set EII_REFERENCE)")
+    return ref
+
+
+REF = None
 SETS = (("t24", 64, 24, False), ("t128", 64, 128, False), ("t160", 100, 160, True))
 SUBSET_SEED = 2
 SUBSET_N = 64
@@ -65,7 +80,9 @@ def sha256_file(p):
 
 
 def import_reference():
+    global REF
     import torch
+    REF = reference_dir()
     sys.path.insert(0, os.path.join(REF, "python"))
     import common
     import intref
@@ -170,6 +187,74 @@ def tables_golden(intref):
     print("tables done:", len(keys), "SiLU keys", flush=True)
 
 
+_SWEEP_JOB = {}
+
+
+def _sweep_block(b):
+    """Row digests of block b of the current sweep case through the reference's Model.linear."""
+    j = _SWEEP_JOB
+    sweep = j["sweep"]
+    a_blk = sweep.activation_block(j["ci"], j["M"], b, j["K"], j["bits_in"]).astype(np.int64)
+    step = 1024 if j["N"] > 4096 else sweep.BLOCK
+    da, do, first8 = [], [], None
+    for r in range(0, a_blk.shape[0], step):
+        out, acc = j["linear"](a_blk[r:r + step], 1 << (j["bits_in"] - 1), j["W"], j["f_in"], j["f_out"], j["bits_out"])
+        da.append(sweep.row_digests(acc, j["N"], False))
+        do.append(sweep.row_digests(out, j["N"], True))
+        if first8 is None:
+            first8 = np.asarray(out[2, :8]).tolist()
+    return np.concatenate(da), np.concatenate(do), first8
+
+
+def sweep_golden(torch, common, intref):
+    """Block digests of the reference's Model.linear (python/intref.py:186-190) over the contraction
+    sweep of sweep.py: acc (the exact int64 matmul_exact) and out = SAT(RS(acc m, n + f_in - f_out))."""
+    sys.path.insert(0, os.path.join(REPO, "exact-integer-inference_b200"))
+    import sweep
+    patch(torch, common, intref, False)
+    M_ = intref.Model(wide=True)
+    cases = []
+    for ci, (name, (wname, wl), (si, li), outs) in enumerate(sweep.CASES):
+        W = (M_.emb_q, M_.emb_m, M_.emb_n) if wname == "embed" else M_.layers[wl][wname]
+        if si == "final_out":
+            bits_in, f_in = 16, 15 - M_.prop["final_out|30"]["k"]
+        else:
+            bits_in, f_in = M_.fmt(si, li)
+        if outs[0] == "grid":
+            f_out, bits_out = outs[1], outs[2]
+        else:
+            bits_out, f_out = M_.fmt(outs[0], outs[1])
+        assert (bits_in, f_in, f_out, bits_out) == sweep.case_formats(ci), name
+        N, K = W[0].shape
+        for M in sweep.MS:
+            t0 = time.time()
+            dacc = np.empty(M, np.uint64)
+            dout = np.empty(M, np.uint64)
+            _SWEEP_JOB.update(ci=ci, M=M, K=K, N=N, W=W, bits_in=bits_in, f_in=f_in, f_out=f_out, bits_out=bits_out,
+                              linear=M_.linear, sweep=sweep)
+            nb = sweep.blocks(M)
+            if nb > 1:  # blocks in forked workers (no GPU here); numpy's elementwise passes are single-threaded
+                import multiprocessing as mp
+                with mp.get_context("fork").Pool(min(nb, 6)) as pool:
+                    res = pool.map(_sweep_block, range(nb))
+            else:
+                res = [_sweep_block(0)]
+            first8 = res[0][2]
+            for b, (da, do, _) in enumerate(res):
+                dacc[sweep.BLOCK * b:sweep.BLOCK * b + len(da)] = da
+                dout[sweep.BLOCK * b:sweep.BLOCK * b + len(do)] = do
+            ba, bo = sweep.block_digests(dacc, M), sweep.block_digests(dout, M)
+            cases.append({"name": name, "case": ci, "M": M, "N": int(N), "K": int(K), "bits_in": bits_in, "f_in": f_in,
+                          "f_out": f_out, "bits_out": bits_out, "acc": f"{sweep.total(ba):016x}",
+                          "out": f"{sweep.total(bo):016x}", "acc_blocks": sweep.hexes(ba), "out_blocks": sweep.hexes(bo),
+                          "out_row2_first8": first8, "seconds": round(time.time() - t0, 1)})
+            print(name, M, round(time.time() - t0, 1), "s", flush=True)
+    with open(os.path.join(HERE, "gemm_sweep_large.json"), "w") as f:
+        json.dump({"note": "digests (hex, mod 2^64) defined in exact-integer-inference_b200/sweep.py, of the reference's "
+                   "Model.linear on the sweep's seeded activations", "seed": sweep.SEED, "block_rows": sweep.BLOCK,
+                   "cases": cases}, f, indent=1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--keep", default=None, help="directory to keep the exported vector sets in")
@@ -177,8 +262,12 @@ def main():
     ap.add_argument("--only-trace", action="store_true")
     ap.add_argument("--only-narrow", action="store_true")
     ap.add_argument("--only-tables", action="store_true")
+    ap.add_argument("--only-sweep", action="store_true")
     args = ap.parse_args()
     torch, common, intref = import_reference()
+    if args.only_sweep:
+        sweep_golden(torch, common, intref)
+        return
     if args.only_tables:
         tables_golden(intref)
         return

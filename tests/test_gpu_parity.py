@@ -383,19 +383,44 @@ def test_forward_t24_unsigned_gated_planes(base_model, base_model_path, monkeypa
         e.close()
 
 
-def test_chunk_sequences_fill_whole_waves(eng, monkeypatch):
-    """Without EII_CHUNK_ROWS the sequences per chunk are a multiple of the SM count (about 65536
-    rows), so the attention's (sequence, KV group) items and the GEMM row blocks spread evenly over
-    the SMs; the variable sets the chunk exactly; the count never exceeds the request."""
-    import torch
+def test_chunk_sequences_equal_chunks(eng, monkeypatch):
+    """Without EII_CHUNK_ROWS the sequences are split into the fewest chunks of at most 65536 rows,
+    all of (nearly) equal size (no small remainder chunk); the variable sets the chunk exactly; the
+    count never exceeds the request."""
     import _eii
-    sms = torch.cuda.get_device_properties(0).multi_processor_count
     monkeypatch.delenv("EII_CHUNK_ROWS", raising=False)
-    cs = eng.chunk_sequences(4096, 128)
-    assert cs % sms == 0 and abs(cs * 128 - 65536) <= sms * 128 // 2
+    assert eng.chunk_sequences(4096, 128) == 512   # 8 chunks of 512 (one GPU)
+    assert eng.chunk_sequences(512, 128) == 512    # the shard of one of 8 GPUs: one chunk
+    assert eng.chunk_sequences(513, 128) == 257    # two chunks of 257 and 256, not 512 + 1
     assert eng.chunk_sequences(3, 128) == 3
-    assert eng.chunk_sequences(100000, 1) % sms == 0
+    assert eng.chunk_sequences(160, 512) == 80     # 128 sequences fit 65536 rows: two chunks of 80
+    for n, T in ((4096, 128), (1000, 160), (100000, 1), (7, 512)):
+        cs = eng.chunk_sequences(n, T)
+        chunks = -(-n // cs)
+        assert cs * T <= 65536 or cs == 1
+        assert n - (chunks - 1) * cs >= cs - chunks   # the last chunk is within one sequence per chunk
     monkeypatch.setenv("EII_CHUNK_ROWS", "16384")
     assert eng.chunk_sequences(4096, 128) == 128
     with pytest.raises(_eii.EiiError):
         eng.chunk_sequences(0, 128)
+
+
+def test_bounded_wait_timeout_reports_error_and_recovers(eng, monkeypatch):
+    """The bounded mbarrier waits: with EII_TEST_STALL_NS set, eii_linear's epilogue warps first wait
+    on a barrier nothing arrives on; the wait gives up after 2 ms, the CTA aborts (producer and MMA
+    thread drain their copies and MMAs before TMEM is freed) and the call reports EII_ERR_DEVICE.
+    The same handle then gives bit-exact results."""
+    import _eii
+    rng = np.random.default_rng(11)
+    a = rng.integers(-32768, 32768, size=(300, 576), dtype=np.int64)
+    W = rng.integers(-127, 128, size=(192, 576), dtype=np.int64).astype(np.int8)
+    m = rng.integers(1 << 13, (1 << 14) + 1, size=192, dtype=np.int64)
+    n = rng.integers(18, 30, size=192, dtype=np.int64)
+    monkeypatch.setenv("EII_TEST_STALL_NS", "2000000")
+    with pytest.raises(_eii.EiiError) as ei:
+        eng.linear(a, 16, W, m, n, 12, 10, 16)
+    assert ei.value.code == _eii.EII_ERR_DEVICE and "104" in str(ei.value)
+    monkeypatch.delenv("EII_TEST_STALL_NS")
+    out, acc = eng.linear(a, 16, W, m, n, 12, 10, 16)
+    want_out, want_acc = oracle_linear(a, 16, W, m, n, 12, 10, 16)
+    assert first_diff(acc, want_acc) is None and first_diff(out, want_out) is None

@@ -76,6 +76,27 @@ def test_oracle_gemm_sweep_matches_reference(base_model):
         assert sha256_arr(out, np.int64) == c["out_sha256"], c["name"]
 
 
+def test_oracle_large_sweep_digests_match_reference(base_model_path):
+    """The oracle's linear over the contraction sweep's seeded activations reproduces the reference's
+    block digests (tests/golden/gemm_sweep_large.json) at M = 512 for all four shapes and M = 4096
+    for the three layer shapes: this pins the activation generator, the digest definition and the
+    formats of exact-integer-inference_b200/sweep.py that the GPU tests and bench.py use."""
+    import sweep
+    for c in golden("gemm_sweep_large.json")["cases"]:
+        if c["M"] > (512 if c["N"] > 4096 else 4096):
+            continue
+        ci, M = c["case"], c["M"]
+        W, m, n = sweep.weights(base_model_path, ci)
+        bits_in, f_in, f_out, bits_out = sweep.case_formats(ci)
+        N, K = W.shape
+        a = np.concatenate([sweep.activation_block(ci, M, b, K, bits_in) for b in range(sweep.blocks(M))])
+        acc = ofw.matmul_exact(a.astype(np.int64), W, 1 << (bits_in - 1))
+        out = ofw.sat(ofw.rs(acc * m[None, :], n + f_in - f_out), bits_out)
+        assert out[2, :8].tolist() == c["out_row2_first8"], c["name"]
+        assert sweep.hexes(sweep.block_digests(sweep.row_digests(acc, N, False), M)) == c["acc_blocks"], c["name"]
+        assert sweep.hexes(sweep.block_digests(sweep.row_digests(out, N, True), M)) == c["out_blocks"], c["name"]
+
+
 def test_oracle_batched_subset_matches_reference(base_model):
     """Sequences of the 4096 x 128 batch, run as one batch through the oracle, reproduce the
     per-sequence logits the reference computed one sequence at a time."""
