@@ -599,6 +599,30 @@ def run_probe(ns):
     print(f"[probe] {ns} x {T} tokens, digest[0] = {int(digests[0].item()) & ((1 << 64) - 1):016x}")
 
 
+def run_probe_sweep(spec):
+    """One eii_linear_plan_run of sweep case NAME at M rows (spec "NAME:M"), for ncu captures of a
+    single GEMM launch; prints the case digest of the outputs."""
+    import torch
+    import _eii
+    import sweep
+    name, M = spec.split(":")
+    M = int(M)
+    ci = [c[0] for c in sweep.CASES].index(name)
+    eng = _eii.Engine(ensure_model(), 0)
+    W, m, n = sweep.weights(model_path(), ci)
+    bits_in, f_in, f_out, bits_out = sweep.case_formats(ci)
+    N, K = W.shape
+    a = torch.cat([torch.from_numpy(sweep.activation_block(ci, M, b, K, bits_in)) for b in range(sweep.blocks(M))]).cuda()
+    out = torch.empty((M, N), dtype=torch.int32, device="cuda")
+    d_out = torch.empty(M, dtype=torch.int64, device="cuda")
+    plan = _eii.LinearPlan(eng, W, m, n, bits_in, f_in, f_out, bits_out)
+    plan.run(a.data_ptr(), M, out.data_ptr(), N, d_out.data_ptr())
+    dig = sweep.total(sweep.block_digests(d_out.cpu().numpy().view(np.uint64), M))
+    plan.close()
+    eng.close()
+    print(f"[probe] {name} M={M}: out digest {dig:016x}")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -609,9 +633,14 @@ def main():
     ap.add_argument("--no-gemm-sweep", action="store_true", help="skip the contraction sweep (config 5) at N=1")
     ap.add_argument("--probe", type=int, default=0, metavar="NSEQ",
                     help="profiling target: one untimed forward of NSEQ x 128 tokens on cuda:0, then exit")
+    ap.add_argument("--probe-sweep", default=None, metavar="NAME:M",
+                    help="profiling target: one contraction-sweep GEMM (sweep.py case NAME at M rows), then exit")
     args = ap.parse_args()
     if args.probe:
         run_probe(args.probe)
+        return
+    if args.probe_sweep:
+        run_probe_sweep(args.probe_sweep)
         return
     if args.warmup < 3:
         log("[bench] note: fewer than 3 warm-up steps")
