@@ -599,6 +599,26 @@ def run_probe(ns):
     print(f"[probe] {ns} x {T} tokens, digest[0] = {int(digests[0].item()) & ((1 << 64) - 1):016x}")
 
 
+def run_probe_decode(ns):
+    """A decoder of `ns` config-4 sequences: a 64-token prompt (eii_decoder_prefill), then four
+    single-token steps (eii_decoder_step_device), for ncu captures of the decode attention."""
+    import torch
+    import _eii
+    eng = _eii.Engine(ensure_model(), 0)
+    ids = np.ascontiguousarray(token_table()[:ns, :T])
+    dec = _eii.Decoder(eng, ns, T)
+    dec.prefill(ids[:, :64], logits=False, digests=True)
+    ids_t = torch.from_numpy(np.ascontiguousarray(ids[:, 64:68].T)).cuda()
+    dig = torch.zeros((4, ns), dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for t in range(4):
+        dec.step_device(ids_t[t].data_ptr(), None, VOCAB, dig[t].data_ptr(), stream)
+    torch.cuda.synchronize()
+    dec.close()
+    eng.close()
+    print(f"[probe] decode {ns} sequences, position 64..67, digest[0][0] = {int(dig[0, 0].item()) & ((1 << 64) - 1):016x}")
+
+
 def run_probe_sweep(spec):
     """One eii_linear_plan_run of sweep case NAME at M rows (spec "NAME:M"), for ncu captures of a
     single GEMM launch; prints the case digest of the outputs."""
@@ -633,6 +653,8 @@ def main():
     ap.add_argument("--no-gemm-sweep", action="store_true", help="skip the contraction sweep (config 5) at N=1")
     ap.add_argument("--probe", type=int, default=0, metavar="NSEQ",
                     help="profiling target: one untimed forward of NSEQ x 128 tokens on cuda:0, then exit")
+    ap.add_argument("--probe-decode", type=int, default=0, metavar="NSEQ",
+                    help="profiling target: a 64-token prompt and four decoding steps of NSEQ sequences, then exit")
     ap.add_argument("--probe-sweep", default=None, metavar="NAME:M",
                     help="profiling target: one contraction-sweep GEMM (sweep.py case NAME at M rows), then exit")
     args = ap.parse_args()
@@ -641,6 +663,9 @@ def main():
         return
     if args.probe_sweep:
         run_probe_sweep(args.probe_sweep)
+        return
+    if args.probe_decode:
+        run_probe_decode(args.probe_decode)
         return
     if args.warmup < 3:
         log("[bench] note: fewer than 3 warm-up steps")

@@ -49,6 +49,9 @@ _SIGS = {
                     ctypes.c_int, ctypes.c_int, _P, _P], ctypes.c_int),
     "eii_block_trace": ([_P, ctypes.c_int, _P, ctypes.c_int, _P], ctypes.c_int),
     "eii_set_residual_grid": ([_P, _P, _P], ctypes.c_int),
+    "eii_set_residual_grid_channels": ([_P, _P, _P], ctypes.c_int),
+    "eii_rmsnorm_trace": ([_P, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P],
+                          ctypes.c_int),
     "eii_table_exp": ([_P], ctypes.c_int),
     "eii_table_silu": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, _P], ctypes.c_int),
     "eii_table_rope": ([ctypes.c_int, _P, _P], ctypes.c_int),
@@ -194,13 +197,17 @@ class Engine:
         return out
 
     def set_residual_grid(self, shift_in, shift_out):
-        """Narrow residual grid shifts per layer (k of resid_in|l, resid_out|l), or None, None for off."""
+        """Narrow residual grid shifts, per layer [30] (k of resid_in|l, resid_out|l) or per layer and
+        channel [30, 576]; None, None turns the grid off."""
         if shift_in is None and shift_out is None:
             check(lib().eii_set_residual_grid(self.h, None, None))
             return
         a = _c(shift_in, np.int32)
         b = _c(shift_out, np.int32)
-        check(lib().eii_set_residual_grid(self.h, ptr(a), ptr(b)))
+        if a.shape != b.shape or a.shape not in ((N_LAYERS,), (N_LAYERS, D_MODEL)):
+            raise EiiError(EII_ERR_ARG, f"grid shifts must be [30] or [30, 576], got {a.shape} and {b.shape}")
+        fn = lib().eii_set_residual_grid if a.ndim == 1 else lib().eii_set_residual_grid_channels
+        check(fn(self.h, ptr(a), ptr(b)))
 
     def block_trace(self, layer, x):
         """Model.block(l, x, trace) of one sequence x [T, 576] -> (new residual, {site: int64 array})."""
@@ -211,12 +218,16 @@ class Engine:
         check(lib().eii_block_trace(self.h, int(layer), ptr(x), T, ctypes.byref(tr)))
         return out["resid_out"].copy(), out
 
-    def rmsnorm(self, x, gain_q, gain_f, f_out, bits_out):
+    def rmsnorm(self, x, gain_q, gain_f, f_out, bits_out, want_trace=False):
+        """Model.rmsnorm on the GPU; with want_trace, (out, U [rows], z [rows, 576])."""
         x = _c(x, np.int64)
         g = _c(gain_q, np.int64)
         out = np.empty_like(x)
-        check(lib().eii_rmsnorm(self.h, ptr(x), x.shape[0], ptr(g), int(gain_f), int(f_out), int(bits_out), ptr(out)))
-        return out
+        U = np.empty(x.shape[0], np.int64) if want_trace else None
+        z = np.empty_like(x) if want_trace else None
+        check(lib().eii_rmsnorm_trace(self.h, ptr(x), x.shape[0], ptr(g), int(gain_f), int(f_out), int(bits_out),
+                                      ptr(out), ptr(U), ptr(z)))
+        return (out, U, z) if want_trace else out
 
     def logits(self, x):
         x = _c(x, np.int64)

@@ -203,8 +203,9 @@ struct eii_engine {
     int final_f = 0, f_y = 0, final_shift = 0;
     int fast_logits = 0;
     uint64_t *dig_a = nullptr, *dig_b = nullptr;  // logits digest weights (positions, vocabulary)
-    // narrow_residual mode: shifts of the residual grid before / after each layer (-1: off)
-    int grid_in[N_LAYERS], grid_out[N_LAYERS];
+    // narrow_residual mode: per-channel shifts of the residual grid before (grid_dev[0][l]) and after
+    // (grid_dev[1][l]) each layer, uint8 [2][N_LAYERS][D_MODEL] on the device
+    uint8_t* grid_dev = nullptr;
     bool grid_on = false;
     int32_t *exp_tab = nullptr, *rope_c = nullptr, *rope_s = nullptr;
     LayerDev L[N_LAYERS];
@@ -494,16 +495,18 @@ int trace_linear(eii_engine* e, int P, const CUtensorMap& A, bool a_blocked, con
     return launch_gemm_p<EPI_LINEAR>(e, P, A, tmB, ep, st, EII_K_GEMM_LINEAR);
 }
 
-int launch_grid(eii_engine* e, int rows, int s, cudaStream_t st) {
+// which = 0: the grid before layer l, 1: after it
+int launch_grid(eii_engine* e, int rows, int which, int l, cudaStream_t st) {
     const int64_t n = (int64_t)rows * D_MODEL;
     const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)e->num_sms * 16);
-    CK(launch_k(k_residual_grid, dim3(blocks), dim3(256), 0, st, e->x, n, s));
+    const uint8_t* s_ch = e->grid_dev + ((size_t)which * N_LAYERS + l) * D_MODEL;
+    CK(launch_k(k_residual_grid, dim3(blocks), dim3(256), 0, st, e->x, n, s_ch));
     return EII_OK;
 }
 
 int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHook* kv = nullptr,
               const TraceHook* trh = nullptr) {
-    if (e->grid_on && !trh) TRY(launch_grid(e, rows, e->grid_in[l], st));
+    if (e->grid_on && !trh) TRY(launch_grid(e, rows, 0, l, st));
     LayerDev& L = e->L[l];
     const ActMaps* am;
     TRY(act_maps(e, rows, &am));
@@ -596,7 +599,7 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     ep.a_blocked = 1; ep.sd_flags = sd_flags; ep.a_sd = sd_flags != nullptr;
     TRY(launch_gemm_p<EPI_RESID>(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, L.Pm == 2 ? L.tm_d : L.tm_d64, ep, st,
                                  EII_K_GEMM_DOWN, &am->x32, &am->x16));
-    if (e->grid_on && !trh) TRY(launch_grid(e, rows, e->grid_out[l], st));
+    if (e->grid_on && !trh) TRY(launch_grid(e, rows, 1, l, st));
     return EII_OK;
 }
 
@@ -1239,22 +1242,37 @@ int eii_verify_tables(const void* data, size_t nbytes) {
     return EII_OK;
 }
 
-int eii_set_residual_grid(eii_engine* e, const int32_t* shift_in, const int32_t* shift_out) {
+static int set_grid(eii_engine* e, const int32_t* shift_in, const int32_t* shift_out, bool per_channel) {
     if (!e) return fail(EII_ERR_ARG, "engine is null");
     if (!shift_in && !shift_out) {
         e->grid_on = false;
         return EII_OK;
     }
     if (!shift_in || !shift_out) return fail(EII_ERR_ARG, "give both shift arrays, or neither to turn the grid off");
-    for (int l = 0; l < N_LAYERS; ++l)
-        if (shift_in[l] < 0 || shift_in[l] > 16 || shift_out[l] < 0 || shift_out[l] > 16)
-            return fail(EII_ERR_ARG, "residual grid shifts must be in [0, 16] (layer %d: %d, %d)", l, shift_in[l], shift_out[l]);
-    for (int l = 0; l < N_LAYERS; ++l) {
-        e->grid_in[l] = shift_in[l];
-        e->grid_out[l] = shift_out[l];
-    }
+    const int per = per_channel ? D_MODEL : 1;
+    std::vector<uint8_t> h((size_t)2 * N_LAYERS * D_MODEL);
+    for (int w = 0; w < 2; ++w)
+        for (int l = 0; l < N_LAYERS; ++l)
+            for (int c = 0; c < D_MODEL; ++c) {
+                const int32_t v = (w ? shift_out : shift_in)[(size_t)l * per + (per_channel ? c : 0)];
+                if (v < 0 || v > 16)
+                    return fail(EII_ERR_ARG, "residual grid shifts must be in [0, 16] (layer %d, channel %d: %d)", l, c, v);
+                h[((size_t)w * N_LAYERS + l) * D_MODEL + c] = (uint8_t)v;
+            }
+    CK(cudaSetDevice(e->device));
+    if (!e->grid_dev) TRY(dalloc(e->weights, &e->grid_dev, h.size()));
+    CK(cudaStreamSynchronize(e->stream));
+    CK(cudaMemcpy(e->grid_dev, h.data(), h.size(), cudaMemcpyHostToDevice));
     e->grid_on = true;
     return EII_OK;
+}
+
+int eii_set_residual_grid(eii_engine* e, const int32_t* shift_in, const int32_t* shift_out) {
+    return set_grid(e, shift_in, shift_out, false);
+}
+
+int eii_set_residual_grid_channels(eii_engine* e, const int32_t* shift_in, const int32_t* shift_out) {
+    return set_grid(e, shift_in, shift_out, true);
 }
 
 int eii_decoder_open(eii_engine* e, int n_seq, int max_T, eii_decoder** out) {
@@ -1448,8 +1466,8 @@ int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_tr
     return EII_OK;
 }
 
-int eii_rmsnorm(eii_engine* e, const int64_t* x, int rows, const int64_t* gain_q, int gain_f, int f_out, int bits_out,
-                int64_t* out) {
+int eii_rmsnorm_trace(eii_engine* e, const int64_t* x, int rows, const int64_t* gain_q, int gain_f, int f_out,
+                      int bits_out, int64_t* out, int64_t* U_out, int64_t* z_out) {
     if (!e || !x || !gain_q || !out || rows < 1) return fail(EII_ERR_ARG, "bad arguments to eii_rmsnorm");
     if (bits_out < 2 || bits_out > 64) return fail(EII_ERR_ARG, "bits_out %d out of range", bits_out);
     CK(cudaSetDevice(e->device));
@@ -1462,17 +1480,26 @@ int eii_rmsnorm(eii_engine* e, const int64_t* x, int rows, const int64_t* gain_q
     }
     std::vector<void*> tmp;
     int32_t* gd;
-    int64_t* od;
+    int64_t *od, *ud = nullptr, *zd = nullptr;
     TRY(dalloc(tmp, &gd, D_MODEL));
-    TRY(dalloc(tmp, &od, (size_t)rows * D_MODEL));
-    int rc = EII_OK;
-    if (cudaMemcpy(gd, g.data(), D_MODEL * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = fail(EII_ERR_CUDA, "gain upload");
-    if (rc == EII_OK) rc = launch_norm(e, e->x, rows, gd, 21 + gain_f - f_out, bits_out, nullptr, 0, od, e->stream);
-    if (rc == EII_OK && cudaMemcpyAsync(out, od, (size_t)rows * D_MODEL * 8, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
-        rc = fail(EII_ERR_CUDA, "download failed");
+    int rc = dalloc(tmp, &od, (size_t)rows * D_MODEL);
+    if (rc == EII_OK && U_out) rc = dalloc(tmp, &ud, (size_t)rows);
+    if (rc == EII_OK && z_out) rc = dalloc(tmp, &zd, (size_t)rows * D_MODEL);
+    if (rc == EII_OK && cudaMemcpy(gd, g.data(), D_MODEL * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = fail(EII_ERR_CUDA, "gain upload");
+    if (rc == EII_OK) rc = launch_norm(e, e->x, rows, gd, 21 + gain_f - f_out, bits_out, nullptr, 0, od, e->stream, ud, zd);
+    struct Dl { void* dst; const void* src; size_t bytes; };
+    const Dl dls[] = {{out, od, (size_t)rows * D_MODEL * 8}, {U_out, ud, (size_t)rows * 8}, {z_out, zd, (size_t)rows * D_MODEL * 8}};
+    for (const Dl& d : dls)
+        if (rc == EII_OK && d.dst && cudaMemcpyAsync(d.dst, d.src, d.bytes, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+            rc = fail(EII_ERR_CUDA, "download failed");
     if (rc == EII_OK) rc = check_device_error(e, e->stream);
     free_list(tmp);
     return rc;
+}
+
+int eii_rmsnorm(eii_engine* e, const int64_t* x, int rows, const int64_t* gain_q, int gain_f, int f_out, int bits_out,
+                int64_t* out) {
+    return eii_rmsnorm_trace(e, x, rows, gain_q, gain_f, f_out, bits_out, out, nullptr, nullptr);
 }
 
 static int linear_device(eii_engine* e, const int64_t* a_dev, int M, int K, int bits_in, const CUtensorMap& tmB,

@@ -49,14 +49,17 @@ __global__ void k_embed(const int64_t* __restrict__ ids, int M, const int8_t* __
 }
 
 // --------------------------------------------------------------------------- residual grid
-// Narrow comparison mode (python/intref.py:303-308): x = SAT16(RS(x, s)) << s, per element, with
-// the per-layer shift s = k of the residual site (0 <= s <= 16, so the result fits int32).
-__global__ void k_residual_grid(int32_t* __restrict__ x, int64_t n, int s) {
+// Narrow comparison mode (python/intref.py:303-308): x = SAT16(RS(x, s)) << s, per element, with the
+// shift s of the element's channel (s[c], 0 <= s <= 16, so the result fits int32).  The per-tensor
+// grid of the reference has one s = k of the residual site for all 576 channels; a per-channel grid
+// (a Model subclass with one exponent per channel) has its own s per channel.
+__global__ void k_residual_grid(int32_t* __restrict__ x, int64_t n, const uint8_t* __restrict__ s_ch) {
     griddep_wait();
     griddep_launch();
-    const int64_t rnd = s >= 1 ? (int64_t(1) << (s - 1)) : 0;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int s = __ldg(s_ch + i % D_MODEL);
+        const int64_t rnd = s >= 1 ? (int64_t(1) << (s - 1)) : 0;
         const int64_t r = (static_cast<int64_t>(x[i]) + rnd) >> s;
         x[i] = static_cast<int32_t>(static_cast<uint32_t>(min(max(r, int64_t(-32768)), int64_t(32767))) << s);
     }

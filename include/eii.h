@@ -89,6 +89,10 @@ int eii_verify_tables(const void* model_bin, size_t nbytes);
  * until turned off with two null pointers.  The narrow site formats (wide=False) need no engine
  * setting: they are a model.bin with INT16 formats and tables (see the drop-in Model). */
 int eii_set_residual_grid(eii_engine* e, const int32_t* shift_in, const int32_t* shift_out);
+/* Same with one shift per channel: shift_in, shift_out [30][576] (x[:, c] = SAT16(RS(x[:, c], s_c)) << s_c,
+ * s_c in [0, 16]), the grid of a Model subclass whose _grid uses per-channel exponents (the
+ * reference's ablate_perchannel.py:31-36 and ablate_layers.py:31-44 restate _grid that way). */
+int eii_set_residual_grid_channels(eii_engine* e, const int32_t* shift_in, const int32_t* shift_out);
 
 /* Incremental (cached) decoding, bit-exact with recomputation.  No reference counterpart: the
  * reference recomputes the whole prefix (python/intref.py:288-301) and lists cached decoding as
@@ -139,6 +143,10 @@ int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_tr
  * x [rows][576] int32-valued -> out [rows][576]; bits_out 16 or 32. */
 int eii_rmsnorm(eii_engine* e, const int64_t* x, int rows, const int64_t* gain_q, int gain_f, int f_out,
                 int bits_out, int64_t* out);
+/* Model.rmsnorm(x, gain, f_out, bits_out, trace) (python/intref.py:168-184): as eii_rmsnorm, plus the
+ * trace values U [rows] (the exact reciprocal root) and z [rows][576] = RS(x U, 16); either may be null. */
+int eii_rmsnorm_trace(eii_engine* e, const int64_t* x, int rows, const int64_t* gain_q, int gain_f, int f_out,
+                      int bits_out, int64_t* out, int64_t* U_out, int64_t* z_out);
 
 /* Final norm + tied logits (python/intref.py:296-300): x [rows][576] -> logits [rows][49152]
  * int64 (f = 16, no saturation). */

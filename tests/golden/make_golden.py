@@ -25,13 +25,16 @@ What it does, for the seeded synthetic model of oracle/synth.py:
      modes and records the logits digests (narrow_t24.json);
   8. records digests of the reference's exp, RoPE and SiLU tables for every format pair of its
      format table (tables.json);
+  8b. runs Model subclasses of the reference with the overrides its ablation scripts use
+     (python/ablate_narrow.py:30-40 fmt, ablate_perchannel.py:21-36 and ablate_layers.py:27-44
+     _grid) on the t24 tokens and records the logits digests (ablation_t24.json);
   9. runs intref.Model.linear on the contraction sweep of exact-integer-inference_b200/sweep.py
      (four weight shapes, M = 512 ... 262144 rows, seeded activations over the full INT16 / INT32
      ranges) and records the block digests of acc and of the requantised outputs
      (gemm_sweep_large.json; about ten minutes of numpy).
 
     python tests/golden/make_golden.py [--keep DIR] [--skip-subset] [--only-trace] [--only-narrow]
-                                       [--only-tables] [--only-sweep]
+                                       [--only-tables] [--only-sweep] [--only-ablation]
 """
 import argparse
 import hashlib
@@ -168,6 +171,70 @@ def narrow_golden(torch, common, intref):
                    "int64 logits [T, 49152] of the reference", "modes": out}, f, indent=1)
 
 
+ABLATION_SEED = 31
+
+
+def ablation_shifts():
+    """Per-channel residual-grid shifts of the per-channel variant: {(site, l): int64 [576]} in [2, 8]
+    from a seeded generator (the reference derives them from calibration maxima, which are not
+    available here; the grid arithmetic is the same)."""
+    rng = np.random.default_rng(ABLATION_SEED)
+    return {(site, l): rng.integers(2, 9, size=576).astype(np.int64) for site in ("resid_in", "resid_out")
+            for l in range(30)}
+
+
+def ablation_golden(torch, common, intref):
+    """Logits digests of reference Model subclasses with the overrides of its ablation scripts, t24."""
+    patch(torch, common, intref, False)
+    ids = synth.window_ids(64, 24)
+    F_RES = intref.F_RES
+
+    class NarrowSites(intref.Model):
+        """fmt: flagged sites stay INT32 unless narrow mode names them (ablate_narrow.py:30-40)."""
+        narrow_sites = None
+
+        def fmt(self, site, l):
+            e = self.prop[f"{site}|{l}"]
+            if e["class"].startswith("flagged"):
+                if self.wide or (self.narrow_sites is not None and site not in self.narrow_sites):
+                    return 32, 31 - e["k"]
+            return 16, 15 - e["k"]
+
+    pcs = ablation_shifts()
+
+    class ChannelGrid(intref.Model):
+        """_grid with one shift per channel (ablate_perchannel.py:31-36)."""
+        def _grid(self, x, site, l):
+            s = pcs[(site, l)][None, :]
+            half = np.where(s > 0, np.int64(1) << np.maximum(s - 1, 0), 0)
+            y = np.where(s > 0, (x + half) >> s, x)
+            return intref.sat(y, 16) << s
+
+    class SomeLayers(intref.Model):
+        """_grid applied at layers 12..28 only (ablate_layers.py:31-34)."""
+        def _grid(self, x, site, l):
+            return super()._grid(x, site, l) if 12 <= l < 29 else x
+
+    out = {}
+    M_ = NarrowSites(wide=False)
+    for name, sites in (("flagged_gated_only", {"mlp_gated"}), ("flagged_ctx_silu_only", {"attn_ctx", "silu_gate"})):
+        M_.narrow_sites = sites
+        lg = M_.forward(ids)
+        out[name] = {"logits_int64_sha256": sha256_bytes(np.ascontiguousarray(lg, dtype=np.int64).tobytes()),
+                     "logits_row0_first8": np.asarray(lg[0, :8]).tolist()}
+        print("ablation", name, flush=True)
+    for name, cls in (("channel_grid", ChannelGrid), ("grid_layers_12_28", SomeLayers)):
+        lg = cls(wide=True).forward(ids, narrow_residual=True)
+        out[name] = {"logits_int64_sha256": sha256_bytes(np.ascontiguousarray(lg, dtype=np.int64).tobytes()),
+                     "logits_row0_first8": np.asarray(lg[0, :8]).tolist()}
+        print("ablation", name, flush=True)
+    with open(os.path.join(HERE, "ablation_t24.json"), "w") as f:
+        json.dump({"window": 64, "tokens": 24, "model": "base", "channel_grid_seed": ABLATION_SEED,
+                   "note": "int64 logits [T, 49152] of reference Model subclasses (fmt / _grid overrides of its "
+                           "ablation scripts); channel_grid shifts: rng(seed).integers(2, 9, 576) per (site, layer), "
+                           "resid_in layers 0..29 then resid_out layers 0..29", "variants": out}, f, indent=1)
+
+
 def tables_golden(intref):
     """Digests of the reference's own mpmath tables (python/intref.py:66-108): exp_table(),
     rope_tables(512) and silu_table(f_g, f_s, bits_s) for every (gate, silu) format pair of the
@@ -263,10 +330,14 @@ def main():
     ap.add_argument("--only-narrow", action="store_true")
     ap.add_argument("--only-tables", action="store_true")
     ap.add_argument("--only-sweep", action="store_true")
+    ap.add_argument("--only-ablation", action="store_true")
     args = ap.parse_args()
     torch, common, intref = import_reference()
     if args.only_sweep:
         sweep_golden(torch, common, intref)
+        return
+    if args.only_ablation:
+        ablation_golden(torch, common, intref)
         return
     if args.only_tables:
         tables_golden(intref)
@@ -365,6 +436,7 @@ def main():
         print("subset done", round(time.time() - t0, 1), "s")
     trace_golden(torch, common, intref)
     narrow_golden(torch, common, intref)
+    ablation_golden(torch, common, intref)
     tables_golden(intref)
     print("vector sets in", out_root)
 

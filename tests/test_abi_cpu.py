@@ -123,20 +123,41 @@ def test_package_model_writer_matches_reference_export(tmp_path):
     assert h == golden("vectors_t24.json")["files"]["model.bin"]["sha256"]
 
 
-def test_dropin_narrow_formats(base_model_path):
-    """wide=False: the drop-in's narrow model.bin carries the narrow formats of the reference's
-    format table (python/intref.py:154-160) at every layer, and INT16 SiLU tables where silu_gate
-    was INT32 (layers 11 and 28)."""
+def test_dropin_formats_follow_fmt(base_model_path):
+    """The drop-in builds the engine's format table from Model.fmt (python/intref.py:154-160) over
+    the reference's proposal: wide mode reproduces the model.bin's own formats; narrow mode
+    (wide=False) gives the narrow table of the reference's formats, with INT16 SiLU tables where
+    silu_gate was INT32 (layers 11 and 28); a subclass fmt override (python/ablate_narrow.py:30-40)
+    changes exactly the sites it names."""
     import json
     import intref as drop
+    fmts = json.load(open(os.path.join(REPO, "oracle", "formats.json")))
     M = drop.Model.__new__(drop.Model)
-    buf = open(base_model_path, "rb").read()
-    M._parse(buf)
-    wide_silu = [Ly["silu"].copy() for Ly in M.layers]
-    M._parse(M._narrow(buf))
-    want = json.load(open(os.path.join(REPO, "oracle", "formats.json")))["narrow"]
-    assert [list(fm) for fm in M._fm] == want
-    changed = [l for l in range(30) if not np.array_equal(M.layers[l]["silu"], wide_silu[l])]
+    M._load(base_model_path, None, wide=True)
+    fm, f_y = M._format_table()
+    assert [list(r) for r in fm] == fmts["wide"] == M._fm_bin and f_y == fmts["f_y"]
+    assert M._model_bin(M._format_table()) == M._base
+    M.wide = False
+    fm, _ = M._format_table()
+    assert [list(r) for r in fm] == fmts["narrow"]
+    nb = M._model_bin(M._format_table())
+    silu = lambda buf, l: np.frombuffer(buf, np.int64, 65536, M._silu_off[l])
+    changed = [l for l in range(30) if not np.array_equal(silu(nb, l), silu(M._base, l))]
     assert changed == [11, 28]
     for l in changed:
-        assert M.layers[l]["silu"].min() >= -32768 and M.layers[l]["silu"].max() <= 32767
+        assert silu(nb, l).min() >= -32768 and silu(nb, l).max() <= 32767
+
+    class GatedOnly(drop.Model):  # only the mlp_gated flagged sites narrow (ablate_narrow.py variant)
+        def fmt(self, site, l):
+            e = self.prop[f"{site}|{l}"]
+            if e["class"].startswith("flagged") and (self.wide or site != "mlp_gated"):
+                return 32, 31 - e["k"]
+            return 16, 15 - e["k"]
+    G = GatedOnly.__new__(GatedOnly)
+    G._load(base_model_path, None, wide=False)
+    gm, _ = G._format_table()
+    mi = 2 * 11  # mlp_gated is the 12th site
+    for l in range(30):
+        for i in range(0, 24, 2):
+            want = fmts["narrow"][l] if i == mi else fmts["wide"][l]
+            assert list(gm[l][i:i + 2]) == want[i:i + 2], (l, i)
