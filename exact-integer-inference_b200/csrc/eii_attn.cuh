@@ -410,4 +410,376 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     if (warp == 0) tmem_dealloc(*tmem_slot, 512);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Integer causal attention on tcgen05 kind::i8 for 128 < T <= 512 (python/intref.py:227-254; T is
+// bounded by the 512-row RoPE table, :151).  One work item = (sequence, query head, 128-row query
+// tile qt); persistent CTAs take the items in order of decreasing qt (the tiles with the most keys
+// first).  Per item:
+//   1. S phase, for each 128-key tile kt <= qt: the K tile of the head's KV group is staged as byte
+//      planes, S = Q K^T runs as the three int32 TMEM accumulators of the short kernel (D0, D1, D2
+//      at columns 0, 128, 256), and the scores s = SAT16(RS(S, shift_s)) go to a [128][T] int16
+//      score buffer in shared memory (only the 32-key blocks that hold a key j <= i of some row of
+//      the warp's lane quadrant).  The next K tile's global loads are issued before the MMA wait.
+//   2. Row statistics over every live key j <= i, four threads per row: rowmax, then
+//      Z = sum E[rowmax - s] (0 beyond DMAX); Z >= E[0] = 2^30 and Z <= 512 * 2^30 < 2^40.
+//   3. PV phase, for each kt <= qt: P = floor((e 65536 + floor(Z/2)) / Z) of the tile's keys as two
+//      u8 planes (the P = 65536 key of a row is kept aside), V^T of the tile's keys as two planes,
+//      and ctx += P V as three TMEM accumulators at columns 0, 64, 128 (the scores have left TMEM).
+//      The next tile's P values and V loads are computed while the current tile's MMAs run.
+//   4. Epilogue as in the short kernel; the v row of a P = 65536 key is read from global memory.
+// Accumulator bounds over up to 512 keys: D0..D2 as in the short kernel (64 dims);
+// C0 <= 512 * 255 * 255 < 2^26, |C1| <= 2 * 512 * 255 * 255 < 2^27, and since
+// sum_j p1_j <= sum_j P_j / 256 <= (65536 + 512) / 256, |C2| <= 258 * 128 < 2^16: the 32-bit
+// context path below stays exact (every term below 2^31).
+constexpr int ATTNL_SS_PITCH = 528;  // int16 per score row: 1056 bytes = 264 words (8 mod 32, as the short kernel)
+constexpr int ATTNL_OFF_Q = 0, ATTNL_OFF_K = ATTN_TC_TILE, ATTNL_OFF_VT = 2 * ATTN_TC_TILE,
+              ATTNL_OFF_P = 3 * ATTN_TC_TILE, ATTNL_OFF_S = 5 * ATTN_TC_TILE,
+              ATTNL_OFF_E = ATTNL_OFF_S + 128 * ATTNL_SS_PITCH * 2;
+constexpr int ATTNL_SMEM = ATTNL_OFF_E + (DMAX + 1 + 3) * 4 + 128 * 4 + 64 + 1024;
+static_assert(ATTNL_SMEM <= 227 * 1024, "long attention shared memory");
+
+// Byte planes of 16 int16 values (two 16-byte loads) into row r, bytes 16c.. (low) and 64 + 16c.. (high)
+// of a 128-byte-row swizzled tile.
+__device__ __forceinline__ void stage_planes16(uint8_t* tile, int r, int c, const int4& a, const int4& b) {
+    const uint32_t w[8] = {static_cast<uint32_t>(a.x), static_cast<uint32_t>(a.y), static_cast<uint32_t>(a.z),
+                           static_cast<uint32_t>(a.w), static_cast<uint32_t>(b.x), static_cast<uint32_t>(b.y),
+                           static_cast<uint32_t>(b.z), static_cast<uint32_t>(b.w)};
+    const uint4 lo = make_uint4(__byte_perm(w[0], w[1], 0x6420), __byte_perm(w[2], w[3], 0x6420),
+                                __byte_perm(w[4], w[5], 0x6420), __byte_perm(w[6], w[7], 0x6420));
+    const uint4 hi = make_uint4(__byte_perm(w[0], w[1], 0x7531), __byte_perm(w[2], w[3], 0x7531),
+                                __byte_perm(w[4], w[5], 0x7531), __byte_perm(w[6], w[7], 0x7531));
+    *reinterpret_cast<uint4*>(tile + sw128(r, c * 16)) = lo;
+    *reinterpret_cast<uint4*>(tile + sw128(r, 64 + c * 16)) = hi;
+}
+
+__global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc_long(AttnParams ap, int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* Qs = sm + ATTNL_OFF_Q;    // row i = [q0 bytes | q1 bytes] of query 128 qt + i
+    uint8_t* Ks = sm + ATTNL_OFF_K;    // row j = [k0 | k1] of key 128 kt + j
+    uint8_t* VT = sm + ATTNL_OFF_VT;   // plane p at VT + p * 8192: row d, byte j (key 128 kt + j)
+    uint8_t* Ps = sm + ATTNL_OFF_P;    // plane p at Ps + p * ATTN_TC_TILE: row i, byte j
+    int16_t* Ss = reinterpret_cast<int16_t*>(sm + ATTNL_OFF_S);  // [128][ATTNL_SS_PITCH]: s of row i, key j
+    int32_t* E = reinterpret_cast<int32_t*>(sm + ATTNL_OFF_E);
+    int32_t* jstar_s = E + DMAX + 1 + 3;  // [128]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(jstar_s + 128);  // [0]: S = Q K^T, [1]: P V
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int T = ap.T;
+    const int nqt = (T + 127) / 128;
+    const int per_qt = (ap.M / T) * N_HEADS;  // (sequence, head) pairs per query-tile index
+    const int items = per_qt * nqt;
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    const int quad = warp & 3, kb = warp >> 2;  // TMEM lane quadrant; key block (S) / dim block (ctx)
+    const int i = quad * 32 + lane;             // tile row of this thread (TMEM lane)
+
+    if (warp == 0) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+    if (tid == 0) { mbar_init(bar, 1); mbar_init(bar + 1, 1); *abort = 0; fence_mbar_init(); }
+    for (int u = tid; u <= DMAX; u += ATTN_TC_THREADS) E[u] = ap.exp_tab[u];
+    griddep_wait();  // q, k, v are the previous kernel's output
+    griddep_launch();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    uint32_t phase_s = 0, phase_p = 0;
+    const uint32_t sQ = smem_u32(Qs), sK = smem_u32(Ks), sV0 = smem_u32(VT), sV1 = smem_u32(VT + 8192);
+    const uint32_t sP0 = smem_u32(Ps), sP1 = smem_u32(Ps + ATTN_TC_TILE);
+    const bool fast = !ap.generic && ap.shift_s >= 8 && ap.shift_s <= 31;
+    const int32_t srnd = fast ? (1 << (ap.shift_s - 1)) : 0;
+    // staging assignment: thread -> (row or key r = tid / 4, 16-value piece c = tid % 4)
+    const int sr = tid >> 2, sc = tid & 3;
+    // softmax assignment: row r = tid / 4, key groups G = jq + 4 m (keys 4 G .. 4 G + 3)
+    const int r = tid >> 2, jq = tid & 3;
+    // V^T assignment: key vj of the tile, dims 16 vdq .. 16 vdq + 15
+    const int vj = tid & 127, vdq = tid >> 7;
+
+    bool ok = true;
+    for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const int qt = nqt - 1 - item / per_qt;
+        const int rem = item % per_qt;
+        const int seq = rem / N_HEADS, hh = rem % N_HEADS, g = hh / 3;
+        const int64_t row0 = static_cast<int64_t>(seq) * T;
+        const int q0 = 128 * qt;
+        if (tid < 128) jstar_s[tid] = -1;
+
+        // ---- stage Q (this head, rows q0..) and K tile 0; rows past T are zero
+        {
+            int4 qa = make_int4(0, 0, 0, 0), qb = qa, ka = qa, kb2 = qa;
+            if (q0 + sr < T) {
+                const int4* src = reinterpret_cast<const int4*>(ap.q + (row0 + q0 + sr) * D_MODEL + hh * 64 + sc * 16);
+                qa = src[0];
+                qb = src[1];
+            }
+            if (sr < T) {
+                const int4* src = reinterpret_cast<const int4*>(ap.k + (row0 + sr) * 192 + g * 64 + sc * 16);
+                ka = src[0];
+                kb2 = src[1];
+            }
+            stage_planes16(Qs, sr, sc, qa, qb);
+            stage_planes16(Ks, sr, sc, ka, kb2);
+        }
+
+        // ---- S phase: scores of every key tile kt <= qt into Ss
+        for (int kt = 0; kt <= qt; ++kt) {
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+#pragma unroll
+                for (int ks = 0; ks < 2; ++ks) {
+                    const uint32_t qlo = sQ + ks * 32, qhi = sQ + 64 + ks * 32, klo = sK + ks * 32, khi = sK + 64 + ks * 32;
+                    const uint32_t acc = ks > 0 ? 1u : 0u;
+                    mma_i8(tmem + 0, smem_desc_sw128(qlo), smem_desc_sw128(klo), idesc_i8(false, false, 128), acc);
+                    mma_i8(tmem + 128, smem_desc_sw128(qhi), smem_desc_sw128(klo), idesc_i8(true, false, 128), acc);
+                    mma_i8(tmem + 128, smem_desc_sw128(qlo), smem_desc_sw128(khi), idesc_i8(false, true, 128), 1u);
+                    mma_i8(tmem + 256, smem_desc_sw128(qhi), smem_desc_sw128(khi), idesc_i8(true, true, 128), acc);
+                }
+                tc_commit(bar);
+            }
+            // the next K tile's loads overlap the MMAs
+            int4 ka = make_int4(0, 0, 0, 0), kb2 = ka;
+            if (kt < qt && 128 * (kt + 1) + sr < T) {
+                const int4* src =
+                    reinterpret_cast<const int4*>(ap.k + (row0 + 128 * (kt + 1) + sr) * 192 + g * 64 + sc * 16);
+                ka = src[0];
+                kb2 = src[1];
+            }
+            if (!__syncthreads_and(mbar_wait(bar, phase_s, abort, err, ERR_TIMEOUT_ATTN))) { ok = false; break; }
+            phase_s ^= 1;
+            tc_fence_after();
+            // key block kb of tile kt holds a live key for some row of this quadrant iff kt < qt or kb <= quad
+            if (kt < qt || kb <= quad) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const int col = kb * 32 + c * 16;
+                    uint32_t d0[16], d1[16], d2[16];
+                    tmem_ld16(tq + col, d0);
+                    tmem_ld16(tq + 128 + col, d1);
+                    tmem_ld16(tq + 256 + col, d2);
+                    tmem_wait_ld();
+                    tmem_launder(d0); tmem_launder(d1); tmem_launder(d2);
+                    uint32_t sp[8];
+#pragma unroll
+                    for (int q = 0; q < 16; q += 2) {
+                        int32_t s2[2];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const int32_t a0 = static_cast<int32_t>(d0[q + u]), a1 = static_cast<int32_t>(d1[q + u]),
+                                          a2 = static_cast<int32_t>(d2[q + u]);
+                            if (fast) {  // exact 32-bit form of RS(65536 a2 + 256 a1 + a0, sh), as the short kernel
+                                const int32_t t = a2 * 256 + a1 + ((a0 + srnd) >> 8);
+                                s2[u] = min(max(t >> (ap.shift_s - 8), -32768), 32767);
+                            } else {
+                                const int64_t S = static_cast<int64_t>(a2) * 65536 + static_cast<int64_t>(a1) * 256 +
+                                                  static_cast<int64_t>(a0);
+                                s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
+                            }
+                        }
+                        sp[q / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
+                    }
+                    uint4* dst = reinterpret_cast<uint4*>(Ss + i * ATTNL_SS_PITCH + 128 * kt + col);
+                    dst[0] = make_uint4(sp[0], sp[1], sp[2], sp[3]);
+                    dst[1] = make_uint4(sp[4], sp[5], sp[6], sp[7]);
+                }
+            }
+            tc_fence_before();
+            __syncthreads();  // Ks and the S columns are free; on the last tile, every score is written
+            tc_fence_after();
+            if (kt < qt) stage_planes16(Ks, sr, sc, ka, kb2);
+        }
+        if (!ok) break;
+
+        // ---- row statistics: rowmax and Z over the live keys j <= position of row r
+        const int rpos = q0 + r;
+        const int nk = rpos < T ? rpos + 1 : 0;
+        const int16_t* srow = Ss + r * ATTNL_SS_PITCH;
+        const int nm = nk > 4 * jq ? (nk - 4 * jq + 15) / 16 : 0;  // live key groups of this thread
+        int32_t mx = -32768;
+#pragma unroll 4
+        for (int m = 0; m < nm; ++m) {
+            const int k0 = 4 * (jq + 4 * m);
+            const uint2 sv = *reinterpret_cast<const uint2*>(srow + k0);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int32_t sk = static_cast<int16_t>((u < 2 ? sv.x : sv.y) >> (16 * (u & 1)));
+                if (k0 + u < nk) mx = max(mx, sk);
+            }
+        }
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        int64_t z = 0;
+#pragma unroll 4
+        for (int m = 0; m < nm; ++m) {
+            const int k0 = 4 * (jq + 4 * m);
+            const uint2 sv = *reinterpret_cast<const uint2*>(srow + k0);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int32_t sk = static_cast<int16_t>((u < 2 ? sv.x : sv.y) >> (16 * (u & 1)));
+                const int32_t dd = mx - sk;
+                z += (k0 + u < nk && dd <= DMAX) ? E[dd] : 0;
+            }
+        }
+        z += __shfl_xor_sync(0xffffffffu, z, 1);
+        z += __shfl_xor_sync(0xffffffffu, z, 2);
+        const int64_t halfZ = z / 2;
+        const float scale = z > 0 ? static_cast<float>(65536.0 / static_cast<double>(z)) : 0.f;
+
+        // P bytes of key tile kt for this thread's groups G = 32 kt + jq + 4 m (m = 0..7)
+        auto p_tile = [&](int kt, uint32_t (&b0)[8], uint32_t (&b1)[8]) {
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int k0 = 4 * (32 * kt + jq + 4 * m);
+                b0[m] = 0;
+                b1[m] = 0;
+                if (k0 < nk) {
+                    const uint2 sv = *reinterpret_cast<const uint2*>(srow + k0);
+                    uint32_t p[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int32_t sk = static_cast<int16_t>((u < 2 ? sv.x : sv.y) >> (16 * (u & 1)));
+                        const int32_t dd = mx - sk;
+                        const int32_t ev = (k0 + u < nk && dd <= DMAX) ? E[dd] : 0;
+                        p[u] = static_cast<uint32_t>(prob_q16_f32(ev, z, halfZ, scale));  // 0 for e = 0
+                        if (p[u] == 65536u) jstar_s[r] = k0 + u;
+                    }
+                    b0[m] = __byte_perm(__byte_perm(p[0], p[1], 0x0040), __byte_perm(p[2], p[3], 0x0040), 0x5410);
+                    b1[m] = __byte_perm(__byte_perm(p[0], p[1], 0x0051), __byte_perm(p[2], p[3], 0x0051), 0x5410);
+                }
+            }
+        };
+        auto v_load = [&](int kt, int4& va, int4& vb) {
+            va = make_int4(0, 0, 0, 0);
+            vb = va;
+            const int key = 128 * kt + vj;
+            if (key < T) {
+                const int4* src = reinterpret_cast<const int4*>(ap.v + (row0 + key) * 192 + g * 64 + vdq * 16);
+                va = src[0];
+                vb = src[1];
+            }
+        };
+
+        // ---- PV phase
+        uint32_t b0[8], b1[8];
+        int4 va, vb;
+        p_tile(0, b0, b1);
+        v_load(0, va, vb);
+        for (int kt = 0; kt <= qt; ++kt) {
+            if (kt > 0) {  // the MMAs of tile kt - 1 have read P and V^T
+                if (!__syncthreads_and(mbar_wait(bar + 1, phase_p, abort, err, ERR_TIMEOUT_ATTN))) { ok = false; break; }
+                phase_p ^= 1;
+                tc_fence_after();
+            }
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int kl = 4 * (jq + 4 * m);  // key of the tile
+                *reinterpret_cast<uint32_t*>(Ps + sw128(r, kl)) = b0[m];
+                *reinterpret_cast<uint32_t*>(Ps + ATTN_TC_TILE + sw128(r, kl)) = b1[m];
+            }
+            {
+                const int16_t* v = reinterpret_cast<const int16_t*>(&va);
+                const int16_t* v2 = reinterpret_cast<const int16_t*>(&vb);
+#pragma unroll
+                for (int d = 0; d < 16; ++d) {
+                    const int16_t x = d < 8 ? v[d] : v2[d - 8];
+                    VT[sw128(vdq * 16 + d, vj)] = static_cast<uint8_t>(x & 0xFF);
+                    VT[8192 + sw128(vdq * 16 + d, vj)] = static_cast<uint8_t>((x >> 8) & 0xFF);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint32_t acc = (kt > 0 || ks > 0) ? 1u : 0u;
+                    const uint64_t p0 = smem_desc_sw128(sP0 + ks * 32), p1 = smem_desc_sw128(sP1 + ks * 32);
+                    const uint64_t v0 = smem_desc_sw128(sV0 + ks * 32), v1 = smem_desc_sw128(sV1 + ks * 32);
+                    mma_i8(tmem + 0, p0, v0, idesc_i8(false, false, 64), acc);
+                    mma_i8(tmem + 64, p1, v0, idesc_i8(false, false, 64), acc);
+                    mma_i8(tmem + 64, p0, v1, idesc_i8(false, true, 64), 1u);
+                    mma_i8(tmem + 128, p1, v1, idesc_i8(false, true, 64), acc);
+                }
+                tc_commit(bar + 1);
+            }
+            if (kt < qt) {
+                p_tile(kt + 1, b0, b1);
+                v_load(kt + 1, va, vb);
+            }
+        }
+        if (!ok) break;
+        if (!__syncthreads_and(mbar_wait(bar + 1, phase_p, abort, err, ERR_TIMEOUT_ATTN))) { ok = false; break; }
+        phase_p ^= 1;
+        tc_fence_after();
+
+        // ---- epilogue: rows of my quadrant, dims 16 kb .. 16 kb + 15
+        {
+            const int col = kb * 16;
+            const int pos = q0 + i;
+            uint32_t c0[16], c1[16], c2[16];
+            tmem_ld16(tq + col, c0);
+            tmem_ld16(tq + 64 + col, c1);
+            tmem_ld16(tq + 128 + col, c2);
+            tmem_wait_ld();
+            tmem_launder(c0); tmem_launder(c1); tmem_launder(c2);
+            if (pos < T) {
+                const int js = jstar_s[i];
+                int16_t vs[16];
+                if (js >= 0) {  // v row of the P = 65536 key (int16, the head's KV group, these 16 dims)
+                    const int4* src = reinterpret_cast<const int4*>(ap.v + (row0 + js) * 192 + g * 64 + col);
+                    *reinterpret_cast<int4*>(&vs[0]) = src[0];
+                    *reinterpret_cast<int4*>(&vs[8]) = src[1];
+                }
+                int32_t out[16];
+                if (!ap.generic && ap.shift_c >= 8 && ap.shift_c <= 31) {
+                    const int32_t crnd = 1 << (ap.shift_c - 1);
+                    const int32_t lim = ap.bits_c < 32 ? (1 << (ap.bits_c - 1)) : 0;
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) {
+                        int32_t t = static_cast<int32_t>(c2[q]) * 256 + static_cast<int32_t>(c1[q]) +
+                                    ((static_cast<int32_t>(c0[q]) + crnd) >> 8);
+                        if (js >= 0) t += static_cast<int32_t>(vs[q]) * 256;
+                        int32_t rr = t >> (ap.shift_c - 8);
+                        if (lim) rr = min(max(rr, -lim), lim - 1);
+                        out[q] = rr;
+                    }
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) {
+                        int64_t a = static_cast<int64_t>(static_cast<int32_t>(c2[q])) * 65536 +
+                                    (static_cast<int64_t>(static_cast<int32_t>(c1[q])) * 256 +
+                                     static_cast<int64_t>(static_cast<int32_t>(c0[q])));
+                        if (js >= 0) a += static_cast<int64_t>(vs[q]) * 65536;
+                        out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
+                    }
+                }
+                const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
+                uint4* dst = reinterpret_cast<uint4*>(ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL));
+                uint32_t w[4];
+                pack_plane<0, 16>(out, w);
+                dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                pack_plane<1, 16>(out, w);
+                dst[pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                if (ap.P == 4) {
+                    pack_plane<2, 16>(out, w);
+                    dst[2 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                    pack_plane<3, 16>(out, w);
+                    dst[3 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }  // item
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(*tmem_slot, 512);
+}
+
 }  // namespace eii

@@ -228,7 +228,7 @@ struct eii_engine {
     // optional per-kernel timing (eii_profile_enable): event pairs around each launch
     bool generic_norm = false;  // EII_NORM=generic: always the generic RMSNorm kernel
     int generic_attention = 0;  // EII_ATTENTION=generic: 64-bit requantisation in the tensor-core attention
-    bool force_cuda_core_attention = false;  // EII_ATTENTION=cuda_core selects the CUDA-core kernel for T <= 128
+    bool force_cuda_core_attention = false;  // EII_ATTENTION=cuda_core selects the CUDA-core kernel (any T)
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_pool;
     std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_pending;
@@ -559,6 +559,11 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
             const int items = nseq * N_KV;
             CK(launch_k(k_attention_tc, dim3(items < e->num_sms ? items : e->num_sms), dim3(ATTN_TC_THREADS), ATTN_TC_SMEM,
                         st, ap, e->err_dev));
+        } else if (!e->force_cuda_core_attention && !trh) {
+            // 128 < T <= 512: persistent over (sequence, head, 128-row query tile) items
+            const int items = nseq * N_HEADS * ((T + 127) / 128);
+            CK(launch_k(k_attention_tc_long, dim3(items < e->num_sms ? items : e->num_sms), dim3(ATTN_TC_THREADS),
+                        ATTNL_SMEM, st, ap, e->err_dev));
         } else
             CK(launch_k(k_attention, dim3(nseq * N_KV), dim3(ATTN_WARPS * 32), attn_smem_bytes(T), st, ap));
     }
@@ -955,7 +960,9 @@ int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
     if (rc == EII_OK && (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               attn_smem_bytes(ROPE_POS)) != cudaSuccess ||
                          cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              ATTN_TC_SMEM) != cudaSuccess))
+                                              ATTN_TC_SMEM) != cudaSuccess ||
+                         cudaFuncSetAttribute(k_attention_tc_long, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              ATTNL_SMEM) != cudaSuccess))
         rc = fail(EII_ERR_CUDA, "attention smem attribute failed");
     if (const char* a = getenv("EII_ATTENTION")) {
         e->force_cuda_core_attention = strcmp(a, "cuda_core") == 0;

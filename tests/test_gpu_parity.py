@@ -186,7 +186,7 @@ def test_errors_are_reported(eng):
 
 
 def test_forward_t128_cuda_core_attention(base_model, base_model_path, monkeypatch):
-    """The CUDA-core attention kernel (used for T > 128) is also exact for T <= 128."""
+    """The CUDA-core attention kernel (the trace's kernel, and a test switch) is exact too."""
     import _eii
     monkeypatch.setenv("EII_ATTENTION", "cuda_core")
     e = _eii.Engine(base_model_path, 0)
@@ -194,6 +194,64 @@ def test_forward_t128_cuda_core_attention(base_model, base_model_path, monkeypat
         _check_set(e, base_model, "t128")
     finally:
         e.close()
+
+
+# ------------------------------------------------------------------ attention for 128 < T <= 512
+def _forward_vs_oracle(e, mdl, ids):
+    out = e.forward(ids, resid=True, logits=True)
+    for s in range(ids.shape[0]):
+        ref = ofw.forward(mdl, ids[s])
+        for l in range(30):
+            d = first_diff(out["resid"][s, l], ref["resid"][l, 0])
+            assert d is None, (s, l, d)
+        d = first_diff(out["logits"][s], ref["logits"][0].astype(np.int32))
+        assert d is None, (s, d)
+
+
+def test_forward_t512_matches_oracle(eng, base_model):
+    """The longest sequence the reference allows (its RoPE table has 512 rows): four 128-row query
+    tiles against up to four key tiles on the tensor cores, every residual and logit exact."""
+    _forward_vs_oracle(eng, base_model, synth.window_ids(7, 512)[None, :])
+
+
+def test_forward_t200_outlier_matches_oracle(eng_outlier, outlier_model):
+    """A ragged T (a 72-row last query tile) on the outlier-gain model (saturating scores)."""
+    _forward_vs_oracle(eng_outlier, outlier_model, synth.window_ids(100, 200)[None, :])
+
+
+@pytest.mark.parametrize("T", [129, 257, 300, 384, 511])
+def test_long_attention_tensor_core_equals_cuda_core(base_model_path, T):
+    """The tensor-core kernel for T > 128 against the CUDA-core kernel on several sequences of the
+    same batch (each item a (sequence, head, query tile)), logits and per-sequence digests."""
+    import _eii
+    table = synth.token_table()
+    ids = table[3:8, :T]
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        tc = e.forward(ids, logits=True, digests=True)
+    finally:
+        e.close()
+    import os
+    old = os.environ.get("EII_ATTENTION")
+    os.environ["EII_ATTENTION"] = "cuda_core"
+    try:
+        e = _eii.Engine(base_model_path, 0)
+        try:
+            cc = e.forward(ids, logits=True, digests=True)
+        finally:
+            e.close()
+    finally:
+        if old is None:
+            del os.environ["EII_ATTENTION"]
+        else:
+            os.environ["EII_ATTENTION"] = old
+    assert np.array_equal(tc["digests"], cc["digests"])
+    assert first_diff(tc["logits"], cc["logits"]) is None
+
+
+def test_decode_long_prompt_base_model(eng):
+    """Prompt of 260 tokens (three query tiles in the prefill), then 40 decoding steps."""
+    _decode_check(eng, np.stack([synth.window_ids(11, 300), synth.window_ids(12, 300)]), 260)
 
 
 @pytest.mark.parametrize("layer", [0, 11])
@@ -314,7 +372,7 @@ def test_decode_from_empty_cache(eng):
 
 
 def test_decode_outlier_model_long_prompt(eng_outlier):
-    """T = 160 (beyond the tensor-core attention's 128): prompt 150, then 10 steps."""
+    """T = 160 (the long tensor-core attention kernel for the prompt): prompt 150, then 10 steps."""
     g = golden("vectors_t160.json")
     ids = synth.window_ids(g["window"], g["tokens"])[None, :]
     _decode_check(eng_outlier, ids, 150)
