@@ -536,6 +536,8 @@ def run_ours(args):
             with tempfile.TemporaryDirectory() as td:
                 line["cpu_baseline"] = cpu_baseline_from_gpu(eng, model_path(), td)
             line["cpu_baseline_numpy"] = cpu_baseline_numpy(eng, model_path())
+        if world == 1 and not args.no_cpu_baseline:
+            line["configs_1_3"] = small_configs_bench()
         if world == 1 and not args.no_gemm_sweep:
             del logits
             torch.cuda.empty_cache()
@@ -545,6 +547,45 @@ def run_ours(args):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def small_configs_bench(repeat=20):
+    """BASELINE configs 1-3 on one GPU: one sequence per forward through eii_forward (the C ABI with
+    host buffers: ids up, int32 logits [T, 49152] down), warm, best of `repeat`; each timed forward's
+    logits are compared with the sha256 the reference's own exporter wrote (tests/golden)."""
+    import _eii
+    import synthetic
+    out = {}
+    for key, name, outlier in (("config1_t24", "t24", False), ("config2_t128", "t128", False),
+                               ("config3_t160_outlier", "t160", True)):
+        path = model_path()
+        if outlier:
+            path = os.path.join(MODEL_DIR, "outlier", "model.bin")
+            if not os.path.exists(path):
+                os.makedirs(os.path.dirname(path), exist_ok=True)
+                synthetic.write_model_bin(path, outlier=True)
+        with open(os.path.join(REPO, "tests", "golden", f"vectors_{name}.json")) as f:
+            golden = json.load(f)
+        g = golden
+        ids = np.ascontiguousarray(synthetic.token_table()[g["window"], :g["tokens"]][None, :])
+        eng = _eii.Engine(path, 0)
+        try:
+            eng.forward(ids)
+            best, exact = None, True
+            for _ in range(repeat):
+                t0 = time.perf_counter()
+                r = eng.forward(ids)
+                dt = time.perf_counter() - t0
+                best = dt if best is None else min(best, dt)
+                exact = exact and hashlib.sha256(r["logits"][0].tobytes()).hexdigest() == \
+                    golden["files"]["exp_logits.i32"]["sha256"]
+        finally:
+            eng.close()
+        out[key] = {"T": int(g["tokens"]), "ms": round(best * 1e3, 3), "tokens_per_s": round(g["tokens"] / best, 1),
+                    "logits_equal_reference": bool(exact)}
+    out["path"] = (f"eii_forward, one sequence, logits copied to host; best of {repeat} warm forwards (wall clock "
+                   "around the C call)")
+    return out
 
 
 def run_reference(args):
