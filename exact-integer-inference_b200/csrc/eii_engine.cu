@@ -34,6 +34,7 @@
 #include "eii_attn.cuh"
 #include "eii_tables.h"
 #include "eii_gemm.cuh"
+#include "eii_tgemm.cuh"
 #include "eii_kernels.cuh"
 
 using namespace eii;
@@ -88,6 +89,12 @@ struct LayerDev {
     int fast_qkv, fast_o, fast_gu, fast_d;  // fast requantisation path applies (see EpiParams::fast)
     int narrow_qkv, narrow_gu;              // requantised values provably fit int32 (EpiParams::narrow)
     int gated_sd;                           // |gated| <= 2^30: signed-digit planes (EpiParams::sd_flags)
+    // down projection on the feature-major GEMM (k_tgemm): the gate/up epilogue writes offset-binary
+    // gated planes; per-feature constants of W_d for the layer's gated format, and 2^(b-1) S_f (the
+    // trace's row-major GEMM on the same planes subtracts it)
+    int t_down = 0;
+    int4* tfeat_d = nullptr;
+    int64_t* corr_d = nullptr;
     int8_t *w_qkv, *w_o, *w_gu, *w_d;
     int2 *msh_qkv, *msh_o, *msh_gu, *msh_d;
     CUtensorMap tm_qkv, tm_o, tm_gu, tm_d, tm_o64, tm_d64;  // *64: boxes of BN_P4 rows for 4-plane GEMMs
@@ -95,6 +102,7 @@ struct LayerDev {
 
 struct ActMaps {
     CUtensorMap h, ctx2, ctx4, gated2, gated4;
+    CUtensorMap gated2t, gated4t;  // the same planes for the feature-major GEMM (all planes of BR rows per box)
     CUtensorMap x32, x16;  // residual tiles for the O/down epilogues (32 or 16 columns x 32 rows)
     CUtensorMap q, k, v;   // RoPE'd q/k and v stores of the QKV epilogue (16 int16 x 32 rows)
 };
@@ -165,6 +173,42 @@ int map_planes(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(EII_ERR_CUDA, "cuTensorMapEncodeTiled(3d K=%llu rows=%llu P=%llu) failed: %d",
+                                       (unsigned long long)K, (unsigned long long)rows, (unsigned long long)planes, (int)r);
+    return EII_OK;
+}
+
+// Planes [planes][rows][K] read by the feature-major GEMM: one box holds all `planes` planes of
+// box_rows rows of a 128-byte K block (128-byte swizzle), stacked plane-major.
+int map_planes_stacked(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint64_t planes, uint32_t box_rows) {
+    EncodeTiledFn enc;
+    TRY(get_encode(&enc));
+    cuuint64_t dims[3] = {K, rows, planes};
+    cuuint64_t strides[2] = {K, K * rows};
+    cuuint32_t box[3] = {128, box_rows, static_cast<cuuint32_t>(planes)};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(EII_ERR_CUDA, "cuTensorMapEncodeTiled(stacked K=%llu rows=%llu P=%llu) failed: %d",
+                                       (unsigned long long)K, (unsigned long long)rows, (unsigned long long)planes, (int)r);
+    return EII_OK;
+}
+
+// Row-blocked planes for the feature-major GEMM: a 4-D map over (16-byte rows of a 128-row block as
+// 8-byte pairs, plane, K chunk, row block) whose box of (box_rows rows, all planes, 8 chunks) lands in
+// shared memory as [8 K chunks][planes][box_rows][16 bytes], the planes stacked along the MMA's N.
+int map_blocked_stacked(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint64_t planes, uint32_t box_rows) {
+    EncodeTiledFn enc;
+    TRY(get_encode(&enc));
+    const uint64_t mblk = (rows + 127) / 128;
+    cuuint64_t dims[4] = {256, planes, K / 16, mblk};
+    cuuint64_t strides[3] = {128 * K * mblk, 2048, 128 * K};
+    cuuint32_t box[4] = {2 * box_rows, static_cast<cuuint32_t>(planes), 8, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, const_cast<void*>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(EII_ERR_CUDA, "cuTensorMapEncodeTiled(blocked stacked K=%llu rows=%llu P=%llu) failed: %d",
                                        (unsigned long long)K, (unsigned long long)rows, (unsigned long long)planes, (int)r);
     return EII_OK;
 }
@@ -371,6 +415,8 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
         TRY(map_blocked(&am.ctx4, e->ctx_planes, D_MODEL, rows, 4));
         TRY(map_blocked(&am.gated2, e->gated_planes, D_FF, rows, 2));
         TRY(map_blocked(&am.gated4, e->gated_planes, D_FF, rows, 4));
+        TRY(map_blocked_stacked(&am.gated2t, e->gated_planes, D_FF, rows, 2, 128));
+        TRY(map_blocked_stacked(&am.gated4t, e->gated_planes, D_FF, rows, 4, 64));
         TRY(map_out(&am.x32, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 32, 32));
         TRY(map_out(&am.x16, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 16, 32));
         TRY(map_out(&am.q, e->q, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, D_MODEL, rows, D_MODEL * 2, 16, 32));
@@ -440,6 +486,72 @@ int launch_gemm_p(eii_engine* e, int P, const CUtensorMap& A, const CUtensorMap&
     return fail(EII_ERR_FORMAT, "unsupported plane count %d", P);
 }
 
+template <int P, int KIND, bool RES>
+int launch_tgemm_r(eii_engine* e, const CUtensorMap& W, const CUtensorMap& A, const TEpi& ep, cudaStream_t st) {
+    using C = TCfg<P, RES>;
+    static std::atomic<unsigned long long> attr_done{0};  // one bit per device
+    const unsigned long long bit = (e->device >= 0 && e->device < 64) ? (1ull << e->device) : 0ull;
+    if (!bit || !(attr_done.load() & bit)) {
+        CK(cudaFuncSetAttribute(k_tgemm<P, KIND, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_done.fetch_or(bit);
+    }
+    const int tiles = ((ep.N + C::BF - 1) / C::BF) * ((ep.M + C::BR - 1) / C::BR);
+    const int grid = tiles < e->num_sms ? tiles : e->num_sms;
+    CK(launch_k(k_tgemm<P, KIND, RES>, dim3(grid), dim3(C::THREADS), C::SMEM, st, W, A, ep));
+    return EII_OK;
+}
+
+// Resident activation planes when the K blocks fit (K <= 640), unless EII_TGEMM_STREAM is set.
+template <int P, int KIND>
+int launch_tgemm(eii_engine* e, const CUtensorMap& W, const CUtensorMap& A, const TEpi& ep, cudaStream_t st,
+                 int prof_kind) {
+    ProfScope ps(e, prof_kind, st);
+    const bool stream_only = getenv("EII_TGEMM_STREAM") != nullptr;
+    if (ep.K <= 128 * TCfg<P, true>::RES_KB && !stream_only) return launch_tgemm_r<P, KIND, true>(e, W, A, ep, st);
+    return launch_tgemm_r<P, KIND, false>(e, W, A, ep, st);
+}
+
+// Per-feature constants of the feature-major GEMM for weights W [N][K], columns (m, shift) and
+// b-bit activations: (m, shift, 2^(shift-1) - 2^(b-1) S_f m) and 2^(b-1) S_f (mod 2^64), S_f the row
+// sum of W.  False (the row-major GEMM is used) when some m is 2^15 or more.
+// Split-mode constants (tg_rs_split) when the activations have two planes, every shift is in [1, 31]
+// and every feature's |acc| <= 2^(b-1) * sum_k |W[f][k]| is below 2^31: (m, shift, -2^15 S_f mod 2^32,
+// 2^(shift-1)).  False otherwise.
+bool t_features_split(const int8_t* W, int N, int K, const std::vector<int2>& msh, int bits, std::vector<int4>* feat) {
+    if (bits != 16) return false;
+    feat->resize(N);
+    for (int f = 0; f < N; ++f) {
+        const int m = msh[f].x, sh = msh[f].y;
+        if (m < 0 || m >= (1 << 15) || sh < 1 || sh > 31) return false;
+        int64_t S = 0, L1 = 0;
+        for (int k = 0; k < K; ++k) {
+            S += W[(size_t)f * K + k];
+            L1 += std::abs(static_cast<int>(W[(size_t)f * K + k]));
+        }
+        if ((L1 << (bits - 1)) >= (int64_t(1) << 31)) return false;
+        const uint32_t negc = static_cast<uint32_t>(-(static_cast<uint64_t>(S) << (bits - 1)));
+        (*feat)[f] = make_int4(m, sh, static_cast<int>(negc), static_cast<int>(1u << (sh - 1)));
+    }
+    return true;
+}
+
+bool t_features(const int8_t* W, int N, int K, const std::vector<int2>& msh, int bits, std::vector<int4>* feat,
+                std::vector<uint64_t>* corr) {
+    feat->resize(N);
+    corr->resize(N);
+    for (int f = 0; f < N; ++f) {
+        const int m = msh[f].x, sh = msh[f].y;
+        if (m < 0 || m >= (1 << 15) || sh < 1 || sh > 62) return false;
+        int64_t S = 0;
+        for (int k = 0; k < K; ++k) S += W[(size_t)f * K + k];
+        const uint64_t c = static_cast<uint64_t>(S) << (bits - 1);
+        const uint64_t kc = (uint64_t(1) << (sh - 1)) - c * static_cast<uint64_t>(m);
+        (*feat)[f] = make_int4(m, sh, static_cast<int>(static_cast<uint32_t>(kc)), static_cast<int>(static_cast<uint32_t>(kc >> 32)));
+        (*corr)[f] = c;
+    }
+    return true;
+}
+
 int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, int shift, int bits,
                 uint8_t* planes, int P, int64_t* out64, cudaStream_t st, int64_t* u_out = nullptr,
                 int64_t* z_out = nullptr, uint32_t* zero_ptr = nullptr, int zero_n = 0) {
@@ -485,13 +597,15 @@ struct TraceHook {
 };
 
 int trace_linear(eii_engine* e, int P, const CUtensorMap& A, bool a_blocked, const int8_t* W, int K, int N,
-                 const int2* msh, int bits_out, int64_t* out, int rows, cudaStream_t st, bool a_sd = false) {
+                 const int2* msh, int bits_out, int64_t* out, int rows, cudaStream_t st, bool a_sd = false,
+                 const int64_t* a_corr = nullptr) {
     CUtensorMap tmB;
     TRY(map_2d(&tmB, W, K, N, P == 4 ? BN_P4 : 128));
     EpiParams ep{};
     ep.M = rows; ep.N = N; ep.K = K; ep.msh = msh; ep.err = e->err_dev; ep.out64 = out; ep.bits_out = bits_out;
     ep.a_blocked = a_blocked ? 1 : 0;
     ep.a_sd = a_sd ? 1 : 0;
+    ep.a_corr = a_corr;  // offset-binary A planes: acc = (planes as unsigned) - a_corr[col]
     return launch_gemm_p<EPI_LINEAR>(e, P, A, tmB, ep, st, EII_K_GEMM_LINEAR);
 }
 
@@ -594,10 +708,20 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     ep.silu_count = L.silu_count; ep.silu_wide = L.silu_wide; ep.silu_d = L.silu_d; ep.bits_s = L.s.bits;
     ep.fast = L.fast_gu; ep.narrow = L.narrow_gu;
     ep.bits_m = L.m.bits; ep.gated_P = L.Pm; ep.gated_planes = e->gated_planes; ep.sd_flags = sd_flags;
+    ep.gated_offset = L.t_down;
     TRY(launch_gemm<2, EPI_GATEUP>(e, am->h, L.tm_gu, ep, st, EII_K_GEMM_GATEUP));
     if (trh)
         TRY(trace_linear(e, L.Pm, L.Pm == 2 ? am->gated2 : am->gated4, true, L.w_d, D_FF, D_MODEL, L.msh_d, 64, trh->dres,
-                         rows, st, L.gated_sd != 0));
+                         rows, st, L.gated_sd != 0, L.t_down ? L.corr_d : nullptr));
+    if (L.t_down) {
+        TEpi tp{};
+        tp.M = rows; tp.N = D_MODEL; tp.K = D_FF; tp.a_blocked = 1; tp.feat = L.tfeat_d; tp.err = e->err_dev;
+        tp.out = e->x; tp.ld = D_MODEL;
+        if (L.Pm == 2) TRY(launch_tgemm<2, EPI_RESID>(e, L.tm_d, am->gated2t, tp, st, EII_K_GEMM_DOWN));
+        else TRY(launch_tgemm<4, EPI_RESID>(e, L.tm_d, am->gated4t, tp, st, EII_K_GEMM_DOWN));
+        if (e->grid_on && !trh) TRY(launch_grid(e, rows, 1, l, st));
+        return EII_OK;
+    }
 
     ep = EpiParams{};
     ep.M = rows; ep.N = D_MODEL; ep.K = D_FF; ep.msh = L.msh_d; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_d;
@@ -926,6 +1050,15 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
             TRY(upload(e, &L.msh_d, msh.data(), D_MODEL));
             TRY(map_2d(&L.tm_d, L.w_d, D_FF, D_MODEL));
             TRY(map_2d(&L.tm_d64, L.w_d, D_FF, D_MODEL, BN_P4));
+            std::vector<int4> tf;
+            std::vector<uint64_t> tc;
+            L.t_down = !getenv("EII_DOWN_ROW_MAJOR") &&
+                       t_features(reinterpret_cast<const int8_t*>(wq[6]), D_MODEL, D_FF, msh, L.m.bits, &tf, &tc);
+            if (L.t_down) {
+                TRY(upload(e, &L.tfeat_d, tf.data(), D_MODEL));
+                TRY(upload(e, &L.corr_d, reinterpret_cast<const int64_t*>(tc.data()), D_MODEL));
+                L.gated_sd = 0;  // offset-binary planes replace the signed digits
+            }
         }
     }
     if (r.left != 0) return fail(EII_ERR_IO, "model.bin has %zu trailing bytes", r.left);
@@ -1438,14 +1571,18 @@ int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_tr
     free_list(tmp);
     if (rc != EII_OK) return rc;
     // planes -> values (row-blocked layout; low planes unsigned, top plane signed)
-    auto unblock = [&](const std::vector<uint8_t>& buf, int P, int K, int64_t stride, int64_t* out, bool all_signed) {
+    // plane bytes -> values: two's complement (top plane signed), signed digits (all planes signed), or
+    // offset binary (all planes unsigned, minus 2^(8P - 1))
+    auto unblock = [&](const std::vector<uint8_t>& buf, int P, int K, int64_t stride, int64_t* out, bool all_signed,
+                       bool offset = false) {
         for (int r = 0; r < rows; ++r)
             for (int c = 0; c < K; ++c) {
                 const int64_t off = blocked_off(r, c, K);
-                int64_t val = 0;
+                int64_t val = offset ? -((int64_t)1 << (8 * P - 1)) : 0;
                 for (int p = 0; p < P; ++p) {
                     const uint8_t b = buf[p * stride + off];
-                    val += (p == P - 1 || all_signed ? (int64_t)(int8_t)b : (int64_t)b) * ((int64_t)1 << (8 * p));
+                    const bool sgn = !offset && (p == P - 1 || all_signed);
+                    val += (sgn ? (int64_t)(int8_t)b : (int64_t)b) * ((int64_t)1 << (8 * p));
                 }
                 out[(size_t)r * K + c] = val;
             }
@@ -1468,7 +1605,7 @@ int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_tr
             if (tr->up_proj) tr->up_proj[(size_t)r * D_FF + j] = u;
             if (tr->silu_gate) tr->silu_gate[(size_t)r * D_FF + j] = silu[(size_t)(g + 32768)];
         }
-    if (tr->mlp_gated) unblock(gatedp, L.Pm, D_FF, gstride, tr->mlp_gated, L.gated_sd != 0);
+    if (tr->mlp_gated) unblock(gatedp, L.Pm, D_FF, gstride, tr->mlp_gated, L.gated_sd != 0, L.t_down != 0);
     put(tr->down_res, dres); put(tr->resid_out, xout);
     return EII_OK;
 }
@@ -1599,6 +1736,12 @@ struct eii_linear_plan {
     int N = 0, K = 0, P = 0, bits_in = 0, bits_out = 0, fast = 0;
     int8_t* w = nullptr;
     int2* msh = nullptr;
+    // feature-major GEMM (k_tgemm): per-feature (m, shift, rounding constant) and 2^(b-1) S_f; used
+    // when every m < 2^15 (always for the reference's quantiser, whose m lies in [2^13, 2^14])
+    int4* tfeat = nullptr;
+    uint64_t* tcorr = nullptr;
+    bool use_t = false;
+    int4* tfeat_split = nullptr;  // split-mode constants, or null
     CUtensorMap tmB;
     std::vector<void*> mem;
     uint8_t* planes = nullptr;
@@ -1624,11 +1767,26 @@ int eii_linear_plan_open(eii_engine* e, const int8_t* W, const int64_t* m, const
     eii_linear_plan* p = new eii_linear_plan;
     p->e = e; p->N = N; p->K = K; p->P = bits_in / 8; p->bits_in = bits_in; p->bits_out = bits_out;
     p->fast = cols_fast(msh) ? 1 : 0;
+    std::vector<int4> tfeat;
+    std::vector<uint64_t> tcorr;
+    p->use_t = !getenv("EII_SWEEP_ROW_MAJOR") && t_features(W, N, K, msh, bits_in, &tfeat, &tcorr);
     int rc = dalloc(p->mem, &p->w, (size_t)N * K);
     if (rc == EII_OK) rc = dalloc(p->mem, &p->msh, (size_t)N);
+    if (rc == EII_OK && p->use_t) rc = dalloc(p->mem, &p->tfeat, (size_t)N);
+    if (rc == EII_OK && p->use_t) rc = dalloc(p->mem, &p->tcorr, (size_t)N);
     if (rc == EII_OK && (cudaMemcpy(p->w, W, (size_t)N * K, cudaMemcpyHostToDevice) != cudaSuccess ||
                          cudaMemcpy(p->msh, msh.data(), (size_t)N * sizeof(int2), cudaMemcpyHostToDevice) != cudaSuccess))
         rc = fail(EII_ERR_CUDA, "weight upload failed");
+    std::vector<int4> tsplit;
+    if (rc == EII_OK && p->use_t && !getenv("EII_TGEMM_WIDE") && t_features_split(W, N, K, msh, bits_in, &tsplit)) {
+        rc = dalloc(p->mem, &p->tfeat_split, (size_t)N);
+        if (rc == EII_OK && cudaMemcpy(p->tfeat_split, tsplit.data(), (size_t)N * sizeof(int4), cudaMemcpyHostToDevice) != cudaSuccess)
+            rc = fail(EII_ERR_CUDA, "feature constant upload failed");
+    }
+    if (rc == EII_OK && p->use_t &&
+        (cudaMemcpy(p->tfeat, tfeat.data(), (size_t)N * sizeof(int4), cudaMemcpyHostToDevice) != cudaSuccess ||
+         cudaMemcpy(p->tcorr, tcorr.data(), (size_t)N * sizeof(uint64_t), cudaMemcpyHostToDevice) != cudaSuccess))
+        rc = fail(EII_ERR_CUDA, "feature constant upload failed");
     if (rc == EII_OK) rc = map_2d(&p->tmB, p->w, K, N, p->P == 4 ? BN_P4 : 128);
     if (rc != EII_OK) {
         free_list(p->mem);
@@ -1666,7 +1824,21 @@ int eii_linear_plan_run(eii_linear_plan* p, const int32_t* a_dev, int M, int32_t
         const int64_t n16 = count / 16;
         const int64_t want = (n16 + 255) / 256, cap = (int64_t)e->num_sms * 8;
         CK(launch_k(k_split_i32, dim3((unsigned)(want < cap ? want : cap)), dim3(256), 0, st, a_dev, count, p->P,
-                    count, p->planes, e->err_dev));
+                    count, p->planes, e->err_dev, p->use_t ? 1 : 0));
+    }
+    if (p->use_t) {
+        CUtensorMap tmA;
+        TRY(map_planes_stacked(&tmA, p->planes, p->K, M, p->P, 256 / p->P));
+        TEpi tp{};
+        tp.M = M; tp.N = p->N; tp.K = p->K; tp.feat = p->tfeat; tp.corr = p->tcorr; tp.err = e->err_dev;
+        if (p->tfeat_split) { tp.feat = p->tfeat_split; tp.split = 1; }  // (the acc digest uses tcorr)
+        tp.bits_out = p->bits_out; tp.out = out_dev; tp.ld = ld_out;
+        tp.dig = reinterpret_cast<unsigned long long*>(dig_out_dev);
+        tp.dig_acc = reinterpret_cast<unsigned long long*>(dig_acc_dev);
+        tp.dig_b = e->dig_b;
+        if (p->P == 2) TRY(launch_tgemm<2, EPI_SWEEP>(e, p->tmB, tmA, tp, st, EII_K_GEMM_SWEEP));
+        else TRY(launch_tgemm<4, EPI_SWEEP>(e, p->tmB, tmA, tp, st, EII_K_GEMM_SWEEP));
+        return check_device_error(e, st);
     }
     CUtensorMap tmA, om;
     TRY(map_planes(&tmA, p->planes, p->K, M, p->P));

@@ -86,6 +86,12 @@ struct EpiParams {
     // whose flag is 0.  a_sd: the A planes are signed digits (every plane multiplied as s8).
     uint32_t* sd_flags;
     int a_sd;
+    // EPI_GATEUP: write the gated planes in offset binary (the bytes of gated + 2^(8 gated_P - 1): all
+    // unsigned, the top byte's sign bit flipped), the layout the feature-major down GEMM reads.
+    int gated_offset;
+    // A planes in offset binary (EPI_LINEAR): every plane is multiplied as unsigned and a_corr[col] =
+    // 2^(b-1) sum_k W[col][k] is subtracted from the combined accumulator.
+    const int64_t* a_corr;
     // EPI_LOGITS: int32 out[row * ld + col] = RS(acc m, shift) (low 32 bits, no SAT)
     int32_t* logits;
     int64_t ld_logits;
@@ -483,7 +489,11 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                     }
                 }
             }
-            if (sd) {  // signed digits: the bytes of (gated + 0x808080) ^ 0x808080
+            if (ep.gated_offset) {
+                const uint32_t flip = ep.gated_P == 4 ? 0x80000000u : 0x8000u;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) gm[i] = static_cast<int32_t>(static_cast<uint32_t>(gm[i]) ^ flip);
+            } else if (sd) {  // signed digits: the bytes of (gated + 0x808080) ^ 0x808080
                 uint32_t any = 0;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -701,11 +711,14 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
             } else {  // EPI_LINEAR (generic path only)
                 int64_t* op = ep.out64 + static_cast<int64_t>(row) * ep.N + gc;
 #pragma unroll
-                for (int i = 0; i < 16; ++i) op[i] = requant_gen<P, 16>(v, i, colp[tc + i], ep.bits_out);
+                for (int i = 0; i < 16; ++i) {
+                    const int64_t acc = combine<P, 16>(v, i) - (ep.a_corr && gc + i < ep.N ? __ldg(ep.a_corr + gc + i) : 0);
+                    op[i] = sat64(rs_col(acc * static_cast<int64_t>(colp[tc + i].x), colp[tc + i].y), ep.bits_out);
+                }
                 if (ep.acc64) {
                     int64_t* ap = ep.acc64 + static_cast<int64_t>(row) * ep.N + gc;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) ap[i] = combine<P, 16>(v, i);
+                    for (int i = 0; i < 16; ++i) ap[i] = combine<P, 16>(v, i) - (ep.a_corr && gc + i < ep.N ? __ldg(ep.a_corr + gc + i) : 0);
                 }
             }
         }
@@ -847,7 +860,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
                 tc_fence_after();
                 const int n_valid = min(C::BN, ep.N - n_blk * C::BN);
                 const uint32_t id_lo = idesc_i8(ep.a_sd != 0, true, n_valid);  // low planes u8, or signed digits
-                const uint32_t id_hi = idesc_i8(true, true, n_valid);
+                const uint32_t id_hi = idesc_i8(ep.a_corr == nullptr, true, n_valid);  // top plane s8, or u8 (offset binary)
                 const uint32_t dbase = tmem_base + buf * C::ACC_COLS;
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort, ep.err, ERR_TIMEOUT_MMA_FULL)) { ok = false; break; }

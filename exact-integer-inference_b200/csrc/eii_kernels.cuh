@@ -623,9 +623,12 @@ __global__ void k_split_planes(const int64_t* __restrict__ a, int64_t count, int
 // int32 activations [M,K] (values within b = 8P bits; count a multiple of 16, 16-byte aligned) ->
 // P byte planes [P][M][K]: 16 values per thread and step (four 16-byte loads, one 16-byte store per
 // plane).  A value outside the signed b-bit range records ERR_BAD_INPUT.
+// offset_binary: the planes are those of a + 2^(b-1) (all unsigned bytes; the top byte's sign bit
+// flipped), as the feature-major GEMM (k_tgemm) reads them.
 __global__ void k_split_i32(const int32_t* __restrict__ a, int64_t count, int P, int64_t plane_stride,
-                            uint8_t* __restrict__ planes, int* err) {
+                            uint8_t* __restrict__ planes, int* err, int offset_binary) {
     const int32_t lo = P == 2 ? -32768 : INT32_MIN, hi = P == 2 ? 32767 : INT32_MAX;
+    const uint32_t flip = offset_binary ? (P == 2 ? 0x8000u : 0x80000000u) : 0u;
     bool bad = false;
     const int64_t n16 = count / 16;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
@@ -635,7 +638,10 @@ __global__ void k_split_i32(const int32_t* __restrict__ a, int64_t count, int P,
 #pragma unroll
         for (int q = 0; q < 4; ++q) *reinterpret_cast<int4*>(&v[4 * q]) = __ldg(src + q);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) bad |= v[j] < lo || v[j] > hi;
+        for (int j = 0; j < 16; ++j) {
+            bad |= v[j] < lo || v[j] > hi;
+            v[j] = static_cast<int32_t>(static_cast<uint32_t>(v[j]) ^ flip);
+        }
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
             if (p >= P) break;

@@ -115,6 +115,19 @@ __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_
 // Generic-proxy shared-memory writes become visible to the async proxy (TMA, tcgen05).
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// One lane of the (fully converged) warp is elected; the others get false.  The warp's values stay
+// warp-uniform, so a role loop run by the whole warp keeps its descriptors and coordinates in uniform
+// registers and only the elected lane issues the TMA / tcgen05 instruction.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(r));
+    return r != 0;
+}
+
 // ------------------------------------------------------------------ tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),

@@ -98,3 +98,22 @@ def test_plan_rejects_out_of_range_activation(eng, base_model_path):
         assert np.array_equal(out.cpu().numpy(), want)
     finally:
         plan.close()
+
+
+@pytest.mark.parametrize("switch", ["EII_TGEMM_WIDE", "EII_TGEMM_STREAM", "EII_SWEEP_ROW_MAJOR"])
+def test_sweep_alternative_paths_match_reference(base_model_path, monkeypatch, switch):
+    """The contraction's other code paths against the same reference digests: the feature-major GEMM
+    with 64-bit requantisation (EII_TGEMM_WIDE) and with streamed instead of resident activation planes
+    (EII_TGEMM_STREAM), and the row-major GEMM (EII_SWEEP_ROW_MAJOR)."""
+    import _eii
+    monkeypatch.setenv(switch, "1")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        for c in _cases(False):
+            if c["M"] > 4096:
+                continue
+            first8, da, do = _run_case(e, base_model_path, c)
+            assert first8 == c["out_row2_first8"], (switch, c["name"], c["M"])
+            assert da == c["acc_blocks"] and do == c["out_blocks"], (switch, c["name"], c["M"])
+    finally:
+        e.close()
