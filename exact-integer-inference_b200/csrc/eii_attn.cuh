@@ -383,6 +383,11 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                             out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
                         }
                     }
+                    if (ap.offset) {  // offset binary: the bytes of ctx + 2^(8P - 1)
+                        const uint32_t flip = ap.P == 4 ? 0x80000000u : 0x8000u;
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) out[q] = static_cast<int32_t>(static_cast<uint32_t>(out[q]) ^ flip);
+                    }
                     // row-blocked planes: this warp's 32 rows x 16 dims are 512 contiguous bytes per plane
                     const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
                     uint4* dst = reinterpret_cast<uint4*>(ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL));
@@ -756,6 +761,11 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc_long(AttnPa
                         if (js >= 0) a += static_cast<int64_t>(vs[q]) * 65536;
                         out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
                     }
+                }
+                if (ap.offset) {  // offset binary: the bytes of ctx + 2^(8P - 1)
+                    const uint32_t flip = ap.P == 4 ? 0x80000000u : 0x8000u;
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) out[q] = static_cast<int32_t>(static_cast<uint32_t>(out[q]) ^ flip);
                 }
                 const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
                 uint4* dst = reinterpret_cast<uint4*>(ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL));

@@ -95,6 +95,10 @@ struct LayerDev {
     int t_down = 0;
     int4* tfeat_d = nullptr;
     int64_t* corr_d = nullptr;
+    // O projection on the feature-major GEMM: the attention kernels write offset-binary context planes
+    int t_o = 0;
+    int4* tfeat_o = nullptr;
+    int64_t* corr_o = nullptr;
     int8_t *w_qkv, *w_o, *w_gu, *w_d;
     int2 *msh_qkv, *msh_o, *msh_gu, *msh_d;
     CUtensorMap tm_qkv, tm_o, tm_gu, tm_d, tm_o64, tm_d64;  // *64: boxes of BN_P4 rows for 4-plane GEMMs
@@ -102,7 +106,7 @@ struct LayerDev {
 
 struct ActMaps {
     CUtensorMap h, ctx2, ctx4, gated2, gated4;
-    CUtensorMap gated2t, gated4t;  // the same planes for the feature-major GEMM (all planes of BR rows per box)
+    CUtensorMap gated2t, gated4t, ctx2t, ctx4t;  // the same planes for the feature-major GEMM (all planes of BR rows per box)
     CUtensorMap x32, x16;  // residual tiles for the O/down epilogues (32 or 16 columns x 32 rows)
     CUtensorMap q, k, v;   // RoPE'd q/k and v stores of the QKV epilogue (16 int16 x 32 rows)
 };
@@ -416,6 +420,8 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
         TRY(map_blocked(&am.gated2, e->gated_planes, D_FF, rows, 2));
         TRY(map_blocked(&am.gated4, e->gated_planes, D_FF, rows, 4));
         TRY(map_blocked_stacked(&am.gated2t, e->gated_planes, D_FF, rows, 2, 128));
+        TRY(map_blocked_stacked(&am.ctx2t, e->ctx_planes, D_MODEL, rows, 2, 128));
+        TRY(map_blocked_stacked(&am.ctx4t, e->ctx_planes, D_MODEL, rows, 4, 64));
         TRY(map_blocked_stacked(&am.gated4t, e->gated_planes, D_FF, rows, 4, 64));
         TRY(map_out(&am.x32, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 32, 32));
         TRY(map_out(&am.x16, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 16, 32));
@@ -654,13 +660,13 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
         AttnDecodeParams dp{};
         dp.q = e->q; dp.kc = kv->kc; dp.vc = kv->vc; dp.max_T = kv->max_T; dp.L = kv->pos + 1; dp.exp_tab = e->exp_tab;
         dp.ctx_planes = e->ctx_planes; dp.P = L.Pc; dp.M = rows;
-        dp.shift_s = L.shift_s; dp.shift_c = L.shift_c; dp.bits_c = L.c.bits;
+        dp.shift_s = L.shift_s; dp.shift_c = L.shift_c; dp.bits_c = L.c.bits; dp.offset = L.t_o;
         ProfScope ps(e, EII_K_ATTENTION, st);
         CK(launch_k(k_attention_decode, dim3(nseq * N_KV), dim3(DECODE_THREADS), 0, st, dp));
     }
     AttnParams ap{};
     ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;
-    ap.M = rows; ap.T = T; ap.shift_s = L.shift_s; ap.shift_c = L.shift_c; ap.bits_c = L.c.bits;
+    ap.M = rows; ap.T = T; ap.shift_s = L.shift_s; ap.shift_c = L.shift_c; ap.bits_c = L.c.bits; ap.offset = L.t_o;
     ap.generic = e->generic_attention;
     if (trh) {
         ap.score_out = trh->score;
@@ -684,12 +690,20 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
 
     if (trh)
         TRY(trace_linear(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, true, L.w_o, D_MODEL, D_MODEL, L.msh_o, 64, trh->ores,
-                         rows, st));
-    ep = EpiParams{};
-    ep.M = rows; ep.N = D_MODEL; ep.K = D_MODEL; ep.msh = L.msh_o; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_o;
-    ep.a_blocked = 1;
-    TRY(launch_gemm_p<EPI_RESID>(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, L.Pc == 2 ? L.tm_o : L.tm_o64, ep, st,
-                                 EII_K_GEMM_O, &am->x32, &am->x16));
+                         rows, st, false, L.t_o ? L.corr_o : nullptr));
+    if (L.t_o) {
+        TEpi tp{};
+        tp.M = rows; tp.N = D_MODEL; tp.K = D_MODEL; tp.a_blocked = 1; tp.feat = L.tfeat_o; tp.err = e->err_dev;
+        tp.out = e->x; tp.ld = D_MODEL;
+        if (L.Pc == 2) TRY(launch_tgemm<2, EPI_RESID>(e, L.tm_o, am->ctx2t, tp, st, EII_K_GEMM_O));
+        else TRY(launch_tgemm<4, EPI_RESID>(e, L.tm_o, am->ctx4t, tp, st, EII_K_GEMM_O));
+    } else {
+        ep = EpiParams{};
+        ep.M = rows; ep.N = D_MODEL; ep.K = D_MODEL; ep.msh = L.msh_o; ep.err = e->err_dev; ep.x = e->x; ep.fast = L.fast_o;
+        ep.a_blocked = 1;
+        TRY(launch_gemm_p<EPI_RESID>(e, L.Pc, L.Pc == 2 ? am->ctx2 : am->ctx4, L.Pc == 2 ? L.tm_o : L.tm_o64, ep, st,
+                                     EII_K_GEMM_O, &am->x32, &am->x16));
+    }
     if (trh) CK(cudaMemcpyAsync(trh->xmid, e->x, sizeof(int32_t) * rows * D_MODEL, cudaMemcpyDeviceToDevice, st));
 
     uint32_t* sd_flags = L.gated_sd ? e->sd_flags + (size_t)l * ((e->cap_rows + 127) / 128) : nullptr;
@@ -1017,6 +1031,16 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
             TRY(upload(e, &L.msh_o, msh.data(), D_MODEL));
             TRY(map_2d(&L.tm_o, L.w_o, D_MODEL, D_MODEL));
             TRY(map_2d(&L.tm_o64, L.w_o, D_MODEL, D_MODEL, BN_P4));
+            std::vector<int4> tf;
+            std::vector<uint64_t> tc;
+            // (measured: with K = 576 the O projection is bound by its epilogue, where the row-major GEMM's
+            // 32-bit residual path is faster; EII_O_FEATURE_MAJOR=1 selects the feature-major GEMM)
+            L.t_o = getenv("EII_O_FEATURE_MAJOR") != nullptr &&
+                    t_features(reinterpret_cast<const int8_t*>(wq[3]), D_MODEL, D_MODEL, msh, L.c.bits, &tf, &tc);
+            if (L.t_o) {
+                TRY(upload(e, &L.tfeat_o, tf.data(), D_MODEL));
+                TRY(upload(e, &L.corr_o, reinterpret_cast<const int64_t*>(tc.data()), D_MODEL));
+            }
         }
         // gate / up interleaved per 128-row tile
         {
@@ -1594,7 +1618,7 @@ int eii_block_trace(eii_engine* e, int layer, const int64_t* x_in, int T, eii_tr
     put(tr->norm1_U, u1); put(tr->norm1_z, z1); put(tr->norm1_out, n1);
     put(tr->q_proj, q); put(tr->k_proj, k); put(tr->v_proj, v); put(tr->q_rope, qr); put(tr->k_rope, kr);
     put(tr->attn_score, score); put(tr->attn_prob, prob);
-    if (tr->attn_ctx) unblock(ctxp, L.Pc, D_MODEL, cstride, tr->attn_ctx, false);
+    if (tr->attn_ctx) unblock(ctxp, L.Pc, D_MODEL, cstride, tr->attn_ctx, false, L.t_o != 0);
     put(tr->o_res, ores); put(tr->resid_mid, xmid);
     put(tr->norm2_U, u2); put(tr->norm2_z, z2); put(tr->norm2_out, n2);
     for (int r = 0; r < rows; ++r)

@@ -316,6 +316,7 @@ struct AttnParams {
     const int32_t* exp_tab;  // [DMAX + 1]
     uint8_t* ctx_planes;     // row-blocked [P][ceil(M/128)][576/16][128 rows][16 bytes] (see blocked_off)
     int P;
+    int offset;              // context planes in offset binary (the bytes of ctx + 2^(8P-1)), as the feature-major O GEMM reads them
     int M, T;
     int shift_s, shift_c, bits_c;
     int generic;  // k_attention_tc: take the 64-bit score and context requantisation for every shift (test switch)
@@ -411,8 +412,10 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attention(AttnParams ap) {
         const int64_t r = row0 + i;
         const int col = hh * 64 + 2 * lane;
         const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
+        const int64_t off = ap.offset ? (int64_t(1) << (8 * ap.P - 1)) : 0;
         for (int p = 0; p < ap.P; ++p) {
-            const uint16_t pair = static_cast<uint16_t>(plane_byte(c0, p)) | (static_cast<uint16_t>(plane_byte(c1, p)) << 8);
+            const uint16_t pair =
+                static_cast<uint16_t>(plane_byte(c0 + off, p)) | (static_cast<uint16_t>(plane_byte(c1 + off, p)) << 8);
             *reinterpret_cast<uint16_t*>(ap.ctx_planes + p * pstride + blocked_off(r, col, D_MODEL)) = pair;
         }
         __syncwarp();
@@ -433,6 +436,7 @@ struct AttnDecodeParams {
     const int32_t* exp_tab;  // [DMAX + 1]
     uint8_t* ctx_planes;     // row-blocked planes (blocked_off), rows = sequences
     int P, M;
+    int offset;              // offset-binary context planes (AttnParams::offset)
     int shift_s, shift_c, bits_c;
 };
 
@@ -599,8 +603,10 @@ __global__ void __launch_bounds__(DECODE_THREADS) k_attention_decode(AttnDecodeP
     c1 = sat64(rs64(c1, ap.shift_c), ap.bits_c);
     const int col = (g * 3 + h) * 64 + 2 * lane;
     const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
+    const int64_t off = ap.offset ? (int64_t(1) << (8 * ap.P - 1)) : 0;
     for (int p = 0; p < ap.P; ++p) {
-        const uint16_t pair = static_cast<uint16_t>(plane_byte(c0, p)) | (static_cast<uint16_t>(plane_byte(c1, p)) << 8);
+        const uint16_t pair =
+            static_cast<uint16_t>(plane_byte(c0 + off, p)) | (static_cast<uint16_t>(plane_byte(c1 + off, p)) << 8);
         *reinterpret_cast<uint16_t*>(ap.ctx_planes + p * pstride + blocked_off(seq, col, D_MODEL)) = pair;
     }
 }

@@ -185,6 +185,36 @@ def test_errors_are_reported(eng):
     assert out["logits"].shape == (1, 3, 49152)
 
 
+@pytest.mark.parametrize("switch", ["EII_O_FEATURE_MAJOR", "EII_DOWN_ROW_MAJOR"])
+def test_forward_alternative_gemm_layouts(base_model, base_model_path, outlier_model, outlier_model_path, monkeypatch,
+                                          switch):
+    """The O projection on the feature-major GEMM (offset-binary context planes from every attention
+    kernel), and the down projection on the row-major GEMM (signed-digit gated planes): the reference's
+    digests for t24 and t160 (the long tensor-core attention), a decode that reaches the decode attention
+    kernel, and the per-site trace (the trace's row-major GEMMs read the same planes)."""
+    import _eii
+    import intref as drop
+    from test_oracle_golden import check_trace, trace_inputs
+    monkeypatch.setenv(switch, "1")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        _check_set(e, base_model, "t24")
+        _decode_check(e, synth.window_ids(64, 12)[None, :], 6)
+    finally:
+        e.close()
+    e = _eii.Engine(outlier_model_path, 0)
+    try:
+        _check_set(e, outlier_model, "t160")
+    finally:
+        e.close()
+    g, xs = trace_inputs(base_model)
+    M = drop.Model(model_bin=base_model_path)
+    for l, x in xs.items():
+        tr = {}
+        M.block(l, x, trace=tr)
+        check_trace(tr, g["layers"][str(l)])
+
+
 def test_forward_t128_cuda_core_attention(base_model, base_model_path, monkeypatch):
     """The CUDA-core attention kernel (the trace's kernel, and a test switch) is exact too."""
     import _eii
