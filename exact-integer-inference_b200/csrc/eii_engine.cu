@@ -106,7 +106,7 @@ struct LayerDev {
 
 struct ActMaps {
     CUtensorMap h, ctx2, ctx4, gated2, gated4;
-    CUtensorMap gated2t, gated4t, ctx2t, ctx4t;  // the same planes for the feature-major GEMM (all planes of BR rows per box)
+    CUtensorMap gated2t, gated4t, ctx2t, ctx4t, ht;  // the same planes for the feature-major GEMM (all planes of BR rows per box)
     CUtensorMap x32, x16;  // residual tiles for the O/down epilogues (32 or 16 columns x 32 rows)
     CUtensorMap q, k, v;   // RoPE'd q/k and v stores of the QKV epilogue (16 int16 x 32 rows)
 };
@@ -250,6 +250,10 @@ struct eii_engine {
     int32_t* final_q = nullptr;
     int final_f = 0, f_y = 0, final_shift = 0;
     int fast_logits = 0;
+    // tied logits on the feature-major GEMM (every shift in [1, 31], m < 2^15): the final norm writes
+    // offset-binary planes; per-vocabulary-row constants
+    int t_logits = 0;
+    int4* tfeat_logits = nullptr;
     uint64_t *dig_a = nullptr, *dig_b = nullptr;  // logits digest weights (positions, vocabulary)
     // narrow_residual mode: per-channel shifts of the residual grid before (grid_dev[0][l]) and after
     // (grid_dev[1][l]) each layer, uint8 [2][N_LAYERS][D_MODEL] on the device
@@ -421,6 +425,7 @@ int act_maps(eii_engine* e, int rows, const ActMaps** out) {
         TRY(map_blocked(&am.gated4, e->gated_planes, D_FF, rows, 4));
         TRY(map_blocked_stacked(&am.gated2t, e->gated_planes, D_FF, rows, 2, 128));
         TRY(map_blocked_stacked(&am.ctx2t, e->ctx_planes, D_MODEL, rows, 2, 128));
+        TRY(map_planes_stacked(&am.ht, e->h_planes, D_MODEL, rows, 2, 128));
         TRY(map_blocked_stacked(&am.ctx4t, e->ctx_planes, D_MODEL, rows, 4, 64));
         TRY(map_blocked_stacked(&am.gated4t, e->gated_planes, D_FF, rows, 4, 64));
         TRY(map_out(&am.x32, e->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, D_MODEL, rows, D_MODEL * 4, 32, 32));
@@ -560,17 +565,17 @@ bool t_features(const int8_t* W, int N, int K, const std::vector<int2>& msh, int
 
 int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, int shift, int bits,
                 uint8_t* planes, int P, int64_t* out64, cudaStream_t st, int64_t* u_out = nullptr,
-                int64_t* z_out = nullptr, uint32_t* zero_ptr = nullptr, int zero_n = 0) {
+                int64_t* z_out = nullptr, uint32_t* zero_ptr = nullptr, int zero_n = 0, bool offset = false) {
     const int rows_per_block = 16;  // 8 warps, two rows each
     ProfScope ps(e, EII_K_NORM, st);
     // the forward pass's own case (two INT16 planes, output shift in [10, 31]) has a lean kernel
     if (planes && P == 2 && bits == 16 && !out64 && !u_out && !z_out && shift >= 10 && shift <= 31 && !e->generic_norm) {
         CK(launch_k(k_rmsnorm_p16, dim3((rows + rows_per_block - 1) / rows_per_block), dim3(256), 0, st, x, rows, gain,
-                    shift, planes, zero_ptr, zero_n));
+                    shift, planes, zero_ptr, zero_n, offset ? 0x80808080u : 0u));
         return EII_OK;
     }
     CK(launch_k(k_rmsnorm, dim3((rows + rows_per_block - 1) / rows_per_block), dim3(256), 0, st, x, rows, gain, shift,
-                bits, planes, P, out64, u_out, z_out, zero_ptr, zero_n));
+                bits, planes, P, out64, u_out, z_out, zero_ptr, zero_n, offset ? 1 : 0));
     return EII_OK;
 }
 
@@ -752,7 +757,15 @@ int run_logits(eii_engine* e, int rows, int T, int32_t* logits, int64_t ld, uint
                int pos0 = 0) {
     const ActMaps* am;
     TRY(act_maps(e, rows, &am));
-    TRY(launch_norm(e, e->x, rows, e->final_q, e->final_shift, 16, e->h_planes, 2, nullptr, st));
+    TRY(launch_norm(e, e->x, rows, e->final_q, e->final_shift, 16, e->h_planes, 2, nullptr, st, nullptr, nullptr, nullptr,
+                    0, e->t_logits != 0));
+    if (e->t_logits) {
+        TEpi tp{};
+        tp.M = rows; tp.N = VOCAB; tp.K = D_MODEL; tp.feat = e->tfeat_logits; tp.err = e->err_dev;
+        tp.out = logits; tp.ld = ld; tp.T = T; tp.pos0 = pos0;
+        tp.dig = reinterpret_cast<unsigned long long*>(digests); tp.dig_a = e->dig_a; tp.dig_b = e->dig_b;
+        return launch_tgemm<2, EPI_LOGITS>(e, e->tm_emb, am->ht, tp, st, EII_K_GEMM_LOGITS);
+    }
     EpiParams ep{};
     ep.M = rows; ep.N = VOCAB; ep.K = D_MODEL; ep.msh = e->msh_logits; ep.err = e->err_dev;
     ep.logits = logits; ep.ld_logits = ld; ep.fast = e->fast_logits;
@@ -947,6 +960,16 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
         TRY(check_col_shifts(msh, "logits", -1));
         e->fast_logits = cols_fast(msh);
         TRY(upload(e, &e->msh_logits, msh.data(), VOCAB));
+        std::vector<int4> tf;
+        std::vector<uint64_t> tc;
+        bool sh31 = true;
+        for (const int2& c : msh) sh31 = sh31 && c.y >= 1 && c.y <= 31;
+        // (measured: with the fused per-sequence digest the feature-major logits GEMM is ~5% slower per clock
+        // than the row-major one at the bench's size, ~20% faster without it; EII_LOGITS_FEATURE_MAJOR=1
+        // selects it)
+        e->t_logits = getenv("EII_LOGITS_FEATURE_MAJOR") != nullptr && sh31 &&
+                      t_features(reinterpret_cast<const int8_t*>(emb_q), VOCAB, D_MODEL, msh, 16, &tf, &tc);
+        if (e->t_logits) TRY(upload(e, &e->tfeat_logits, tf.data(), VOCAB));
     }
     TRY(map_2d(&e->tm_emb, e->emb_q, D_MODEL, VOCAB));
 

@@ -115,7 +115,7 @@ __device__ __forceinline__ int64_t half_sum64(int64_t v) {
 __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain, int shift_out,
                           int bits_out, uint8_t* __restrict__ planes, int P, int64_t* __restrict__ out64,
                           int64_t* __restrict__ u_out, int64_t* __restrict__ z_out, uint32_t* __restrict__ zero_ptr,
-                          int zero_n) {
+                          int zero_n, int offset) {
     const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
     const int l = threadIdx.x & 15;
     const bool live = row < M;
@@ -175,7 +175,9 @@ __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* _
             const uint32_t w23 = (static_cast<uint32_t>(o[2]) & 0xFFFFu) | (static_cast<uint32_t>(o[3]) << 16);
             // plane 0 gets the low bytes (o0, o1, o2, o3), plane 1 the high bytes
             *reinterpret_cast<uint32_t*>(planes + static_cast<int64_t>(row) * D_MODEL + c) = __byte_perm(w01, w23, 0x6420);
-            *reinterpret_cast<uint32_t*>(planes + (static_cast<int64_t>(M) + row) * D_MODEL + c) = __byte_perm(w01, w23, 0x7531);
+            // offset-binary planes: the high byte's sign bit flipped
+            *reinterpret_cast<uint32_t*>(planes + (static_cast<int64_t>(M) + row) * D_MODEL + c) =
+                __byte_perm(w01, w23, 0x7531) ^ (offset ? 0x80808080u : 0u);
             continue;
         }
         int64_t o[4];
@@ -186,10 +188,12 @@ __global__ void k_rmsnorm(const int32_t* __restrict__ x, int M, const int32_t* _
             o[u] = sat64(rs64(z * g[u] * 3, shift_out), bits_out);
         }
         if (planes) {
+            const int64_t off = offset ? (int64_t(1) << (8 * P - 1)) : 0;  // offset-binary planes of o + 2^(8P-1)
             for (int p = 0; p < P; ++p) {
-                const uint32_t quad = static_cast<uint32_t>(plane_byte(o[0], p)) | (static_cast<uint32_t>(plane_byte(o[1], p)) << 8) |
-                                      (static_cast<uint32_t>(plane_byte(o[2], p)) << 16) |
-                                      (static_cast<uint32_t>(plane_byte(o[3], p)) << 24);
+                const uint32_t quad = static_cast<uint32_t>(plane_byte(o[0] + off, p)) |
+                                      (static_cast<uint32_t>(plane_byte(o[1] + off, p)) << 8) |
+                                      (static_cast<uint32_t>(plane_byte(o[2] + off, p)) << 16) |
+                                      (static_cast<uint32_t>(plane_byte(o[3] + off, p)) << 24);
                 *reinterpret_cast<uint32_t*>(planes + (static_cast<int64_t>(p) * M + row) * D_MODEL + c) = quad;
             }
         }
@@ -228,7 +232,7 @@ __device__ __forceinline__ void add96(uint32_t& a0, uint32_t& a1, uint32_t& a2, 
 // Four 256-thread blocks per SM (at most 64 registers): more loads in flight on the HBM-bound path.
 __global__ void __launch_bounds__(256, 4) k_rmsnorm_p16(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain,
                                                       int shift_out, uint8_t* __restrict__ planes,
-                                                      uint32_t* __restrict__ zero_ptr, int zero_n) {
+                                                      uint32_t* __restrict__ zero_ptr, int zero_n, uint32_t top_flip) {
     const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
     const int l = threadIdx.x & 15;
     const bool live = row < M;
@@ -286,7 +290,8 @@ __global__ void __launch_bounds__(256, 4) k_rmsnorm_p16(const int32_t* __restric
         const uint32_t w23 = __byte_perm(static_cast<uint32_t>(o[2]), static_cast<uint32_t>(o[3]), 0x5410);
         // plane 0 gets the low bytes (o0, o1, o2, o3), plane 1 the high bytes
         *reinterpret_cast<uint32_t*>(planes + static_cast<int64_t>(row) * D_MODEL + c) = __byte_perm(w01, w23, 0x6420);
-        *reinterpret_cast<uint32_t*>(planes + (static_cast<int64_t>(M) + row) * D_MODEL + c) = __byte_perm(w01, w23, 0x7531);
+        // top_flip = 0x80808080: offset-binary planes (the high byte's sign bit flipped)
+        *reinterpret_cast<uint32_t*>(planes + (static_cast<int64_t>(M) + row) * D_MODEL + c) = __byte_perm(w01, w23, 0x7531) ^ top_flip;
     }
 }
 

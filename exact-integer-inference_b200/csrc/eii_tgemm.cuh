@@ -64,6 +64,10 @@ struct TEpi {
     unsigned long long* dig;
     unsigned long long* dig_acc;
     const uint64_t* dig_b;   // w_f
+    // LOGITS: out = low 32 bits of RS(acc m, s) (every s in [1, 31], checked on the host); optional
+    // per-sequence digest dig[row / T] += sum over (t, f) of uint32(out) * dig_b[f] * dig_a[pos0 + row % T]
+    int T, pos0;
+    const uint64_t* dig_a;
 };
 
 // RES: the activation planes of a row block stay resident in shared memory (all K blocks, K <= 640)
@@ -332,12 +336,32 @@ __global__ void __launch_bounds__(TCfg<P, RES>::THREADS, 1)
         const int quad = warp & 3, rsub = (warp - 2) >> 2;
         griddep_wait();
         const bool digs = KIND == EPI_SWEEP && (ep.dig || ep.dig_acc);
+        const bool ldig = KIND == EPI_LOGITS && ep.dig != nullptr;
         // per-row digest sums of this warp's rows (lane: the row reduce_rows16_row names, per 16-row chunk)
         constexpr int NCH = C::ROWS_PER_WARP / 16;
         uint64_t dsum[NCH], asum[NCH];
 #pragma unroll
         for (int j = 0; j < NCH; ++j) dsum[j] = asum[j] = 0;
         int dig_r = -1;
+        // LOGITS digest, per lane: sum over this CTA's run of feature tiles of dig_b[f] * (sum over the chunk's
+        // rows of uint32(out) dig_a[t]) for chunk j (rows of one sequence, lseq[j]); reduced over the warp and
+        // added to the sequence's digest when the row block changes (lr) or the run ends
+        uint64_t lacc[NCH];
+        int lseq[NCH];
+        int lr = -1;
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) { lacc[j] = 0; lseq[j] = -1; }
+        auto lflush = [&]() {
+#pragma unroll
+            for (int j = 0; j < NCH; ++j) {
+                uint64_t w = lacc[j];
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+                if (lane == 0 && lseq[j] >= 0 && lseq[j] * ep.T < ep.M) atomicAdd(ep.dig + lseq[j], static_cast<unsigned long long>(w));
+                lacc[j] = 0;
+                lseq[j] = -1;
+            }
+        };
         auto dig_flush = [&]() {
             if (dig_r < 0 || (lane & 1)) return;
 #pragma unroll
@@ -359,12 +383,17 @@ __global__ void __launch_bounds__(TCfg<P, RES>::THREADS, 1)
             uint64_t wf = 0, corr = 0;
             if (f_ok) {
                 fc = __ldg(ep.feat + f);
+                if (ldig) wf = __ldg(ep.dig_b + f);
                 if (digs) {
                     wf = __ldg(ep.dig_b + f);
                     if (ep.dig_acc) corr = __ldg(ep.corr + f);
                 }
             }
             const uint64_t kc = (static_cast<uint64_t>(static_cast<uint32_t>(fc.w)) << 32) | static_cast<uint32_t>(fc.z);
+            if (ldig && r_blk != lr) {
+                lflush();
+                lr = r_blk;
+            }
             if (digs && r_blk != dig_r) {
                 dig_flush();
 #pragma unroll
@@ -393,6 +422,54 @@ __global__ void __launch_bounds__(TCfg<P, RES>::THREADS, 1)
                 tmem_wait_ld();
 #pragma unroll
                 for (int p = 0; p < P; ++p) tmem_launder(v[p]);
+                if constexpr (KIND == EPI_LOGITS) {
+                    // logits (python/intref.py:298-300, low 32 bits as exp_logits.i32 stores them)
+                    int32_t* op = ep.out + static_cast<int64_t>(row0) * ep.ld + f;
+                    uint32_t ys[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const uint64_t tt = tg_sum<P>(v, i, fc.x, kc);
+                        ys[i] = __funnelshift_r(static_cast<uint32_t>(tt), static_cast<uint32_t>(tt >> 32), fc.y);
+                        if (f_ok && row0 + i < ep.M) __stcs(op + i * ep.ld, static_cast<int32_t>(ys[i]));
+                    }
+                    // digest: per lane (feature f) s = sum_t uint32(out) dig_a[t] over rows of one sequence, then
+                    // dig_b[f] s summed over the warp's lanes is added to that sequence's digest
+                    if (ldig) {
+                        auto flush = [&](int sq, uint64_t sum) {
+                            uint64_t w = sum * wf;
+#pragma unroll
+                            for (int o = 16; o >= 1; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+                            if (lane == 0 && sq * ep.T < ep.M) atomicAdd(ep.dig + sq, static_cast<unsigned long long>(w));
+                        };
+                        const int seq0 = row0 / ep.T, t0 = row0 - seq0 * ep.T;
+                        if (t0 + 16 <= ep.T) {  // the chunk lies in one sequence (always when 16 divides T)
+                            const uint64_t* da = ep.dig_a + ep.pos0 + t0;
+                            uint64_t s0 = 0, s1 = 0;
+#pragma unroll
+                            for (int i = 0; i < 16; i += 2) {
+                                const uint64_t a0 = __ldg(da + i), a1 = __ldg(da + i + 1);
+                                if (row0 + i < ep.M) s0 += static_cast<uint64_t>(ys[i]) * a0;
+                                if (row0 + i + 1 < ep.M) s1 += static_cast<uint64_t>(ys[i + 1]) * a1;
+                            }
+                            lacc[j] += (s0 + s1) * wf;
+                            lseq[j] = seq0;
+                        } else {
+                            int sq = seq0, t = t0;
+                            uint64_t ds = 0;
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                if (row0 + i < ep.M) ds += static_cast<uint64_t>(ys[i]) * __ldg(ep.dig_a + ep.pos0 + t);
+                                if (++t == ep.T) {
+                                    flush(sq, ds);
+                                    ds = 0;
+                                    ++sq;
+                                    t = 0;
+                                }
+                            }
+                            if (t != 0) flush(sq, ds);
+                        }
+                    }
+                }
                 if constexpr (KIND == EPI_RESID) {
                     // x = SAT32(x + RS(acc m, s)) (python/intref.py:261,281; the residual term is not saturated)
                     int32_t* xp = ep.out + static_cast<int64_t>(row0) * ep.ld + f;
@@ -453,6 +530,7 @@ __global__ void __launch_bounds__(TCfg<P, RES>::THREADS, 1)
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
         if (digs) dig_flush();
+        if (ldig) lflush();
     }
     tc_fence_before();
     __syncthreads();
