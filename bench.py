@@ -660,6 +660,23 @@ def run_probe_decode(ns):
     print(f"[probe] decode {ns} sequences, position 64..67, digest[0][0] = {int(dig[0, 0].item()) & ((1 << 64) - 1):016x}")
 
 
+def run_probe_mma():
+    """Cycles per tcgen05.mma.kind::i8 (M = 128, K = 32) on every SM: by N alone, and at N = 256 beside
+    16 warps of each kind of background work (eii_mma_rate); one JSON object."""
+    import _eii
+    names = {0: "none", 1: "shared-memory loads", 2: "TMEM loads", 3: "64-bit multiply-add", 4: "global stores",
+             5: "32-bit IMAD", 6: "FFMA", 7: "integer ALU", 8: "32x32->64 multiply-accumulate"}
+    peak = 128 * 32 * 256 / 8192.0  # cycles of one N = 256 MMA at 8192 int8 MACs per cycle per SM
+    out = {"by_n": {}, "n256_with_16_background_warps": {}}
+    for n in (64, 128, 256):
+        c = _eii.mma_rate(0, n, 0, 128)
+        out["by_n"][n] = {"cycles_per_mma": round(c, 1), "frac_of_8192_macs_per_cycle": round(128 * 32 * n / c / 8192, 3)}
+    for z in range(9):
+        c = _eii.mma_rate(0, 256, z, 640)
+        out["n256_with_16_background_warps"][names[z]] = {"cycles_per_mma": round(c, 1), "frac": round(peak / c, 3)}
+    print(json.dumps(out, indent=1))
+
+
 def run_probe_sweep(spec):
     """One eii_linear_plan_run of sweep case NAME at M rows (spec "NAME:M"), for ncu captures of a
     single GEMM launch; prints the case digest of the outputs."""
@@ -696,6 +713,8 @@ def main():
                     help="profiling target: one untimed forward of NSEQ x 128 tokens on cuda:0, then exit")
     ap.add_argument("--probe-decode", type=int, default=0, metavar="NSEQ",
                     help="profiling target: a 64-token prompt and four decoding steps of NSEQ sequences, then exit")
+    ap.add_argument("--probe-mma", action="store_true",
+                    help="tcgen05 kind::i8 MMA rate by N and beside background work (eii_mma_rate), then exit")
     ap.add_argument("--probe-sweep", default=None, metavar="NAME:M",
                     help="profiling target: one contraction-sweep GEMM (sweep.py case NAME at M rows), then exit")
     args = ap.parse_args()
@@ -704,6 +723,9 @@ def main():
         return
     if args.probe_sweep:
         run_probe_sweep(args.probe_sweep)
+        return
+    if args.probe_mma:
+        run_probe_mma()
         return
     if args.probe_decode:
         run_probe_decode(args.probe_decode)

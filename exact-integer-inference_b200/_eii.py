@@ -43,6 +43,8 @@ _SIGS = {
     "eii_kernel_name": ([ctypes.c_int], ctypes.c_char_p),
     "eii_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
     "eii_chunk_sequences": ([_P, ctypes.c_int, ctypes.c_int], ctypes.c_int),
+    "eii_mma_rate": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                      ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
     "eii_profile_read": ([_P, ctypes.c_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)],
                          ctypes.c_int),
     "eii_linear": ([_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
@@ -101,6 +103,14 @@ def lib():
             f.restype = res
         _lib = L
     return _lib
+
+
+def mma_rate(device, n, noise=0, threads=640, iters=2000):
+    """Cycles per tcgen05.mma.kind::i8 (M = 128, N = n, K = 32) with background work `noise` on the
+    other warps (include/eii.h, eii_mma_rate)."""
+    c = ctypes.c_double()
+    check(lib().eii_mma_rate(device, n, noise, threads, iters, ctypes.byref(c)))
+    return c.value
 
 
 def check(rc):

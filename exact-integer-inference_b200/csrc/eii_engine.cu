@@ -35,6 +35,7 @@
 #include "eii_tables.h"
 #include "eii_gemm.cuh"
 #include "eii_tgemm.cuh"
+#include "eii_mma_probe.cuh"
 #include "eii_kernels.cuh"
 
 using namespace eii;
@@ -2013,4 +2014,38 @@ extern "C" int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_i
     if (code == ERR_BAD_INPUT) return fail(EII_ERR_ARG, "a_dev holds a value outside the signed %d-bit range", bits_in);
     if (code) return fail(EII_ERR_DEVICE, "kernel reported error %d (bounded wait timed out)", code);
     return EII_OK;
+}
+
+// =========================================================================== MMA-rate probe
+extern "C" int eii_mma_rate(int device, int n, int noise, int threads, int iters, double* cycles_per_mma) {
+    if (!cycles_per_mma) return fail(EII_ERR_ARG, "null output of eii_mma_rate");
+    if (n < 16 || n > 256 || n % 16) return fail(EII_ERR_ARG, "n must be a multiple of 16 in [16, 256] (got %d)", n);
+    if (noise < 0 || noise > 8) return fail(EII_ERR_ARG, "noise must be in [0, 8] (got %d)", noise);
+    if (threads != 128 && threads != 256 && threads != 640) return fail(EII_ERR_ARG, "threads must be 128, 256 or 640");
+    if (iters < 1 || iters > 100000) return fail(EII_ERR_ARG, "iters must be in [1, 100000]");
+    CK(cudaSetDevice(device));
+    int sms = 0;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    CK(cudaFuncSetAttribute(k_mma_probe, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_PROBE_SMEM));
+    std::vector<void*> mem;
+    unsigned long long* clk = nullptr;
+    int* err = nullptr;
+    int* scratch = nullptr;
+    int rc = dalloc(mem, &clk, 2);
+    if (rc == EII_OK) rc = dalloc(mem, &err, 1);
+    if (rc == EII_OK) rc = dalloc(mem, &scratch, (size_t)sms * 65536);
+    if (rc == EII_OK && cudaMemset(err, 0, sizeof(int)) != cudaSuccess) rc = fail(EII_ERR_CUDA, "memset failed");
+    if (rc == EII_OK) {
+        k_mma_probe<<<sms, threads, MMA_PROBE_SMEM>>>(n, iters, noise, clk, scratch, err);
+        if (cudaDeviceSynchronize() != cudaSuccess) rc = fail(EII_ERR_CUDA, "MMA probe failed: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+    unsigned long long c = 0;
+    int e = 0;
+    if (rc == EII_OK && (cudaMemcpy(&c, clk, sizeof(c), cudaMemcpyDeviceToHost) != cudaSuccess ||
+                         cudaMemcpy(&e, err, sizeof(e), cudaMemcpyDeviceToHost) != cudaSuccess))
+        rc = fail(EII_ERR_CUDA, "probe readback failed");
+    if (rc == EII_OK && e) rc = fail(EII_ERR_DEVICE, "MMA probe wait timed out");
+    free_list(mem);
+    if (rc == EII_OK) *cycles_per_mma = static_cast<double>(c) / (4.0 * iters);
+    return rc;
 }

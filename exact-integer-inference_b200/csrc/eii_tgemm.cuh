@@ -1,13 +1,15 @@
 // Feature-major byte-plane integer GEMM on tcgen05 kind::i8: output features in the TMEM lanes,
 // activation rows x byte planes in the MMA's N dimension.
 //
-// One tcgen05.mma.kind::i8 with M = 128 and K = 32 costs the same ~139 cycles for N = 64, 128 or
-// 256 on B200 (measured), so the tensor rate grows with N: N = 256 runs at 92 % of the int8 peak,
-// N = 128 at 46 %.  Here every MMA has N = 256: the activation tile is the P byte planes of BR =
-// 256 / P rows stacked along N, so one instruction multiplies a 128-feature weight tile with all
-// planes of BR rows, and the int32 accumulator of (feature f, plane p, row j) sits in TMEM lane f,
-// column p * BR + j.  A tile's accumulators take 256 of the 512 TMEM columns, so two tiles are in
-// flight: the epilogue of one runs while the MMAs of the next fill the other half.
+// Every MMA has N = 256: the activation tile is the P byte planes of BR = 256 / P rows stacked along
+// N, so one instruction multiplies a 128-feature weight tile with all planes of BR rows, and the int32
+// accumulator of (feature f, plane p, row j) sits in TMEM lane f, column p * BR + j.  A tile's
+// accumulators take 256 of the 512 TMEM columns for any plane count, so two tiles are always in
+// flight: the epilogue of one runs while the MMAs of the next fill the other half.  (The row-major
+// GEMM keeps one accumulator per plane; with four planes its 128-wide tiles fill all of TMEM and its
+// epilogue cannot overlap the next tile's MMAs, which is what made the 4-plane down projection slow.)
+// The MMA rate itself does not depend on N here: back to back, an M = 128, K = 32 kind::i8 MMA takes
+// 64 cycles at N = 128 and 128 at N = 256, the full 8192 MACs per cycle per SM (bench.py --probe-mma).
 //
 // One instruction needs one operand type for all planes, so the activation planes are offset
 // binary: for b-bit activations a, the planes are the bytes of a + 2^(b-1) (all u8; the low planes
@@ -134,9 +136,8 @@ __device__ __forceinline__ uint64_t tg_sum(const uint32_t (&v)[P][16], int i, in
 }
 
 // Requantisation without wide multiplies (two-plane activations, |acc| < 2^31 proven on the host for
-// every feature, shift s in [1, 31]).  A 32x32->64 multiply-add in the epilogue slows the concurrent
-// tcgen05 MMAs far more than 32-bit integer work (measured on B200: 16 warps of IMAD.WIDE cut the MMA
-// rate to 4 %, of 32-bit IMAD to 52 %, of integer ALU ops to 70 %), so:
+// every feature, shift s in [1, 31]).  Dense 32x32->64 multiply-accumulate work beside the MMAs slows
+// them several-fold, while 32-bit IMAD and ALU work leaves them at full rate (bench.py --probe-mma), so:
 //   acc = v0 + 2^8 v1 - 2^15 S_f                (mod 2^32; exact since |acc| < 2^31)
 //   acc m = (a1 2^16 + a0) m = p1 2^16 + a0 m,  a1 = acc >> 16 (signed), a0 = acc & 0xFFFF, p1 = a1 m
 //   u = a0 m + 2^(s-1) < 2^32;  (hi:lo) = p1 2^16 + u = acc m + 2^(s-1)   (a 48-bit value)

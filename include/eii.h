@@ -241,6 +241,15 @@ int eii_profile_read(eii_engine* e, int kind, double* total_ms, int64_t* launche
  * reference runs one sequence at a time). */
 int eii_chunk_sequences(const eii_engine* e, int n_seq, int T);
 
+/* Measurement probe (no reference counterpart): cycles per tcgen05.mma.kind::i8 of M = 128, N = n,
+ * K = 32 from shared-memory operands, issued back to back by one thread per SM on every SM of
+ * `device`, while warps 4 .. threads/32 - 1 of each CTA run background work `noise` (0 none,
+ * 1 shared-memory loads, 2 TMEM loads, 3 64-bit multiply-adds, 4 global stores, 5 32-bit IMAD,
+ * 6 FFMA, 7 integer ALU, 8 32x32->64 multiply-accumulate).  n a multiple of 16 in [16, 256];
+ * threads 128, 256 or 640; iters in [1, 100000] (4 MMAs each).  The numbers behind the GEMMs' tile
+ * shapes (bench.py --probe-mma). */
+int eii_mma_rate(int device, int n, int noise, int threads, int iters, double* cycles_per_mma);
+
 #ifdef __cplusplus
 }
 #endif
