@@ -665,13 +665,14 @@ def run_probe_mma():
     16 warps of each kind of background work (eii_mma_rate); one JSON object."""
     import _eii
     names = {0: "none", 1: "shared-memory loads", 2: "TMEM loads", 3: "64-bit multiply-add", 4: "global stores",
-             5: "32-bit IMAD", 6: "FFMA", 7: "integer ALU", 8: "32x32->64 multiply-accumulate"}
+             5: "32-bit IMAD", 6: "FFMA", 7: "integer ALU", 8: "32x32->64 multiply-accumulate",
+             9: "shared-memory stores", 10: "cp.async global->shared", 11: "cp.async.bulk global->shared"}
     peak = 128 * 32 * 256 / 8192.0  # cycles of one N = 256 MMA at 8192 int8 MACs per cycle per SM
     out = {"by_n": {}, "n256_with_16_background_warps": {}}
     for n in (64, 128, 256):
         c = _eii.mma_rate(0, n, 0, 128)
         out["by_n"][n] = {"cycles_per_mma": round(c, 1), "frac_of_8192_macs_per_cycle": round(128 * 32 * n / c / 8192, 3)}
-    for z in range(9):
+    for z in range(12):
         c = _eii.mma_rate(0, 256, z, 640)
         out["n256_with_16_background_warps"][names[z]] = {"cycles_per_mma": round(c, 1), "frac": round(peak / c, 3)}
     print(json.dumps(out, indent=1))

@@ -89,6 +89,7 @@ struct LayerDev {
     int silu_lo, silu_count, silu_wide, silu_d;
     int fast_qkv, fast_o, fast_gu, fast_d;  // fast requantisation path applies (see EpiParams::fast)
     int narrow_qkv, narrow_gu;              // requantised values provably fit int32 (EpiParams::narrow)
+    int acc32_qkv, acc32_gu;                // two-plane accumulators provably fit int32 (EpiParams::acc32)
     int gated_sd;                           // |gated| <= 2^30: signed-digit planes (EpiParams::sd_flags)
     // down projection on the feature-major GEMM (k_tgemm): the gate/up epilogue writes offset-binary
     // gated planes; per-feature constants of W_d for the layer's gated format, and 2^(b-1) S_f (the
@@ -726,7 +727,7 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     ep.silu = L.silu; ep.bits_g = L.g.bits; ep.bits_u = L.u.bits; ep.gated_shift = L.gated_shift;
     ep.silu_neg = L.silu_neg; ep.silu_smem = L.silu_neg != nullptr; ep.silu_lo = L.silu_lo;
     ep.silu_count = L.silu_count; ep.silu_wide = L.silu_wide; ep.silu_d = L.silu_d; ep.bits_s = L.s.bits;
-    ep.fast = L.fast_gu; ep.narrow = L.narrow_gu;
+    ep.fast = L.fast_gu; ep.narrow = L.narrow_gu; ep.acc32 = L.acc32_gu;
     ep.bits_m = L.m.bits; ep.gated_P = L.Pm; ep.gated_planes = e->gated_planes; ep.sd_flags = sd_flags;
     ep.gated_offset = L.t_down;
     TRY(launch_gemm<2, EPI_GATEUP>(e, am->h, L.tm_gu, ep, st, EII_K_GEMM_GATEUP));
@@ -858,7 +859,7 @@ int compact_silu(eii_engine* e, LayerDev& L, const int64_t* tab) {
     for (int g = lo; g <= 0; ++g)
         if (tab[g + 32768] < INT16_MIN || tab[g + 32768] > INT16_MAX) wide = true;
     const int count = 1 - lo;
-    if ((size_t)count * (wide ? 4 : 2) > (size_t)SILU_SMEM_BYTES) return EII_OK;
+    if ((size_t)(count + 1) * (wide ? 4 : 2) > (size_t)SILU_SMEM_BYTES) return EII_OK;  // + the zero past the table
     const int64_t smax = (int64_t(1) << (L.s.bits - 1)) - 1, smin = -smax - 1;
     for (int g = -32768; g <= 32767; ++g) {
         const int a = g < 0 ? g : -g;
@@ -895,6 +896,16 @@ bool cols_narrow(const int8_t* w, int N, int K, const std::vector<int2>& msh, in
         if (sh < 1 || sh > 31 || msh[j].x < 0) return false;
         const __int128 bound = static_cast<__int128>(amax) * l1 * msh[j].x + (static_cast<__int128>(1) << (sh - 1));
         if (bound >= (static_cast<__int128>(1) << (31 + sh))) return false;
+    }
+    return true;
+}
+
+// True when every column's |acc| <= amax * sum_k |w[j][k]| is below 2^31 (EpiParams::acc32).
+bool cols_acc32(const int8_t* w, int N, int K, int64_t amax) {
+    for (int j = 0; j < N; ++j) {
+        int64_t l1 = 0;
+        for (int k = 0; k < K; ++k) l1 += std::abs(static_cast<int>(w[(size_t)j * K + k]));
+        if (amax * l1 >= (int64_t(1) << 31)) return false;
     }
     return true;
 }
@@ -1082,6 +1093,7 @@ int load_model(eii_engine* e, const uint8_t* data, size_t nbytes) {
             TRY(check_col_shifts(msh, "gate/up", l));
             L.fast_gu = cols_fast(msh) && L.gated_shift >= 0 && L.gated_shift <= 31;
             L.narrow_gu = L.fast_gu && cols_narrow(w.data(), 2 * D_FF, D_MODEL, msh, 32768);
+            L.acc32_gu = L.narrow_gu && cols_acc32(w.data(), 2 * D_FF, D_MODEL, 32768) && !getenv("EII_NO_ACC32");
             // |SAT32(RS(silu * up, gs))| <= |silu * up| <= 2^15 * 2^15 when both are INT16 and gs >= 0
             L.gated_sd = L.m.bits == 32 && L.s.bits == 16 && L.u.bits == 16 && L.gated_shift >= 0 && !getenv("EII_NO_SD");
             TRY(upload(e, &L.w_gu, w.data(), w.size()));
@@ -2020,7 +2032,7 @@ extern "C" int eii_linear_noalloc(const int64_t* a_dev, int M, int K, int bits_i
 extern "C" int eii_mma_rate(int device, int n, int noise, int threads, int iters, double* cycles_per_mma) {
     if (!cycles_per_mma) return fail(EII_ERR_ARG, "null output of eii_mma_rate");
     if (n < 16 || n > 256 || n % 16) return fail(EII_ERR_ARG, "n must be a multiple of 16 in [16, 256] (got %d)", n);
-    if (noise < 0 || noise > 8) return fail(EII_ERR_ARG, "noise must be in [0, 8] (got %d)", noise);
+    if (noise < 0 || noise > 11) return fail(EII_ERR_ARG, "noise must be in [0, 11] (got %d)", noise);
     if (threads != 128 && threads != 256 && threads != 640) return fail(EII_ERR_ARG, "threads must be 128, 256 or 640");
     if (iters < 1 || iters > 100000) return fail(EII_ERR_ARG, "iters must be in [1, 100000]");
     CK(cudaSetDevice(device));

@@ -72,6 +72,10 @@ struct EpiParams {
     // needs no 64-bit saturation test; the RoPE shifts are >= 16 for the same reason.
     int narrow;
     int bits_g, bits_u, gated_shift, bits_m, gated_P;
+    // acc32 = for every column, 2^(b-1) * sum_k |W[col][k]| < 2^31 (host-checked): the two-plane
+    // accumulator acc = v0 + 2^8 v1 fits int32, so the narrow requantisation needs one 32x32->64
+    // multiply-add instead of two
+    int acc32;
     // gated planes in the row-blocked layout [gated_P][ceil(M/128)][N/32][128 rows][16 bytes]: each
     // 16-feature group of a 128-row block is one 2 KB run, so an epilogue warp's 32 rows x 16 features
     // of a plane are 512 contiguous bytes (coalesced stores).  The down GEMM reads it with a 4-D map.
@@ -247,6 +251,15 @@ __device__ __forceinline__ int32_t rs_narrow(const uint32_t (&v)[P][N], int i, i
 }
 __device__ __forceinline__ int32_t clamp16(int32_t v) { return min(max(v, -32768), 32767); }
 
+// Narrow requantisation with the two-plane accumulator combined in 32 bits (EpiParams::acc32).
+template <int P, int N>
+__device__ __forceinline__ int32_t rs_acc32(const uint32_t (&v)[P][N], int i, int4 cp) {
+    const int32_t acc = static_cast<int32_t>(v[0][i]) + static_cast<int32_t>(v[1][i] << 8);
+    const int64_t t = static_cast<int64_t>(acc) * cp.x + static_cast<int64_t>(static_cast<uint32_t>(cp.z));
+    return static_cast<int32_t>(
+        __funnelshift_r(static_cast<uint32_t>(t), static_cast<uint32_t>(static_cast<uint64_t>(t) >> 32), cp.y));
+}
+
 // Fast requantisation of one element: SAT_bits(RS(acc m, sh)).
 template <int P, int N>
 __device__ __forceinline__ int32_t requant_fast(const uint32_t (&v)[P][N], int i, int4 cp, int bits) {
@@ -288,17 +301,22 @@ __device__ __forceinline__ void pack_plane(const int32_t (&x)[N], uint32_t (&w)[
 
 // Gate/up/SiLU/gated product for 16 features, all-32-bit path: INT16 gate and up, compact INT16
 // SiLU table with shift d <= 15 (so g * 2^d < 2^31), gated shift in [0, 31].
-template <int P, int N, int BITS_M, bool NARROW>
+// The compact table holds count = 1 - lo_g entries for inputs lo_g .. 0 and a zero past them
+// (tab[count] = 0), so inputs below lo_g map there by an unsigned min instead of a test.
+template <int P, int N, int BITS_M, bool NARROW, bool ACC32>
 __device__ __forceinline__ void gateup_lean(const uint32_t (&vg)[P][N], const uint32_t (&vu)[P][N], const int4* cpg,
-                                            const int4* cpu, const int16_t* tab, int lo_g, int d, int gs, int64_t grnd,
-                                            int32_t (&gm)[N]) {
+                                            const int4* cpu, const int16_t* tab, int lo_g, int count, int d, int gs,
+                                            int64_t grnd, int32_t (&gm)[N]) {
 #pragma unroll
     for (int i = 0; i < N; ++i) {
-        const int32_t g = NARROW ? clamp16(rs_narrow<P, N>(vg, i, cpg[i])) : requant_fast<P, N>(vg, i, cpg[i], 16);
-        const int32_t u = NARROW ? clamp16(rs_narrow<P, N>(vu, i, cpu[i])) : requant_fast<P, N>(vu, i, cpu[i], 16);
+        const int32_t g = ACC32 ? clamp16(rs_acc32<P, N>(vg, i, cpg[i]))
+                                : (NARROW ? clamp16(rs_narrow<P, N>(vg, i, cpg[i])) : requant_fast<P, N>(vg, i, cpg[i], 16));
+        const int32_t u = ACC32 ? clamp16(rs_acc32<P, N>(vu, i, cpu[i]))
+                                : (NARROW ? clamp16(rs_narrow<P, N>(vu, i, cpu[i])) : requant_fast<P, N>(vu, i, cpu[i], 16));
         const int32_t a = min(g, -g);
-        int32_t sg = a >= lo_g ? static_cast<int32_t>(tab[a - lo_g]) : 0;
-        if (g > 0) sg = min(max(sg + (g << d), -32768), 32767);
+        const uint32_t idx = min(static_cast<uint32_t>(a - lo_g), static_cast<uint32_t>(count));
+        // silu(g) = silu(-|g|) + g 2^d for g > 0 (SAT16), the table value itself for g <= 0
+        const int32_t sg = min(max(static_cast<int32_t>(tab[idx]) + (max(g, 0) << d), -32768), 32767);
         // |sg u| <= 2^30 and 2^(gs-1) <= 2^30, so RS(sg u, gs) lies in [-2^30, 2^30]: it fits int32 and
         // SAT32 never applies; SAT16 is a clamp of that int32
         const int64_t prod = static_cast<int64_t>(sg) * u + grnd;
@@ -460,14 +478,19 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
             if (!row_ok) continue;
             int32_t gm[8];
             const int16_t* tab16 = static_cast<const int16_t*>(silu_tab);
-            if (lean && MODE == 2 && ep.bits_m == 32) {
-                gateup_lean<P, 8, 32, true>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
+            const int cnt = ep.silu_count;
+            if (P == 2 && lean && MODE == 2 && ep.acc32 && ep.bits_m == 32) {
+                gateup_lean<P, 8, 32, true, true>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, cnt, ep.silu_d, gs, grnd, gm);
+            } else if (P == 2 && lean && MODE == 2 && ep.acc32 && ep.bits_m == 16) {
+                gateup_lean<P, 8, 16, true, true>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, cnt, ep.silu_d, gs, grnd, gm);
+            } else if (lean && MODE == 2 && ep.bits_m == 32) {
+                gateup_lean<P, 8, 32, true, false>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, cnt, ep.silu_d, gs, grnd, gm);
             } else if (lean && MODE == 2 && ep.bits_m == 16) {
-                gateup_lean<P, 8, 16, true>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
+                gateup_lean<P, 8, 16, true, false>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, cnt, ep.silu_d, gs, grnd, gm);
             } else if (lean && ep.bits_m == 32) {
-                gateup_lean<P, 8, 32, false>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
+                gateup_lean<P, 8, 32, false, false>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, cnt, ep.silu_d, gs, grnd, gm);
             } else if (lean && ep.bits_m == 16) {
-                gateup_lean<P, 8, 16, false>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, ep.silu_d, gs, grnd, gm);
+                gateup_lean<P, 8, 16, false, false>(vg, vu, colp + f0, colp + 64 + f0, tab16, ep.silu_lo, cnt, ep.silu_d, gs, grnd, gm);
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -914,8 +937,8 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             }
         }
         if constexpr (KIND == EPI_GATEUP) {
-            if (ep.silu_smem) {  // stage the compact SiLU table once per CTA
-                const int nbytes = ep.silu_count * (ep.silu_wide ? 4 : 2);
+            if (ep.silu_smem) {  // stage the compact SiLU table (and the zero past it) once per CTA
+                const int nbytes = (ep.silu_count + 1) * (ep.silu_wide ? 4 : 2);
                 const int n16 = (nbytes + 15) / 16;
                 for (int q = et; q < n16; q += C::EPI_THREADS)
                     reinterpret_cast<int4*>(silu_tab)[q] = __ldg(reinterpret_cast<const int4*>(ep.silu_neg) + q);

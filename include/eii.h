@@ -245,7 +245,8 @@ int eii_chunk_sequences(const eii_engine* e, int n_seq, int T);
  * K = 32 from shared-memory operands, issued back to back by one thread per SM on every SM of
  * `device`, while warps 4 .. threads/32 - 1 of each CTA run background work `noise` (0 none,
  * 1 shared-memory loads, 2 TMEM loads, 3 64-bit multiply-adds, 4 global stores, 5 32-bit IMAD,
- * 6 FFMA, 7 integer ALU, 8 32x32->64 multiply-accumulate).  n a multiple of 16 in [16, 256];
+ * 6 FFMA, 7 integer ALU, 8 32x32->64 multiply-accumulate, 9 shared-memory stores, 10 cp.async global ->
+ * shared copies, 11 cp.async.bulk global -> shared copies).  n a multiple of 16 in [16, 256];
  * threads 128, 256 or 640; iters in [1, 100000] (4 MMAs each).  The numbers behind the GEMMs' tile
  * shapes (bench.py --probe-mma). */
 int eii_mma_rate(int device, int n, int noise, int threads, int iters, double* cycles_per_mma);
