@@ -185,7 +185,7 @@ def test_errors_are_reported(eng):
     assert out["logits"].shape == (1, 3, 49152)
 
 
-@pytest.mark.parametrize("switch", ["EII_O_FEATURE_MAJOR", "EII_DOWN_ROW_MAJOR", "EII_LOGITS_FEATURE_MAJOR"])
+@pytest.mark.parametrize("switch", ["EII_O_FEATURE_MAJOR", "EII_DOWN_ROW_MAJOR", "EII_LOGITS_FEATURE_MAJOR", "EII_NO_ACC32"])
 def test_forward_alternative_gemm_layouts(base_model, base_model_path, outlier_model, outlier_model_path, monkeypatch,
                                           switch):
     """The O projection on the feature-major GEMM (offset-binary context planes from every attention
