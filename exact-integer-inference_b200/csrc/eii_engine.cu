@@ -283,6 +283,7 @@ struct eii_engine {
     bool generic_norm = false;  // EII_NORM=generic: always the generic RMSNorm kernel
     int generic_attention = 0;  // EII_ATTENTION=generic: 64-bit requantisation in the tensor-core attention
     bool force_cuda_core_attention = false;  // EII_ATTENTION=cuda_core selects the CUDA-core kernel (any T)
+    bool decode_unstaged = false;  // EII_DECODE_UNSTAGED: decoding steps use k_attention_decode at every L
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_pool;
     std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_pending;
@@ -657,19 +658,22 @@ int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHo
     ep.pos0 = decode ? kv->pos : 0;
     TRY(launch_gemm<2, EPI_QKV>(e, am->h, L.tm_qkv, ep, st, EII_K_GEMM_QKV, &am->q, &am->k, &am->v));
 
-    if (kv) {  // keep this pass's k, v rows: T per sequence (prompt) or one at position pos (step)
+    if (kv && !decode) {  // keep the prompt's k, v rows (T per sequence); a step's row is appended by the attention
         const size_t row = 192 * sizeof(int16_t), pitch = row * kv->max_T;
-        const int p0 = decode ? kv->pos : 0;
-        CK(cudaMemcpy2DAsync(kv->kc + (size_t)p0 * 192, pitch, e->k, row * T, row * T, nseq, cudaMemcpyDeviceToDevice, st));
-        CK(cudaMemcpy2DAsync(kv->vc + (size_t)p0 * 192, pitch, e->v, row * T, row * T, nseq, cudaMemcpyDeviceToDevice, st));
+        CK(cudaMemcpy2DAsync(kv->kc, pitch, e->k, row * T, row * T, nseq, cudaMemcpyDeviceToDevice, st));
+        CK(cudaMemcpy2DAsync(kv->vc, pitch, e->v, row * T, row * T, nseq, cudaMemcpyDeviceToDevice, st));
     }
     if (decode) {
         AttnDecodeParams dp{};
-        dp.q = e->q; dp.kc = kv->kc; dp.vc = kv->vc; dp.max_T = kv->max_T; dp.L = kv->pos + 1; dp.exp_tab = e->exp_tab;
+        dp.q = e->q; dp.k_step = e->k; dp.v_step = e->v; dp.kc = kv->kc; dp.vc = kv->vc; dp.max_T = kv->max_T;
+        dp.L = kv->pos + 1; dp.exp_tab = e->exp_tab;
         dp.ctx_planes = e->ctx_planes; dp.P = L.Pc; dp.M = rows;
         dp.shift_s = L.shift_s; dp.shift_c = L.shift_c; dp.bits_c = L.c.bits; dp.offset = L.t_o;
         ProfScope ps(e, EII_K_ATTENTION, st);
-        CK(launch_k(k_attention_decode, dim3(nseq * N_KV), dim3(DECODE_THREADS), 0, st, dp));
+        if (dp.L <= DECODE_STAGE_L && !e->decode_unstaged)
+            CK(launch_k(k_attention_decode_s, dim3(nseq * N_KV), dim3(DECODE_THREADS), decode_stage_smem(dp.L), st, dp));
+        else
+            CK(launch_k(k_attention_decode, dim3(nseq * N_KV), dim3(DECODE_THREADS), 0, st, dp));
     }
     AttnParams ap{};
     ap.q = e->q; ap.k = e->k; ap.v = e->v; ap.exp_tab = e->exp_tab; ap.ctx_planes = e->ctx_planes; ap.P = L.Pc;
@@ -1157,6 +1161,7 @@ int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
                          cudaFuncSetAttribute(k_attention_tc_long, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               ATTNL_SMEM) != cudaSuccess))
         rc = fail(EII_ERR_CUDA, "attention smem attribute failed");
+    if (rc == EII_OK && getenv("EII_DECODE_UNSTAGED")) e->decode_unstaged = true;
     if (const char* a = getenv("EII_ATTENTION")) {
         e->force_cuda_core_attention = strcmp(a, "cuda_core") == 0;
         e->generic_attention = strcmp(a, "generic") == 0;

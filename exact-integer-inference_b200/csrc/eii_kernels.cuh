@@ -434,8 +434,10 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attention(AttnParams ap) {
 // as k_attention, so the row equals the one a full recomputation produces.
 struct AttnDecodeParams {
     const int16_t* q;        // [n, 576] queries of this step
-    const int16_t* kc;       // cache of this layer, first sequence of the launch
-    const int16_t* vc;
+    const int16_t* k_step;   // [n, 192] this step's k (post-RoPE) and v rows: key L - 1, appended to the
+    const int16_t* v_step;   //   cache at row L - 1 by the kernel
+    int16_t* kc;             // cache of this layer, first sequence of the launch
+    int16_t* vc;
     int max_T;               // cache rows per sequence
     int L;                   // keys per sequence (position + 1), <= DECODE_MAX_L
     const int32_t* exp_tab;  // [DMAX + 1]
@@ -465,9 +467,21 @@ __device__ __forceinline__ int32_t dp4a_us(uint32_t a, uint32_t b, int32_t c) {
 }
 constexpr int DECODE_THREADS = 128;
 
+// Appends this step's k and v rows of (sequence seq, KV group g) to the cache at row L - 1: 128 bytes
+// each, as eight 16-byte pieces (threads 0 .. 15).  Only this block reads that part of the cache in
+// this launch, and it reads key L - 1 from the step's rows, so the append needs no ordering.
+__device__ __forceinline__ void decode_append(const AttnDecodeParams& ap, int seq, int g, int tid) {
+    if (tid < 16) {
+        const int c = tid & 7;
+        const int16_t* src = (tid < 8 ? ap.k_step : ap.v_step) + static_cast<int64_t>(seq) * 192 + g * 64;
+        int16_t* dst = (tid < 8 ? ap.kc : ap.vc) + (static_cast<int64_t>(seq) * ap.max_T + ap.L - 1) * 192 + g * 64;
+        reinterpret_cast<int4*>(dst)[c] = reinterpret_cast<const int4*>(src)[c];
+    }
+}
+
 // Block = one (sequence, KV group): each key row k_j is read once and scored against the group's
 // three query heads; scores, then e, then P live in shared memory; P.V runs one thread per (head,
-// dim pair).
+// dim pair).  For any L <= DECODE_MAX_L; k_attention_decode_s below covers L <= DECODE_STAGE_L.
 __global__ void __launch_bounds__(DECODE_THREADS) k_attention_decode(AttnDecodeParams ap) {
     __shared__ int32_t E[DMAX + 1 + 3];
     __shared__ uint2 qb[3][16];  // per head, 4 dims per entry: (low bytes u8 x4, high bytes s8 x4)
@@ -484,13 +498,16 @@ __global__ void __launch_bounds__(DECODE_THREADS) k_attention_decode(AttnDecodeP
                               tid % 16);
         qb[tid / 16][tid % 16] = make_uint2(__byte_perm(w.x, w.y, 0x6420), __byte_perm(w.x, w.y, 0x7531));
     }
+    decode_append(ap, seq, g, tid);
     __syncthreads();
     const int16_t* kb = ap.kc + static_cast<int64_t>(seq) * ap.max_T * 192 + g * 64;
     const int16_t* vb = ap.vc + static_cast<int64_t>(seq) * ap.max_T * 192 + g * 64;
+    const int16_t* k_last = ap.k_step + static_cast<int64_t>(seq) * 192 + g * 64;
+    const int16_t* v_last = ap.v_step + static_cast<int64_t>(seq) * 192 + g * 64;
     // scores s_hj = SAT16(RS(q_h . k_j, shift_s))
     int32_t lmax[3] = {INT32_MIN, INT32_MIN, INT32_MIN};
     for (int j = tid; j < L; j += DECODE_THREADS) {
-        const uint4* k4 = reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(j) * 192);
+        const uint4* k4 = reinterpret_cast<const uint4*>(j == L - 1 ? k_last : kb + static_cast<int64_t>(j) * 192);
         // q.k = 65536 D2 + 256 D1 + D0 over byte planes with 4-way byte dot products (each partial
         // sum is below 64 * 255 * 255 < 2^31, as in the tensor-core attention)
         int32_t d0[3] = {0, 0, 0}, d1[3] = {0, 0, 0}, d2[3] = {0, 0, 0};
@@ -579,7 +596,8 @@ __global__ void __launch_bounds__(DECODE_THREADS) k_attention_decode(AttnDecodeP
     const uint32_t* vl = reinterpret_cast<const uint32_t*>(vb) + lane;
 #pragma unroll 4
     for (int j = kq; j < L; j += 4) {
-        const uint32_t vv = __ldg(vl + static_cast<int64_t>(j) * 96);
+        const uint32_t vv = j == L - 1 ? __ldg(reinterpret_cast<const uint32_t*>(v_last) + lane)
+                                       : __ldg(vl + static_cast<int64_t>(j) * 96);
         const int32_t v0 = static_cast<int16_t>(vv & 0xFFFF), v1 = static_cast<int16_t>(vv >> 16);
 #pragma unroll
         for (int h = 0; h < 3; ++h) {
@@ -590,6 +608,182 @@ __global__ void __launch_bounds__(DECODE_THREADS) k_attention_decode(AttnDecodeP
     }
     __syncthreads();  // S is no longer read: reuse it for the partial sums
     int64_t* part = reinterpret_cast<int64_t*>(&S[0][0]);  // [4 quarters][3 heads][32 lanes][2]
+#pragma unroll
+    for (int h = 0; h < 3; ++h) {
+        part[((kq * 3 + h) * 32 + lane) * 2] = a0[h];
+        part[((kq * 3 + h) * 32 + lane) * 2 + 1] = a1[h];
+    }
+    __syncthreads();
+    if (tid >= 96) return;
+    const int h = tid / 32;
+    int64_t c0 = 0, c1 = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        c0 += part[((q * 3 + h) * 32 + lane) * 2];
+        c1 += part[((q * 3 + h) * 32 + lane) * 2 + 1];
+    }
+    c0 = sat64(rs64(c0, ap.shift_c), ap.bits_c);
+    c1 = sat64(rs64(c1, ap.shift_c), ap.bits_c);
+    const int col = (g * 3 + h) * 64 + 2 * lane;
+    const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
+    const int64_t off = ap.offset ? (int64_t(1) << (8 * ap.P - 1)) : 0;
+    for (int p = 0; p < ap.P; ++p) {
+        const uint16_t pair =
+            static_cast<uint16_t>(plane_byte(c0 + off, p)) | (static_cast<uint16_t>(plane_byte(c1 + off, p)) << 8);
+        *reinterpret_cast<uint16_t*>(ap.ctx_planes + p * pstride + blocked_off(seq, col, D_MODEL)) = pair;
+    }
+}
+
+// Decode attention for L <= DECODE_STAGE_L keys, with the block's K and V rows staged in shared memory.
+// The same integer operations as k_attention_decode, so both give the row a full recomputation gives.
+// Latency is what bounds a decoding step (a few hundred sequences, tens of microseconds per kernel),
+// so the block issues every cache read up front as 16-byte asynchronous copies (one DRAM latency
+// instead of one per dependent load batch), looks the exp table up through L1 instead of staging
+// all of it, accumulates P.V with 32x32->64 multiply-adds, and keeps to 46 registers per thread and
+// about 19 KB of shared memory at L = 66, so that 11 blocks fit on an SM and the 1536 blocks of a
+// 512-sequence step run as one wave.
+constexpr int DECODE_STAGE_L = 128;
+constexpr int DECODE_K_PITCH = 144;  // bytes per staged key row: 8 threads' 16-byte reads of 8 rows hit distinct banks
+
+__host__ __device__ constexpr int decode_stage_smem(int L) {
+    // [K rows, pitch 144 B; reused for the P.V partial sums, 6 KB] [V rows, 128 B] [scores / e / P: 3 x L int32]
+    return ((L * DECODE_K_PITCH > 6144 ? L * DECODE_K_PITCH : 6144) + L * 128 + 3 * L * 4 + 15) & ~15;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+
+__global__ void __launch_bounds__(DECODE_THREADS, 11) k_attention_decode_s(AttnDecodeParams ap) {
+    extern __shared__ __align__(16) uint8_t dsm[];
+    const int L = ap.L;
+    const int kbytes = L * DECODE_K_PITCH > 6144 ? L * DECODE_K_PITCH : 6144;
+    uint8_t* Ks = dsm;
+    uint8_t* Vs = dsm + kbytes;
+    int32_t* S = reinterpret_cast<int32_t*>(Vs + L * 128);  // [3][L]
+    __shared__ uint2 qb[3][16];  // per head, 4 dims per entry: (low bytes u8 x4, high bytes s8 x4)
+    __shared__ int32_t red_max[3][DECODE_THREADS / 32];
+    __shared__ int64_t red_z[3][DECODE_THREADS / 32];
+    const int seq = blockIdx.x / N_KV, g = blockIdx.x % N_KV;
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    griddep_wait();  // q, k, v of this step are the previous kernel's output
+    griddep_launch();
+    {   // stage keys 0 .. L-2 from the cache and key L - 1 from this step's rows; append the latter
+        const int16_t* kb = ap.kc + static_cast<int64_t>(seq) * ap.max_T * 192 + g * 64;
+        const int16_t* vb = ap.vc + static_cast<int64_t>(seq) * ap.max_T * 192 + g * 64;
+        const int16_t* k_last = ap.k_step + static_cast<int64_t>(seq) * 192 + g * 64;
+        const int16_t* v_last = ap.v_step + static_cast<int64_t>(seq) * 192 + g * 64;
+        for (int u = tid; u < L * 8; u += DECODE_THREADS) {
+            const int j = u >> 3, c = u & 7;
+            const int16_t* ks = j == L - 1 ? k_last : kb + static_cast<int64_t>(j) * 192;
+            const int16_t* vs = j == L - 1 ? v_last : vb + static_cast<int64_t>(j) * 192;
+            cp_async16(Ks + j * DECODE_K_PITCH + c * 16, ks + c * 8);
+            cp_async16(Vs + j * 128 + c * 16, vs + c * 8);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    decode_append(ap, seq, g, tid);
+    if (tid < 48) {
+        const uint2 w = __ldg(reinterpret_cast<const uint2*>(ap.q + static_cast<int64_t>(seq) * D_MODEL + (g * 3 + tid / 16) * 64) +
+                              tid % 16);
+        qb[tid / 16][tid % 16] = make_uint2(__byte_perm(w.x, w.y, 0x6420), __byte_perm(w.x, w.y, 0x7531));
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    // scores s_hj = SAT16(RS(q_h . k_j, shift_s)), thread j for key j
+    int32_t lmax[3] = {INT32_MIN, INT32_MIN, INT32_MIN};
+    if (tid < L) {
+        const uint4* k4 = reinterpret_cast<const uint4*>(Ks + tid * DECODE_K_PITCH);
+        int32_t d0[3] = {0, 0, 0}, d1[3] = {0, 0, 0}, d2[3] = {0, 0, 0};
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const uint4 t = k4[w];
+            const uint32_t k0a = __byte_perm(t.x, t.y, 0x6420), k1a = __byte_perm(t.x, t.y, 0x7531);
+            const uint32_t k0b = __byte_perm(t.z, t.w, 0x6420), k1b = __byte_perm(t.z, t.w, 0x7531);
+#pragma unroll
+            for (int h = 0; h < 3; ++h) {
+                const uint2 qa = qb[h][2 * w], qc = qb[h][2 * w + 1];
+                d0[h] = dp4a_uu(qa.x, k0a, d0[h]);
+                d0[h] = dp4a_uu(qc.x, k0b, d0[h]);
+                d1[h] = dp4a_su(qa.y, k0a, d1[h]);
+                d1[h] = dp4a_su(qc.y, k0b, d1[h]);
+                d1[h] = dp4a_us(qa.x, k1a, d1[h]);
+                d1[h] = dp4a_us(qc.x, k1b, d1[h]);
+                d2[h] = __dp4a(static_cast<int>(qa.y), static_cast<int>(k1a), d2[h]);
+                d2[h] = __dp4a(static_cast<int>(qc.y), static_cast<int>(k1b), d2[h]);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            const int64_t acc = static_cast<int64_t>(d2[h]) * 65536 + static_cast<int64_t>(d1[h]) * 256 + d0[h];
+            const int32_t sj = static_cast<int32_t>(sat64(rs64(acc, ap.shift_s), 16));
+            S[h * L + tid] = sj;
+            lmax[h] = sj;
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < 3; ++h) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lmax[h] = max(lmax[h], __shfl_xor_sync(0xffffffffu, lmax[h], o));
+        if (lane == 0) red_max[h][warp] = lmax[h];
+    }
+    __syncthreads();
+    // e_hj = E[rowmax_h - s_hj] (0 beyond DMAX), Z_h = sum_j e_hj; the table is read through L1
+    int64_t lz[3] = {0, 0, 0};
+    if (tid < L) {
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            int32_t rmax = red_max[h][0];
+#pragma unroll
+            for (int w = 1; w < DECODE_THREADS / 32; ++w) rmax = max(rmax, red_max[h][w]);
+            const int32_t dd = rmax - S[h * L + tid];
+            const int32_t ej = dd <= DMAX ? __ldg(ap.exp_tab + dd) : 0;
+            S[h * L + tid] = ej;
+            lz[h] = ej;
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < 3; ++h) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lz[h] += __shfl_xor_sync(0xffffffffu, lz[h], o);
+        if (lane == 0) red_z[h][warp] = lz[h];
+    }
+    __syncthreads();
+    // P_hj = floor((e_hj 65536 + floor(Z_h/2)) / Z_h), exact (double estimate, integer remainder fix-up)
+    if (tid < L) {
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            int64_t Z = 0;
+#pragma unroll
+            for (int w = 0; w < DECODE_THREADS / 32; ++w) Z += red_z[h][w];
+            const int64_t n = static_cast<int64_t>(S[h * L + tid]) * 65536 + Z / 2;
+            int64_t p = static_cast<int64_t>(static_cast<double>(n) * (1.0 / static_cast<double>(Z)));
+            int64_t r = n - p * Z;
+            if (r < 0) { --p; r += Z; }
+            if (r < 0) { --p; r += Z; }
+            if (r >= Z) { ++p; r -= Z; }
+            if (r >= Z) { ++p; }
+            S[h * L + tid] = static_cast<int32_t>(p);
+        }
+    }
+    __syncthreads();
+    // ctx_hd = SAT(RS(sum_j P_hj v_jd, shift_c), bits_c): thread (key quarter tid / 32, dims 2 lane,
+    // 2 lane + 1) sums keys j = quarter (mod 4) for the three heads (P <= 65536 and |v| < 2^15, so each
+    // product is one 32x32->64 multiply-add); the quarters add up in shared memory.
+    const int kq = tid / 32;
+    int64_t a0[3] = {0, 0, 0}, a1[3] = {0, 0, 0};
+#pragma unroll 4
+    for (int j = kq; j < L; j += 4) {
+        const uint32_t vv = reinterpret_cast<const uint32_t*>(Vs + j * 128)[lane];
+        const int32_t v0 = static_cast<int16_t>(vv & 0xFFFF), v1 = static_cast<int16_t>(vv >> 16);
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            const int32_t p = S[h * L + j];
+            a0[h] += static_cast<int64_t>(p) * v0;
+            a1[h] += static_cast<int64_t>(p) * v1;
+        }
+    }
+    int64_t* part = reinterpret_cast<int64_t*>(Ks);  // [4 quarters][3 heads][32 lanes][2]: K is no longer read
 #pragma unroll
     for (int h = 0; h < 3; ++h) {
         part[((kq * 3 + h) * 32 + lane) * 2] = a0[h];

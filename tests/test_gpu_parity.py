@@ -402,6 +402,25 @@ def test_decode_from_empty_cache(eng):
     _decode_check(eng, synth.window_ids(70, 9)[None, :], 0)
 
 
+def test_decode_across_staged_limit(eng):
+    """Steps at L = 121 .. 128 keys run the staged decode kernel, L = 129 .. 136 the general one; both
+    append their step's K/V row to the cache that the other then reads."""
+    _decode_check(eng, np.stack([synth.window_ids(80, 136), synth.window_ids(81, 136)]), 120)
+
+
+def test_decode_unstaged_kernel(base_model_path, monkeypatch):
+    """EII_DECODE_UNSTAGED: the general decode kernel at L <= 128, where steps otherwise take the
+    staged one, from an empty cache and after a prompt."""
+    import _eii
+    monkeypatch.setenv("EII_DECODE_UNSTAGED", "1")
+    e = _eii.Engine(base_model_path, 0)
+    try:
+        _decode_check(e, synth.window_ids(70, 9)[None, :], 0)
+        _decode_check(e, np.stack([synth.window_ids(64, 40), synth.window_ids(65, 40)]), 30)
+    finally:
+        e.close()
+
+
 def test_decode_outlier_model_long_prompt(eng_outlier):
     """T = 160 (the long tensor-core attention kernel for the prompt): prompt 150, then 10 steps."""
     g = golden("vectors_t160.json")
