@@ -281,6 +281,7 @@ struct eii_engine {
     std::vector<void*> workspace;
     // optional per-kernel timing (eii_profile_enable): event pairs around each launch
     bool generic_norm = false;  // EII_NORM=generic: always the generic RMSNorm kernel
+    bool fuse_norm = true;      // EII_NO_NORM_FUSION: the first layer's RMSNorm as its own kernel
     int generic_attention = 0;  // EII_ATTENTION=generic: 64-bit requantisation in the tensor-core attention
     bool force_cuda_core_attention = false;  // EII_ATTENTION=cuda_core selects the CUDA-core kernel (any T)
     bool decode_unstaged = false;  // EII_DECODE_UNSTAGED: decoding steps use k_attention_decode at every L
@@ -582,7 +583,23 @@ int launch_norm(eii_engine* e, const int32_t* x, int rows, const int32_t* gain, 
     return EII_OK;
 }
 
-int launch_embed(eii_engine* e, const int64_t* ids, int rows, cudaStream_t st) {
+// The embedding of `rows` tokens into x.  With normed != nullptr, the first layer's RMSNorm planes are
+// produced in the same kernel (k_embed_norm) when launch_norm would take its lean two-plane kernel and
+// no residual grid runs before the layer; *normed tells whether they were.  (The same fusion into the
+// feature-major down projection, for the next layer's norm, measured slower than the norm kernel: the
+// GEMM's 16 epilogue warps hide the norm's L2 latency and isqrt far worse than 32 warps per SM do.)
+int launch_embed(eii_engine* e, const int64_t* ids, int rows, cudaStream_t st, bool* normed = nullptr) {
+    if (normed) *normed = false;
+    const LayerDev& L0 = e->L[0];
+    if (normed && e->fuse_norm && !e->generic_norm && !e->grid_on && L0.h.bits == 16 && L0.norm1_shift >= 10 &&
+        L0.norm1_shift <= 31) {
+        ProfScope ps(e, EII_K_EMBED, st);
+        CK(launch_k(k_embed_norm, dim3((rows + 15) / 16), dim3(256), 0, st, ids, rows, (const int8_t*)e->emb_q,
+                    (const int32_t*)e->emb_m, (const int32_t*)e->emb_n, e->x, e->err_dev, (const int32_t*)L0.ln1,
+                    L0.norm1_shift, e->h_planes, 0u));
+        *normed = true;
+        return EII_OK;
+    }
     const int rows_per_block = 8;
     ProfScope ps(e, EII_K_EMBED, st);
     CK(launch_k(k_embed, dim3((rows + rows_per_block - 1) / rows_per_block), dim3(32 * rows_per_block), 0, st, ids, rows,
@@ -632,15 +649,16 @@ int launch_grid(eii_engine* e, int rows, int which, int l, cudaStream_t st) {
     return EII_OK;
 }
 
+// norm_done: the layer's first norm is already in h_planes (the embedding produced it).
 int run_layer(eii_engine* e, int l, int rows, int T, cudaStream_t st, const KvHook* kv = nullptr,
-              const TraceHook* trh = nullptr) {
+              const TraceHook* trh = nullptr, bool norm_done = false) {
     if (e->grid_on && !trh) TRY(launch_grid(e, rows, 0, l, st));
     LayerDev& L = e->L[l];
     const ActMaps* am;
     TRY(act_maps(e, rows, &am));
     const int nseq = rows / T;
     const bool decode = kv && kv->pos >= 0;
-    TRY(launch_norm(e, e->x, rows, L.ln1, L.norm1_shift, L.h.bits, e->h_planes, 2, nullptr, st));
+    if (!norm_done) TRY(launch_norm(e, e->x, rows, L.ln1, L.norm1_shift, L.h.bits, e->h_planes, 2, nullptr, st));
     if (trh) {
         TRY(launch_norm(e, e->x, rows, L.ln1, L.norm1_shift, L.h.bits, nullptr, 0, trh->n1, st, trh->u1, trh->z1));
         TRY(trace_linear(e, 2, am->h, false, L.w_qkv, D_MODEL, 576, L.msh_qkv, L.q.bits, trh->q, rows, st));
@@ -1167,6 +1185,7 @@ int open_common(const void* data, size_t nbytes, int device, eii_engine** out) {
         e->generic_attention = strcmp(a, "generic") == 0;
     }
     if (const char* a = getenv("EII_NORM")) e->generic_norm = strcmp(a, "generic") == 0;
+    if (getenv("EII_NO_NORM_FUSION")) e->fuse_norm = false;
     if (rc != EII_OK) {
         eii_close(e);
         return rc;
@@ -1220,14 +1239,15 @@ int forward_host(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* e
             rc = fail(EII_ERR_CUDA, "ids upload failed");
             break;
         }
-        rc = launch_embed(e, e->ids_dev, rows, st);
+        bool normed = false;
+        rc = launch_embed(e, e->ids_dev, rows, st, &normed);
         if (rc == EII_OK && embed_out &&
             cudaMemcpyAsync(embed_out + (int64_t)s0 * T * D_MODEL, e->x, row_bytes * rows, cudaMemcpyDeviceToHost, st) != cudaSuccess)
             rc = fail(EII_ERR_CUDA, "embed download failed");
         for (int l = 0; l < N_LAYERS && rc == EII_OK; ++l) {
             KvHook kv;
             if (dec) kv = dec_hook(dec, l, s0, pos);
-            rc = run_layer(e, l, rows, T, st, dec ? &kv : nullptr);
+            rc = run_layer(e, l, rows, T, st, dec ? &kv : nullptr, nullptr, l == 0 && normed);
             if (rc == EII_OK && resid_out) {
                 // resid_out is [n_seq][30][T][576]: one T x 576 block per sequence and layer.
                 const size_t blk = row_bytes * T;
@@ -1269,11 +1289,12 @@ int forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int3
     for (int s0 = 0; s0 < n_seq; s0 += cs) {
         const int ns = (n_seq - s0) < cs ? (n_seq - s0) : cs;
         const int rows = ns * T;
-        TRY(launch_embed(e, ids_dev + (int64_t)s0 * T, rows, st));
+        bool normed = false;
+        TRY(launch_embed(e, ids_dev + (int64_t)s0 * T, rows, st, &normed));
         for (int l = 0; l < N_LAYERS; ++l) {
             KvHook kv;
             if (dec) kv = dec_hook(dec, l, s0, pos);
-            TRY(run_layer(e, l, rows, T, st, dec ? &kv : nullptr));
+            TRY(run_layer(e, l, rows, T, st, dec ? &kv : nullptr, nullptr, l == 0 && normed));
         }
         if (logits_dev || digests_dev) {
             int32_t* lg = logits_dev ? logits_dev + (int64_t)s0 * T * ld : e->logits_ws;

@@ -229,21 +229,14 @@ __device__ __forceinline__ void add96(uint32_t& a0, uint32_t& a1, uint32_t& a2, 
         : "r"(b0), "r"(b1), "r"(b2));
 }
 
-// Four 256-thread blocks per SM (at most 64 registers): more loads in flight on the HBM-bound path.
-__global__ void __launch_bounds__(256, 4) k_rmsnorm_p16(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain,
-                                                      int shift_out, uint8_t* __restrict__ planes,
-                                                      uint32_t* __restrict__ zero_ptr, int zero_n, uint32_t top_flip) {
-    const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
+// The per-row part of the two-plane RMSNorm, shared by k_rmsnorm_p16 and k_embed_norm.  A warp normalises two rows: lanes 0-15 the
+// row `row` of the lower half-warp, lanes 16-31 that of the upper; lane l of a half holds columns
+// 64 i + 4 l .. 64 i + 4 l + 3 (i < 9) in v[i].  The whole warp calls it (shuffles); a row >= M
+// (live false, v zero) stores nothing.
+__device__ __forceinline__ void rmsnorm_pair_finish(const int4 (&v)[9], int row, bool live, int M,
+                                                    const int32_t* __restrict__ gain, int shift_out,
+                                                    uint8_t* __restrict__ planes, uint32_t top_flip) {
     const int l = threadIdx.x & 15;
-    const bool live = row < M;
-    griddep_wait();
-    griddep_launch();
-    if (zero_ptr && blockIdx.x == 0)  // flag words the next kernels fill (signed-digit gated planes)
-        for (int i = threadIdx.x; i < zero_n; i += blockDim.x) zero_ptr[i] = 0;
-    const int4* xr = reinterpret_cast<const int4*>(x + static_cast<int64_t>(live ? row : 0) * D_MODEL);
-    int4 v[9];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) v[i] = live ? xr[16 * i + l] : make_int4(0, 0, 0, 0);
     uint32_t a0 = 0, a1 = 0, a2 = 0;
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
@@ -293,6 +286,65 @@ __global__ void __launch_bounds__(256, 4) k_rmsnorm_p16(const int32_t* __restric
         // top_flip = 0x80808080: offset-binary planes (the high byte's sign bit flipped)
         *reinterpret_cast<uint32_t*>(planes + (static_cast<int64_t>(M) + row) * D_MODEL + c) = __byte_perm(w01, w23, 0x7531) ^ top_flip;
     }
+}
+
+// Loads the two rows of a warp (layout of rmsnorm_pair_finish) and normalises them.
+__device__ __forceinline__ void rmsnorm_pair_p16(const int32_t* __restrict__ x, int row, int M, const int32_t* __restrict__ gain,
+                                                 int shift_out, uint8_t* __restrict__ planes, uint32_t top_flip) {
+    const int l = threadIdx.x & 15;
+    const bool live = row < M;
+    const int4* xr = reinterpret_cast<const int4*>(x + static_cast<int64_t>(live ? row : 0) * D_MODEL);
+    int4 v[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) v[i] = live ? xr[16 * i + l] : make_int4(0, 0, 0, 0);
+    rmsnorm_pair_finish(v, row, live, M, gain, shift_out, planes, top_flip);
+}
+
+// Four 256-thread blocks per SM (at most 64 registers): more loads in flight on the HBM-bound path.
+__global__ void __launch_bounds__(256, 4) k_rmsnorm_p16(const int32_t* __restrict__ x, int M, const int32_t* __restrict__ gain,
+                                                      int shift_out, uint8_t* __restrict__ planes,
+                                                      uint32_t* __restrict__ zero_ptr, int zero_n, uint32_t top_flip) {
+    const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
+    griddep_wait();
+    griddep_launch();
+    if (zero_ptr && blockIdx.x == 0)  // flag words the next kernels fill (signed-digit gated planes)
+        for (int i = threadIdx.x; i < zero_n; i += blockDim.x) zero_ptr[i] = 0;
+    rmsnorm_pair_p16(x, row, M, gain, shift_out, planes, top_flip);
+}
+
+// Embedding (as k_embed) with the first layer's RMSNorm fused: two rows per warp in the layout of
+// rmsnorm_pair_finish (lane l of a half-warp builds columns 64 i + 4 l .. +3 of its row from one
+// 4-byte load per i), x is stored and the norm runs on the values in registers.
+__global__ void __launch_bounds__(256) k_embed_norm(const int64_t* __restrict__ ids, int M, const int8_t* __restrict__ emb_q,
+                                                   const int32_t* __restrict__ emb_m, const int32_t* __restrict__ emb_n,
+                                                   int32_t* __restrict__ x, int* err, const int32_t* __restrict__ gain,
+                                                   int shift_out, uint8_t* __restrict__ planes, uint32_t top_flip) {
+    const int row = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + ((threadIdx.x >> 4) & 1);
+    const int l = threadIdx.x & 15;
+    const bool live = row < M;
+    griddep_wait();
+    griddep_launch();
+    int64_t id = live ? ids[row] : 0;
+    if (id < 0 || id >= VOCAB) {
+        if (l == 0) atomicCAS(err, 0, ERR_BAD_TOKEN);
+        id = 0;
+    }
+    const int64_t m = emb_m[id];
+    const int sh = emb_n[id] - F_RES;
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(emb_q + id * D_MODEL);
+    int4* dst = reinterpret_cast<int4*>(x + static_cast<int64_t>(live ? row : 0) * D_MODEL);
+    int4 v[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) {
+        const uint32_t w = __ldg(src + 16 * i + l);
+        int32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            o[q] = static_cast<int32_t>(rs64(static_cast<int64_t>(static_cast<int8_t>(w >> (8 * q))) * m, sh));
+        v[i] = make_int4(o[0], o[1], o[2], o[3]);
+        if (live) dst[16 * i + l] = v[i];
+    }
+    rmsnorm_pair_finish(v, row, live, M, gain, shift_out, planes, top_flip);
 }
 
 // --------------------------------------------------------------------------- row-blocked planes

@@ -185,14 +185,16 @@ def test_errors_are_reported(eng):
     assert out["logits"].shape == (1, 3, 49152)
 
 
-@pytest.mark.parametrize("switch", ["EII_O_FEATURE_MAJOR", "EII_DOWN_ROW_MAJOR", "EII_LOGITS_FEATURE_MAJOR", "EII_NO_ACC32"])
+@pytest.mark.parametrize("switch", ["EII_O_FEATURE_MAJOR", "EII_DOWN_ROW_MAJOR", "EII_LOGITS_FEATURE_MAJOR", "EII_NO_ACC32",
+                                    "EII_NO_NORM_FUSION"])
 def test_forward_alternative_gemm_layouts(base_model, base_model_path, outlier_model, outlier_model_path, monkeypatch,
                                           switch):
     """The O projection on the feature-major GEMM (offset-binary context planes from every attention
     kernel), the down projection on the row-major GEMM (signed-digit gated planes), and the tied logits
     on the feature-major GEMM (offset-binary final-norm planes, per-sequence digests): the reference's
     digests for t24 and t160 (the long tensor-core attention), a decode that reaches the decode attention
-    kernel, and the per-site trace (the trace's row-major GEMMs read the same planes)."""
+    kernel, and the per-site trace (the trace's row-major GEMMs read the same planes).  EII_NO_NORM_FUSION:
+    the first layer's RMSNorm as its own kernel (by default the embedding kernel produces its planes)."""
     import _eii
     import intref as drop
     from test_oracle_golden import check_trace, trace_inputs
