@@ -201,8 +201,9 @@ void eii_linear_plan_close(eii_linear_plan* p);
  *   library holds until the process exits).  Limits: (bits_in / 8) * M * K <= EII_NOALLOC_PLANE_BYTES,
  *   N <= EII_NOALLOC_MAX_N, K a multiple of 32 up to 1536, N a multiple of 16; larger sizes are
  *   rejected with EII_ERR_ARG.
- *   The first call on a device resolves the scratch addresses for that device (cudaGetSymbolAddress),
- *   so make that first call before any stream capture.  Every call shares the same scratch: calls
+ *   Every call reads its error word back and synchronises `stream` before it returns, so no call
+ *   can be captured into a CUDA graph.  The first call on a device also resolves the scratch
+ *   addresses for that device (cudaGetSymbolAddress).  Every call shares the same scratch: calls
  *   that overlap on the GPU (different streams or threads at the same time) race and must be
  *   serialised by the caller. */
 #define EII_NOALLOC_PLANE_BYTES (16u * 1024u * 1024u)
