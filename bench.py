@@ -314,10 +314,11 @@ def decode_bench(eng, ids_host, ids_dev, ns, fwd_digests, stream, barrier, max_o
         barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record()
-        for t in range(1, T - T0):
-            dec.step_device(ids_t[t].data_ptr(), step_logits.data_ptr(), VOCAB, step_dig[t].data_ptr(), stream)
+        for t in range(1, T - T0):  # enqueued back to back; device-side errors surface at sync()
+            dec.step_device_async(ids_t[t].data_ptr(), step_logits.data_ptr(), VOCAB, step_dig[t].data_ptr(), stream)
         ev1.record()
         torch.cuda.synchronize()
+        dec.sync(stream)
         ms = max_over_ranks(ev0.elapsed_time(ev1))
         total = (torch.from_numpy(pre.view(np.int64).copy()).cuda() + step_dig.sum(dim=0)).cpu().numpy()
         exact = bool(np.array_equal(total, fwd_digests.cpu().numpy()))
@@ -325,7 +326,8 @@ def decode_bench(eng, ids_host, ids_dev, ns, fwd_digests, stream, barrier, max_o
         dec.close()
     return {"unit": UNIT, "n_seq": N_SEQ, "prompt_tokens": T0, "timed_steps": T - T0 - 1, "ms": round(ms, 3),
             "ms_per_step": round(ms / (T - T0 - 1), 3),
-            "path": "eii_decoder_prefill, then eii_decoder_step_device (K/V cache, one token per sequence per step)",
+            "path": "eii_decoder_prefill, then eii_decoder_step_device_async (K/V cache, one token per sequence per "
+                    "step, steps enqueued back to back) and eii_decoder_sync",
             "exact_vs_forward_digests": exact}
 
 

@@ -62,6 +62,8 @@ _SIGS = {
     "eii_decoder_prefill": ([_P, _P, ctypes.c_int, _P, _P], ctypes.c_int),
     "eii_decoder_step": ([_P, _P, _P, _P], ctypes.c_int),
     "eii_decoder_step_device": ([_P, _P, _P, ctypes.c_int64, _P, _P], ctypes.c_int),
+    "eii_decoder_step_device_async": ([_P, _P, _P, ctypes.c_int64, _P, _P], ctypes.c_int),
+    "eii_decoder_sync": ([_P, _P], ctypes.c_int),
     "eii_decoder_position": ([_P], ctypes.c_int),
     "eii_decoder_reset": ([_P], ctypes.c_int),
     "eii_decoder_close": ([_P], None),
@@ -375,6 +377,16 @@ class Decoder:
                                             ctypes.c_void_p(logits_ptr) if logits_ptr else None, ld,
                                             ctypes.c_void_p(digests_ptr) if digests_ptr else None,
                                             ctypes.c_void_p(stream) if stream else None))
+
+    def step_device_async(self, ids_ptr, logits_ptr=None, ld=VOCAB, digests_ptr=None, stream=None):
+        """step_device without waiting: device-side errors surface at the next sync()."""
+        check(lib().eii_decoder_step_device_async(self.h, ctypes.c_void_p(ids_ptr),
+                                                  ctypes.c_void_p(logits_ptr) if logits_ptr else None, ld,
+                                                  ctypes.c_void_p(digests_ptr) if digests_ptr else None,
+                                                  ctypes.c_void_p(stream) if stream else None))
+
+    def sync(self, stream=None):
+        check(lib().eii_decoder_sync(self.h, ctypes.c_void_p(stream) if stream else None))
 
 
 def _mix64(z):

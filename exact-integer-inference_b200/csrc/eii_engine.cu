@@ -1275,8 +1275,10 @@ int forward_host(eii_engine* e, const int64_t* ids, int n_seq, int T, int32_t* e
 }
 
 // Device-resident forward (eii_forward_device), or a decoder prompt pass / step as in forward_host.
+// sync = false: return once the work is enqueued (eii_decoder_step_device_async); device-side errors
+// stay in the error word for the next check.
 int forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int32_t* logits_dev, int64_t ld,
-                   uint64_t* digests_dev, void* stream, eii_decoder* dec, int pos) {
+                   uint64_t* digests_dev, void* stream, eii_decoder* dec, int pos, bool sync = true) {
     if (!ids_dev) return fail(EII_ERR_ARG, "ids_dev is null");
     if (logits_dev && (ld < VOCAB || (ld % 4) != 0 || (reinterpret_cast<uintptr_t>(logits_dev) & 15)))
         return fail(EII_ERR_ARG, "logits_dev must be 16-byte aligned with ld >= %d, ld %% 4 == 0", VOCAB);
@@ -1302,7 +1304,7 @@ int forward_device(eii_engine* e, const int64_t* ids_dev, int n_seq, int T, int3
             TRY(run_logits(e, rows, T, lg, lld, digests_dev ? digests_dev + s0 : nullptr, st, pos < 0 ? 0 : pos));
         }
     }
-    return check_device_error(e, st);
+    return sync ? check_device_error(e, st) : EII_OK;
 }
 
 }  // namespace
@@ -1550,6 +1552,21 @@ int eii_decoder_step_device(eii_decoder* d, const int64_t* ids_dev, int32_t* log
     TRY(forward_device(d->e, ids_dev, d->n_seq, 1, logits_dev, ld, digests_dev, stream, d, d->pos));
     ++d->pos;
     return EII_OK;
+}
+
+int eii_decoder_step_device_async(eii_decoder* d, const int64_t* ids_dev, int32_t* logits_dev, int64_t ld,
+                                  uint64_t* digests_dev, void* stream) {
+    if (!d) return fail(EII_ERR_ARG, "decoder is null");
+    if (d->pos >= d->max_T) return fail(EII_ERR_ARG, "the K/V cache is full (max_T = %d)", d->max_T);
+    TRY(forward_device(d->e, ids_dev, d->n_seq, 1, logits_dev, ld, digests_dev, stream, d, d->pos, false));
+    ++d->pos;
+    return EII_OK;
+}
+
+int eii_decoder_sync(eii_decoder* d, void* stream) {
+    if (!d) return fail(EII_ERR_ARG, "decoder is null");
+    CK(cudaSetDevice(d->e->device));
+    return check_device_error(d->e, stream ? static_cast<cudaStream_t>(stream) : d->e->stream);
 }
 
 int eii_decoder_position(const eii_decoder* d) { return d ? d->pos : -1; }

@@ -113,6 +113,16 @@ int eii_decoder_step(eii_decoder* d, const int64_t* ids, int32_t* logits_out, ui
 /* Device pointers as in eii_forward_device (logits_dev rows of ld_logits elements). */
 int eii_decoder_step_device(eii_decoder* d, const int64_t* ids_dev, int32_t* logits_dev, int64_t ld_logits,
                             uint64_t* digests_dev, void* stream);
+/* The same step, returning once it is enqueued on `stream` (no synchronisation): a serving loop
+ * issues its steps back to back and calls eii_decoder_sync when it needs the results.  Argument
+ * errors are returned at once; device-side errors of the enqueued steps (a token id outside the
+ * vocabulary, a bounded wait that ran out) are returned by the next eii_decoder_sync, after which
+ * the cache contents are undefined (eii_decoder_reset and prefill again).  Consecutive steps of one
+ * decoder must go to the same stream, or the caller orders them. */
+int eii_decoder_step_device_async(eii_decoder* d, const int64_t* ids_dev, int32_t* logits_dev, int64_t ld_logits,
+                                  uint64_t* digests_dev, void* stream);
+/* Waits for the work on `stream` (null = the engine's stream) and reports a device-side error. */
+int eii_decoder_sync(eii_decoder* d, void* stream);
 int eii_decoder_position(const eii_decoder* d); /* tokens in the cache, -1 for a null decoder */
 int eii_decoder_reset(eii_decoder* d);          /* back to position 0 (the cache is reused) */
 void eii_decoder_close(eii_decoder* d);

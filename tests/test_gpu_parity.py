@@ -423,6 +423,46 @@ def test_decode_unstaged_kernel(base_model_path, monkeypatch):
         e.close()
 
 
+def test_decode_async_steps_and_deferred_errors(eng, base_model):
+    """eii_decoder_step_device_async: steps enqueued back to back on a side stream give the forward's
+    logits rows and digests after eii_decoder_sync; a token id outside the vocabulary in an enqueued
+    step is reported by the next sync (EII_ERR_ARG), and the engine works again afterwards."""
+    import torch
+    import _eii
+    ids = np.stack([synth.window_ids(70 + i, 16) for i in range(3)])
+    n, T = ids.shape
+    T0 = 9
+    ref = eng.forward(ids, logits=True, digests=True)
+    dec = _eii.Decoder(eng, n, T)
+    try:
+        pre = dec.prefill(ids[:, :T0], logits=False, digests=True)["digests"]
+        side = torch.cuda.Stream()
+        ids_d = torch.from_numpy(np.ascontiguousarray(ids[:, T0:].T)).cuda()
+        lg = torch.empty((T - T0, n, _eii.VOCAB), dtype=torch.int32, device="cuda")
+        dg = torch.zeros((T - T0, n), dtype=torch.int64, device="cuda")
+        with torch.cuda.stream(side):
+            for t in range(T - T0):
+                dec.step_device_async(ids_d[t].data_ptr(), lg[t].data_ptr(), _eii.VOCAB, dg[t].data_ptr(), side.cuda_stream)
+        dec.sync(side.cuda_stream)
+        assert dec.position == T
+        for t in range(T - T0):
+            d = first_diff(lg[t].cpu().numpy(), ref["logits"][:, T0 + t])
+            assert d is None, (t, d)
+        total = pre.view(np.uint64) + dg.sum(dim=0).cpu().numpy().view(np.uint64)
+        assert np.array_equal(total, ref["digests"])
+        dec.reset()
+        dec.prefill(ids[:, :T0], logits=False)
+        bad = torch.tensor([0, _eii.VOCAB, 1], dtype=torch.int64, device="cuda")
+        with torch.cuda.stream(side):
+            dec.step_device_async(bad.data_ptr(), lg[0].data_ptr(), _eii.VOCAB, None, side.cuda_stream)
+        with pytest.raises(_eii.EiiError) as ei:
+            dec.sync(side.cuda_stream)
+        assert ei.value.code == _eii.EII_ERR_ARG
+    finally:
+        dec.close()
+    _check_set(eng, base_model, "t24")
+
+
 def test_decode_outlier_model_long_prompt(eng_outlier):
     """T = 160 (the long tensor-core attention kernel for the prompt): prompt 150, then 10 steps."""
     g = golden("vectors_t160.json")
