@@ -191,6 +191,20 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
         __syncthreads();
         tc_fence_after();
         if (tid == 0) issue_s(0);
+        {   // the CTA's next item: its q (3 heads), k and v rows into L2 while this item runs, so that its
+            // staging reads hit L2 instead of every CTA reading DRAM at once at each item start
+            const int nitem = item + gridDim.x;
+            if (nitem < items) {
+                const int64_t nrow0 = static_cast<int64_t>(nitem / N_KV) * T;
+                const int ng = nitem % N_KV;
+                for (int u = tid; u < T * 5; u += ATTN_TC_THREADS) {  // five 128-byte lines per row
+                    const int r = u / 5, w = u % 5;
+                    const int16_t* a = w < 3 ? ap.q + (nrow0 + r) * D_MODEL + ng * 192 + w * 64
+                                             : (w == 3 ? ap.k : ap.v) + (nrow0 + r) * 192 + ng * 64;
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+                }
+            }
+        }
 
         for (int h = 0; h < 3; ++h) {  // h = packed tile
             const int slot = 4 * h + quad, hq = slot % 3, bq = 3 - slot / 3;
