@@ -148,7 +148,12 @@ struct GemmCfg {
                                      : (KIND == EPI_RESID || KIND == EPI_SWEEP) ? ((P == 4 && BN == 128) ? 2048 : (BN / 4) * 4 * 32)
                                      : (KIND == EPI_QKV ? 2048 : 0);
     static constexpr int STAGES = (P == 2) ? (KIND == EPI_LINEAR ? 4 : 3) : (BN == 128 ? 2 : 3);
-    static constexpr int EPI_WARPS = 16;  // 4 per TMEM lane quadrant, each owns 32 tile columns
+    // Epilogue warps: 4 per TMEM lane quadrant, each owning one 32-column group of the tile; gate/up
+    // uses 2 per quadrant, each taking two column groups in turn: 10 warps in all put at most 3 warps on
+    // an SM sub-partition, so its heavy epilogue gets 168 registers instead of 96 and does not spill
+    // (18 warps put 5 on two sub-partitions: 16384 / (5 x 32) registers per thread).
+    static constexpr int EPI_WARPS = KIND == EPI_GATEUP ? 8 : 16;
+    static constexpr int CG_PER_WARP = 16 / EPI_WARPS;
     static constexpr int EPI_THREADS = 32 * EPI_WARPS;
     static constexpr int THREADS = 64 + EPI_THREADS;
     static constexpr int BAR_BYTES = 512;
@@ -165,17 +170,17 @@ struct GemmCfg {
     static_assert(SMEM <= SMEM_LIMIT, "shared memory budget");
 };
 
-// Barrier of the 512 epilogue threads (named barrier 1) that also ANDs a flag across them, so that a
-// timed-out wait in one warp makes every epilogue warp leave together.
-__device__ __forceinline__ bool epi_barrier_and(bool v) {
+// Barrier of the nthreads epilogue threads (named barrier 1) that also ANDs a flag across them, so
+// that a timed-out wait in one warp makes every epilogue warp leave together.
+__device__ __forceinline__ bool epi_barrier_and(bool v, uint32_t nthreads) {
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred pi, po;\n\t"
         "setp.ne.u32 pi, %1, 0;\n\t"
-        "bar.red.and.pred po, 1, 512, pi;\n\t"
+        "bar.red.and.pred po, 1, %2, pi;\n\t"
         "selp.u32 %0, 1, 0, po;\n\t}\n"
         : "=r"(r)
-        : "r"(static_cast<uint32_t>(v))
+        : "r"(static_cast<uint32_t>(v)), "r"(nthreads)
         : "memory");
     return r != 0;
 }
@@ -919,9 +924,9 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
         }
     } else {
         const int e = warp - 2;
-        const int et = threadIdx.x - 64;  // 0 .. 511
+        const int et = threadIdx.x - 64;  // 0 .. EPI_THREADS - 1
         const int quad = warp & 3;
-        const int cg = e >> 2;
+        const int cg = e >> 2;  // first column group of this warp
         uint8_t* stg = staging + e * C::STG_BYTES;
         const EpiMaps maps{&tmC0, &tmC1, &tmC2};
         uint32_t xphase = 0;
@@ -1002,7 +1007,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
                 ok = ok && mbar_wait(&xbar[e], xphase, abort, ep.err, ERR_TIMEOUT_EPI);
                 xphase ^= 1;
             }
-            if (!epi_barrier_and(ok)) break;
+            if (!epi_barrier_and(ok, C::EPI_THREADS)) break;
             tc_fence_after();
             // parameters of this CTA's next tile go into the other buffer now (published by the next
             // tile's barrier), so their global-load latency is hidden behind this tile's epilogue
@@ -1013,15 +1018,19 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
             }
             const uint64_t* digw = digw_all + (acc_iter & 1) * C::BN;
             const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
-            if (KIND != EPI_LINEAR && ep.narrow && (KIND == EPI_QKV || KIND == EPI_GATEUP))
-                epilogue_tile<P, KIND, 2>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                          xphase, abort, digw, dsum, asum);
-            else if (KIND != EPI_LINEAR && KIND != EPI_QKV && ep.fast)
-                epilogue_tile<P, KIND, 1>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                          xphase, abort, digw, dsum, asum);
-            else
-                epilogue_tile<P, KIND, 0>(ep, tacc, m_blk, n_blk, cg, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                          xphase, abort, digw, dsum, asum);
+#pragma unroll 1
+            for (int k = 0; k < C::CG_PER_WARP; ++k) {  // this warp's column groups (one, or two for gate/up)
+                const int cgk = cg + k * (C::EPI_WARPS / 4);
+                if (KIND != EPI_LINEAR && ep.narrow && (KIND == EPI_QKV || KIND == EPI_GATEUP))
+                    epilogue_tile<P, KIND, 2>(ep, tacc, m_blk, n_blk, cgk, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
+                                              xphase, abort, digw, dsum, asum);
+                else if (KIND != EPI_LINEAR && KIND != EPI_QKV && ep.fast)
+                    epilogue_tile<P, KIND, 1>(ep, tacc, m_blk, n_blk, cgk, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
+                                              xphase, abort, digw, dsum, asum);
+                else
+                    epilogue_tile<P, KIND, 0>(ep, tacc, m_blk, n_blk, cgk, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
+                                              xphase, abort, digw, dsum, asum);
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
