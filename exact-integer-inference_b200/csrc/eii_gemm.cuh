@@ -148,11 +148,16 @@ struct GemmCfg {
                                      : (KIND == EPI_RESID || KIND == EPI_SWEEP) ? ((P == 4 && BN == 128) ? 2048 : (BN / 4) * 4 * 32)
                                      : (KIND == EPI_QKV ? 2048 : 0);
     static constexpr int STAGES = (P == 2) ? (KIND == EPI_LINEAR ? 4 : 3) : (BN == 128 ? 2 : 3);
-    // Epilogue warps: 4 per TMEM lane quadrant, each owning one 32-column group of the tile; gate/up
-    // uses 2 per quadrant, each taking two column groups in turn: 10 warps in all put at most 3 warps on
-    // an SM sub-partition, so its heavy epilogue gets 168 registers instead of 96 and does not spill
-    // (18 warps put 5 on two sub-partitions: 16384 / (5 x 32) registers per thread).
-    static constexpr int EPI_WARPS = KIND == EPI_GATEUP ? 8 : 16;
+    // Epilogue warps: 4 per TMEM lane quadrant, each owning one 32-column group of the tile.  Gate/up
+    // and QKV use 2 per quadrant, each taking two column groups in turn (with a staging buffer for
+    // each): 10 warps in all put at most 3 warps on an SM sub-partition, so these heavy epilogues get
+    // 168 registers instead of 96 and do not spill (18 warps put 5 on two sub-partitions: 16384 /
+    // (5 x 32) registers per thread); measured -10% (gate/up) and -6% (QKV).  The logits epilogue does
+    // not spill at 96 and ran 5% slower with 8 warps; the residual epilogue loads one residual tile
+    // per warp.  Both keep 16.  (The feature-major GEMM's 4-plane residual epilogue with 8 warps, two
+    // row quarters each, stopped spilling but ran 30% slower: its per-row residual loads are latency
+    // bound, and half the warps keep half as many in flight.)
+    static constexpr int EPI_WARPS = (KIND == EPI_GATEUP || KIND == EPI_QKV) ? 8 : 16;
     static constexpr int CG_PER_WARP = 16 / EPI_WARPS;
     static constexpr int EPI_THREADS = 32 * EPI_WARPS;
     static constexpr int THREADS = 64 + EPI_THREADS;
@@ -163,7 +168,7 @@ struct GemmCfg {
     // QKV: the RoPE cos/sin rows of positions pos0 .. pos0 + T - 1 (T <= 128), rows padded to 36 words
     static constexpr int ROPE_BYTES = KIND == EPI_QKV ? 2 * ROPE_SMEM_ROWS * ROPE_SMEM_PITCH * 4 : 0;
     static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;  // 1024-aligned
-    static constexpr int BAR_OFFSET = STG_OFFSET + EPI_WARPS * STG_BYTES;
+    static constexpr int BAR_OFFSET = STG_OFFSET + EPI_WARPS * CG_PER_WARP * STG_BYTES;
     static constexpr int SMEM = BAR_OFFSET + 1024 + BAR_BYTES + COLP_BYTES + DIGW_BYTES + SILU_BYTES + ROPE_BYTES;
     static_assert(NB >= 1, "accumulators must fit in TMEM");
     static_assert(STG_BYTES % 1024 == 0, "staging buffers are 1024-byte aligned");
@@ -357,7 +362,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                                               int quad, int lane, const int4* colp, const void* silu_tab,
                                               uint8_t* stg, const EpiMaps& maps, uint64_t* xbar, uint32_t& xphase,
                                               volatile int* abort, const uint64_t* digw, uint64_t& dsum,
-                                              uint64_t& asum) {
+                                              uint64_t& asum, bool first_cg) {
     constexpr int BN = (P == 4) ? BN_P4 : 128;
     const int row = m_blk * 128 + quad * 32 + lane;
     const bool row_ok = row < ep.M;
@@ -381,7 +386,9 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
         // staging: dims [sub, sub + 16) and [32 + sub, 32 + sub + 16) of the head, 32 rows each (SW32)
         uint8_t* sa = stg;
         uint8_t* sb = stg + 1024;
-        if (lane == 0) bulk_wait_read0();
+        // a warp's first column group of a tile waits until every earlier store has read its staging
+        // buffer (one buffer per column group of the warp, so the second group need not wait)
+        if (lane == 0 && first_cg) bulk_wait_read0();
         __syncwarp();
 #pragma unroll 1
         for (int h8 = 0; h8 < 16; h8 += 8) {  // 8 dims at a time keeps the pass free of spills
@@ -704,7 +711,8 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
     } else {
         constexpr int NCOL = BN / 4;  // columns of this warp: 32 (P = 2) or 16 (P = 4)
         if constexpr (KIND == EPI_LOGITS) {
-            if (lane == 0) bulk_wait_read0();  // the previous tile's store has read the staging buffer
+            // as QKV: the warp's first column group of the tile waits for every earlier store's read
+            if (lane == 0 && first_cg) bulk_wait_read0();
             __syncwarp();
         }
 #pragma unroll 1
@@ -927,7 +935,7 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
         const int et = threadIdx.x - 64;  // 0 .. EPI_THREADS - 1
         const int quad = warp & 3;
         const int cg = e >> 2;  // first column group of this warp
-        uint8_t* stg = staging + e * C::STG_BYTES;
+        uint8_t* stg = staging + e * C::CG_PER_WARP * C::STG_BYTES;  // one buffer per column group of the warp
         const EpiMaps maps{&tmC0, &tmC1, &tmC2};
         uint32_t xphase = 0;
         if constexpr (KIND == EPI_QKV) {
@@ -1021,15 +1029,16 @@ __global__ void __launch_bounds__(GemmCfg<P, KIND>::THREADS, 1)
 #pragma unroll 1
             for (int k = 0; k < C::CG_PER_WARP; ++k) {  // this warp's column groups (one, or two for gate/up)
                 const int cgk = cg + k * (C::EPI_WARPS / 4);
+                uint8_t* stgk = stg + k * C::STG_BYTES;
                 if (KIND != EPI_LINEAR && ep.narrow && (KIND == EPI_QKV || KIND == EPI_GATEUP))
-                    epilogue_tile<P, KIND, 2>(ep, tacc, m_blk, n_blk, cgk, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                              xphase, abort, digw, dsum, asum);
+                    epilogue_tile<P, KIND, 2>(ep, tacc, m_blk, n_blk, cgk, quad, lane, colp, silu_tab, stgk, maps, &xbar[e],
+                                              xphase, abort, digw, dsum, asum, k == 0);
                 else if (KIND != EPI_LINEAR && KIND != EPI_QKV && ep.fast)
-                    epilogue_tile<P, KIND, 1>(ep, tacc, m_blk, n_blk, cgk, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                              xphase, abort, digw, dsum, asum);
+                    epilogue_tile<P, KIND, 1>(ep, tacc, m_blk, n_blk, cgk, quad, lane, colp, silu_tab, stgk, maps, &xbar[e],
+                                              xphase, abort, digw, dsum, asum, k == 0);
                 else
-                    epilogue_tile<P, KIND, 0>(ep, tacc, m_blk, n_blk, cgk, quad, lane, colp, silu_tab, stg, maps, &xbar[e],
-                                              xphase, abort, digw, dsum, asum);
+                    epilogue_tile<P, KIND, 0>(ep, tacc, m_blk, n_blk, cgk, quad, lane, colp, silu_tab, stgk, maps, &xbar[e],
+                                              xphase, abort, digw, dsum, asum, k == 0);
             }
             tc_fence_before();
             __syncwarp();
