@@ -124,8 +124,8 @@ __device__ __forceinline__ int reduce_rows16_row(int lane) {
 }
 
 // 64-bit requantisation sum of one (feature, row): sum_p 2^(8p) v_p m + K (mod 2^64), m < 2^15.
-template <int P>
-__device__ __forceinline__ uint64_t tg_sum(const uint32_t (&v)[P][16], int i, int m, uint64_t kc) {
+template <int P, int N = 16>
+__device__ __forceinline__ uint64_t tg_sum(const uint32_t (&v)[P][N], int i, int m, uint64_t kc) {
     uint64_t t = static_cast<uint64_t>(static_cast<int64_t>(static_cast<int32_t>(v[0][i])) * m) + kc;
     t += static_cast<uint64_t>(static_cast<int64_t>(static_cast<int32_t>(v[1][i])) * (m << 8));
     if constexpr (P == 4) {
@@ -411,6 +411,32 @@ __global__ void __launch_bounds__(TCfg<P, RES>::THREADS, 1)
 #pragma unroll
             for (int j = 0; j < NCH; ++j) {
                 const int row0 = r_blk * C::BR + rsub * C::ROWS_PER_WARP + 16 * j;
+                if constexpr (KIND == EPI_RESID && P == 4) {
+                    // four planes: two halves of 8 rows, so that a half's planes and residuals fit the
+                    // 96 registers of the 16-warp epilogue without spilling
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int r0 = row0 + 8 * hh;
+                        int32_t* xp = ep.out + static_cast<int64_t>(r0) * ep.ld + f;
+                        int32_t x8[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) x8[i] = (f_ok && r0 + i < ep.M) ? xp[i * ep.ld] : 0;
+                        uint32_t v8[P][8];
+#pragma unroll
+                        for (int p = 0; p < P; ++p) tmem_ld8(tacc + p * C::BR + 16 * j + 8 * hh, v8[p]);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int p = 0; p < P; ++p) tmem_launder(v8[p]);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int64_t y = (static_cast<int64_t>(tg_sum<P, 8>(v8, i, fc.x, kc)) >> fc.y) + x8[i];
+                            const int32_t r = static_cast<int32_t>(
+                                min(max(y, static_cast<int64_t>(INT32_MIN)), static_cast<int64_t>(INT32_MAX)));
+                            if (f_ok && r0 + i < ep.M) xp[i * ep.ld] = r;
+                        }
+                    }
+                    continue;
+                }
                 int32_t xo[16];
                 if constexpr (KIND == EPI_RESID) {  // this lane's residual column of the 16 rows (coalesced over lanes)
                     const int32_t* xp = ep.out + static_cast<int64_t>(row0) * ep.ld + f;
