@@ -585,37 +585,44 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 if (!mbar_wait(xbar, xphase, abort, ep.err, ERR_TIMEOUT_EPI)) return;
                 xphase ^= 1;
             }
-            uint32_t v[P][16];
-            load_planes<P, 16>(tacc + tc, v);
-            if constexpr (P == 4) {
-                if (!top4) {  // top signed-digit plane not computed for this row block
+            // two planes: two sub-rounds of 8 columns, whose planes and residuals fit the 96 registers
+            // of the 16-warp epilogue without spilling (four planes spill elsewhere; one round of 16)
+            constexpr int RW = P == 2 ? 8 : 16;
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) v[3][q] = 0;
-                }
-            }
-            if (row_ok) {
-                int32_t xo[16];
+            for (int h = 0; h < 16; h += RW) {
+                uint32_t v[P][RW];
+                load_planes<P, RW>(tacc + tc + h, v);
+                if constexpr (P == 4) {
+                    if (!top4) {  // top signed-digit plane not computed for this row block
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<int4*>(&xo[4 * q]) = *reinterpret_cast<const int4*>(stg + stg_off<S>(lane, 4 * slot + q));
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int4 cp = colp[tc + i];
-                    if constexpr (MODE >= 1) {
-                        int32_t hi;
-                        uint32_t lo;
-                        shr31(mulround<P, 16>(v, i, cp), cp.y, hi, lo);
-                        const int64_t r = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(hi)) << 32) | lo);
-                        const int64_t y = r + xo[i];
-                        xo[i] = sat_hl(static_cast<int32_t>(static_cast<uint64_t>(y) >> 32), static_cast<uint32_t>(y), 32);
-                    } else {
-                        const int64_t r = rs_col(combine<P, 16>(v, i) * static_cast<int64_t>(cp.x), cp.y);
-                        xo[i] = static_cast<int32_t>(sat64(static_cast<int64_t>(xo[i]) + r, 32));
+                        for (int q = 0; q < RW; ++q) v[3][q] = 0;
                     }
                 }
+                if (row_ok) {
+                    int32_t xo[RW];
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<int4*>(stg + stg_off<S>(lane, 4 * slot + q)) = *reinterpret_cast<int4*>(&xo[4 * q]);
+                    for (int q = 0; q < RW / 4; ++q)
+                        *reinterpret_cast<int4*>(&xo[4 * q]) =
+                            *reinterpret_cast<const int4*>(stg + stg_off<S>(lane, 4 * slot + h / 4 + q));
+#pragma unroll
+                    for (int i = 0; i < RW; ++i) {
+                        const int4 cp = colp[tc + h + i];
+                        if constexpr (MODE >= 1) {
+                            int32_t hi;
+                            uint32_t lo;
+                            shr31(mulround<P, RW>(v, i, cp), cp.y, hi, lo);
+                            const int64_t r = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(hi)) << 32) | lo);
+                            const int64_t y = r + xo[i];
+                            xo[i] = sat_hl(static_cast<int32_t>(static_cast<uint64_t>(y) >> 32), static_cast<uint32_t>(y), 32);
+                        } else {
+                            const int64_t r = rs_col(combine<P, RW>(v, i) * static_cast<int64_t>(cp.x), cp.y);
+                            xo[i] = static_cast<int32_t>(sat64(static_cast<int64_t>(xo[i]) + r, 32));
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < RW / 4; ++q)
+                        *reinterpret_cast<int4*>(stg + stg_off<S>(lane, 4 * slot + h / 4 + q)) = *reinterpret_cast<int4*>(&xo[4 * q]);
+                }
             }
             if (XCH == 1) {
                 fence_async_smem();
