@@ -207,6 +207,30 @@ __device__ __forceinline__ void load_planes(uint32_t taddr, uint32_t (&v)[P][N])
     for (int p = 0; p < P; ++p) tmem_launder(v[p]);
 }
 
+// Two sets of columns (e.g. gate and up, or RoPE partners d and d + 32) behind one wait::ld, so the
+// second set's TMEM latency overlaps the first's.
+template <int P, int N>
+__device__ __forceinline__ void load_planes2(uint32_t ta, uint32_t (&va)[P][N], uint32_t tb, uint32_t (&vb)[P][N]) {
+    static_assert(N == 8 || N == 16, "8 or 16 columns");
+    constexpr int PS = (P == 4) ? BN_P4 : 128;
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+        if constexpr (N == 16) {
+            tmem_ld16(ta + p * PS, va[p]);
+            tmem_ld16(tb + p * PS, vb[p]);
+        } else {
+            tmem_ld8(ta + p * PS, va[p]);
+            tmem_ld8(tb + p * PS, vb[p]);
+        }
+    }
+    tmem_wait_ld();
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+        tmem_launder(va[p]);
+        tmem_launder(vb[p]);
+    }
+}
+
 template <int P, int N>
 __device__ __forceinline__ int64_t combine(const uint32_t (&v)[P][N], int i) {
     int64_t a = 0;
@@ -414,8 +438,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 }
             }
             uint32_t va[P][8], vb[P][8];
-            load_planes<P, 8>(tacc + 64 * hl + d0, va);
-            load_planes<P, 8>(tacc + 64 * hl + 32 + d0, vb);
+            load_planes2<P, 8>(tacc + 64 * hl + d0, va, tacc + 64 * hl + 32 + d0, vb);
             if (!row_ok) continue;
             int16_t oa[8], ob[8];
 #pragma unroll
@@ -485,8 +508,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
         for (int h8 = 0; h8 < 16; h8 += 8) {  // 8 features at a time keeps the pass free of spills
             const int f0 = 16 * cg + h8;
             uint32_t vg[P][8], vu[P][8];
-            load_planes<P, 8>(tacc + f0, vg);
-            load_planes<P, 8>(tacc + 64 + f0, vu);
+            load_planes2<P, 8>(tacc + f0, vg, tacc + 64 + f0, vu);
             if (!row_ok) continue;
             int32_t gm[8];
             const int16_t* tab16 = static_cast<const int16_t*>(silu_tab);
