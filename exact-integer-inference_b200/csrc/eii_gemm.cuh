@@ -14,10 +14,11 @@
 //               weight tile [128 x 128 B], 128-byte swizzle, into a STAGES-deep smem ring.
 //   warp 1      TMEM allocator + single-thread MMA issuer: 4 (or 2 for a half block) K=32 steps
 //               x P planes of tcgen05.mma.cta_group::1.kind::i8, M=128, N=n_valid.
-//   warps 2-17  16 epilogue warps (4 per TMEM lane quadrant): tcgen05.ld of the P accumulators,
-//               plane combination, requantise RS/SAT, and the fused step of the caller (RoPE,
-//               residual add, SiLU-gated product, logits and digest), stored through shared-memory
-//               staging and TMA (or straight to the row-blocked gated planes).
+//   warps 2..   epilogue warps (16, 4 per TMEM lane quadrant; 8, 2 per quadrant, for gate/up and
+//               QKV, see GemmCfg::EPI_WARPS): tcgen05.ld of the P accumulators, plane combination,
+//               requantise RS/SAT, and the fused step of the caller (RoPE, residual add, SiLU-gated
+//               product, logits and digest), stored through shared-memory staging and TMA (or
+//               straight to the row-blocked gated planes).
 // TMEM: P*BN int32 columns per accumulator set; 2 sets (double buffered) for P = 2, one for P = 4.
 #pragma once
 #include <cstdint>
