@@ -83,6 +83,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
     if (warp == 0) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
     if (tid == 0) { mbar_init(bar, 1); mbar_init(bar + 1, 1); *abort = 0; fence_mbar_init(); }
     for (int u = tid; u <= DMAX; u += ATTN_TC_THREADS) E[u] = ap.exp_tab[u];  // model table
+    if (tid == 0) E[DMAX + 1] = 0;  // the softmax clamps distances past DMAX to this entry
     griddep_wait();  // q, k, v are the previous kernel's output
     griddep_launch();
     tc_fence_before();
@@ -271,36 +272,49 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                 // a thread's key groups ascend with m, so the live ones are m < nm (branches, not predicates:
                 // the unrolled division would otherwise run for every key of the row's 128)
                 const int nm = nk > 4 * jq ? (nk - 4 * jq + 15) / 16 : 0;
+                // scores stay packed as int16 pairs: the row max by 16-bit SIMD max, the keys of the row's
+                // last group past its position (live < 4) replaced by -32768, which cannot raise it
                 uint2 sv[8];
-                int32_t mx = -32768;
+                uint32_t mx2 = 0x80008000u;
 #pragma unroll
                 for (int m = 0; m < 8; ++m) {
                     if (m >= nm) break;
                     const int k0 = 4 * (jq + 4 * m);
                     sv[m] = *reinterpret_cast<const uint2*>(srow + k0);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
-                        if (k0 + u < nk) mx = max(mx, sk);
+                    uint2 w = sv[m];
+                    const int live = nk - k0;  // >= 1
+                    if (live < 4) {
+                        if (live < 2) w.x = (w.x & 0xFFFFu) | 0x80000000u;
+                        w.y = live < 3 ? 0x80008000u : ((w.y & 0xFFFFu) | 0x80000000u);
                     }
+                    mx2 = __vmaxs2(mx2, __vmaxs2(w.x, w.y));
                 }
+                int32_t mx = max(static_cast<int32_t>(static_cast<int16_t>(mx2 & 0xFFFFu)),
+                                 static_cast<int32_t>(static_cast<int16_t>(mx2 >> 16)));
                 mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
                 mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
                 // e of each live key (0 past the row's position or beyond DMAX, which makes P = 0 below),
                 // kept in this thread's shared-memory slots for the division pass
+                // distances mx - s in [0, 65535] by 16-bit SIMD subtraction (exact modulo 2^16), clamped to
+                // DMAX + 1 (E there is 0); pairs of e <= 2^30 add up exactly in 32 bits
                 int64_t z = 0;
+                const uint32_t mxx = (static_cast<uint32_t>(mx) & 0xFFFFu) * 0x10001u;
+                constexpr uint32_t cap = static_cast<uint32_t>(DMAX + 1) * 0x10001u;
 #pragma unroll
                 for (int m = 0; m < 8; ++m) {
                     if (m >= nm) break;
                     const int k0 = 4 * (jq + 4 * m);
-                    int32_t ev[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int32_t sk = static_cast<int16_t>((u < 2 ? sv[m].x : sv[m].y) >> (16 * (u & 1)));
-                        const int32_t dd = mx - sk;
-                        ev[u] = (k0 + u < nk && dd <= DMAX) ? E[dd] : 0;
-                        z += ev[u];
+                    const uint32_t d01 = __vminu2(__vsub2(mxx, sv[m].x), cap);
+                    const uint32_t d23 = __vminu2(__vsub2(mxx, sv[m].y), cap);
+                    int32_t ev[4] = {E[d01 & 0xFFFFu], E[d01 >> 16], E[d23 & 0xFFFFu], E[d23 >> 16]};
+                    const int live = nk - k0;  // keys past the row's position get e = 0
+                    if (live < 4) {
+                        if (live < 2) ev[1] = 0;
+                        if (live < 3) ev[2] = 0;
+                        ev[3] = 0;
                     }
+                    z += static_cast<int64_t>(static_cast<uint32_t>(ev[0]) + static_cast<uint32_t>(ev[1])) +
+                         static_cast<int64_t>(static_cast<uint32_t>(ev[2]) + static_cast<uint32_t>(ev[3]));
                     Et[m * ATTN_TC_THREADS + tid] = make_int4(ev[0], ev[1], ev[2], ev[3]);
                 }
                 z += __shfl_xor_sync(0xffffffffu, z, 1);
