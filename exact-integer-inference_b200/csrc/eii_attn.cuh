@@ -43,6 +43,13 @@ constexpr int ATTN_ET_BYTES = 8 * 512 * 16;
 //       e values | scores [128][144] int16 | E | j* [128] int32 | barrier, TMEM slot, abort
 constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + ATTN_ET_BYTES + 128 * ATTN_SS_PITCH * 2 + (DMAX + 1 + 3) * 4 + 128 * 4 + 64;
 
+// Two int32 saturated to int16 and packed: hi into bits 31..16, lo into bits 15..0.
+__device__ __forceinline__ uint32_t pack_sat_s16(int32_t hi, int32_t lo) {
+    uint32_t d;
+    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(d) : "r"(hi), "r"(lo));
+    return d;
+}
+
 // Byte offset of byte b of row r inside a 128-byte-row tile with the 128-byte swizzle.
 __device__ __forceinline__ int sw128(int r, int b) { return r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15); }
 
@@ -240,16 +247,17 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                             if (fast) {
                                 // S + 2^(sh-1) = 2^8 (2^8 a2 + a1 + ((a0 + 2^(sh-1)) >> 8)) + ((a0 + 2^(sh-1)) & 255),
                                 // so RS(S, sh) = (2^8 a2 + a1 + ((a0 + 2^(sh-1)) >> 8)) >> (sh - 8): every term
-                                // fits int32 (|a0| < 2^22, |a1| < 2^22, |a2| <= 2^20, 2^(sh-1) <= 2^30)
+                                // fits int32 (|a0| < 2^22, |a1| < 2^22, |a2| <= 2^20, 2^(sh-1) <= 2^30); SAT16 is
+                                // applied by the saturating pack below
                                 const int32_t t = a2 * 256 + a1 + ((a0 + static_cast<int32_t>(srnd)) >> 8);
-                                s2[u] = min(max(t >> (ap.shift_s - 8), -32768), 32767);
+                                s2[u] = t >> (ap.shift_s - 8);
                             } else {
                                 const int64_t S = static_cast<int64_t>(a2) * 65536 + static_cast<int64_t>(a1) * 256 +
                                                   static_cast<int64_t>(a0);
                                 s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
                             }
                         }
-                        sp[q / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
+                        sp[q / 2] = pack_sat_s16(s2[1], s2[0]);  // key q in the low half, q + 1 in the high
                     }
                     uint4* dst = reinterpret_cast<uint4*>(Ss + i * ATTN_SS_PITCH + col);
                     dst[0] = make_uint4(sp[0], sp[1], sp[2], sp[3]);
@@ -605,14 +613,14 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc_long(AttnPa
                                           a2 = static_cast<int32_t>(d2[q + u]);
                             if (fast) {  // exact 32-bit form of RS(65536 a2 + 256 a1 + a0, sh), as the short kernel
                                 const int32_t t = a2 * 256 + a1 + ((a0 + srnd) >> 8);
-                                s2[u] = min(max(t >> (ap.shift_s - 8), -32768), 32767);
+                                s2[u] = t >> (ap.shift_s - 8);  // SAT16 by the saturating pack
                             } else {
                                 const int64_t S = static_cast<int64_t>(a2) * 65536 + static_cast<int64_t>(a1) * 256 +
                                                   static_cast<int64_t>(a0);
                                 s2[u] = static_cast<int32_t>(sat64(rs64(S, ap.shift_s), 16));
                             }
                         }
-                        sp[q / 2] = (static_cast<uint32_t>(s2[0]) & 0xFFFF) | (static_cast<uint32_t>(s2[1]) << 16);
+                        sp[q / 2] = pack_sat_s16(s2[1], s2[0]);
                     }
                     uint4* dst = reinterpret_cast<uint4*>(Ss + i * ATTNL_SS_PITCH + 128 * kt + col);
                     dst[0] = make_uint4(sp[0], sp[1], sp[2], sp[3]);
