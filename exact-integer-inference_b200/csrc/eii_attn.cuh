@@ -427,16 +427,14 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                     // row-blocked planes: this warp's 32 rows x 16 dims are 512 contiguous bytes per plane
                     const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
                     uint4* dst = reinterpret_cast<uint4*>(ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL));
-                    uint32_t w[4];
-                    pack_plane<0, 16>(out, w);
-                    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                    pack_plane<1, 16>(out, w);
-                    dst[pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                    uint32_t w[4][4];
+                    if (ap.P == 4) pack_planes<16, true>(out, w[0], w[1], w[2], w[3]);
+                    else pack_planes<16, false>(out, w[0], w[1], w[2], w[3]);
+                    dst[0] = make_uint4(w[0][0], w[0][1], w[0][2], w[0][3]);
+                    dst[pstride / 16] = make_uint4(w[1][0], w[1][1], w[1][2], w[1][3]);
                     if (ap.P == 4) {
-                        pack_plane<2, 16>(out, w);
-                        dst[2 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
-                        pack_plane<3, 16>(out, w);
-                        dst[3 * pstride / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+                        dst[2 * pstride / 16] = make_uint4(w[2][0], w[2][1], w[2][2], w[2][3]);
+                        dst[3 * pstride / 16] = make_uint4(w[3][0], w[3][1], w[3][2], w[3][3]);
                     }
                 }
             }

@@ -334,6 +334,27 @@ __device__ __forceinline__ void pack_plane(const int32_t (&x)[N], uint32_t (&w)[
     }
 }
 
+// All byte planes of N values at once by a byte transpose of each group of four: planes 0 and 1
+// (two permutes each per four values, against three per plane one plane at a time), and with
+// FOUR, planes 2 and 3 as well (eight permutes per four values for the four planes, against twelve).
+template <int N, bool FOUR>
+__device__ __forceinline__ void pack_planes(const int32_t (&x)[N], uint32_t (&w0)[N / 4], uint32_t (&w1)[N / 4],
+                                            uint32_t (&w2)[N / 4], uint32_t (&w3)[N / 4]) {
+#pragma unroll
+    for (int q = 0; q < N / 4; ++q) {
+        const uint32_t x0 = static_cast<uint32_t>(x[4 * q]), x1 = static_cast<uint32_t>(x[4 * q + 1]);
+        const uint32_t x2 = static_cast<uint32_t>(x[4 * q + 2]), x3 = static_cast<uint32_t>(x[4 * q + 3]);
+        const uint32_t t0 = __byte_perm(x0, x1, 0x5140), t2 = __byte_perm(x2, x3, 0x5140);  // bytes 0, 1 of each
+        w0[q] = __byte_perm(t0, t2, 0x5410);
+        w1[q] = __byte_perm(t0, t2, 0x7632);
+        if constexpr (FOUR) {
+            const uint32_t t1 = __byte_perm(x0, x1, 0x7362), t3 = __byte_perm(x2, x3, 0x7362);  // bytes 2, 3
+            w2[q] = __byte_perm(t1, t3, 0x5410);
+            w3[q] = __byte_perm(t1, t3, 0x7632);
+        }
+    }
+}
+
 // Gate/up/SiLU/gated product for 16 features, all-32-bit path: INT16 gate and up, compact INT16
 // SiLU table with shift d <= 15 (so g * 2^d < 2^31), gated shift in [0, 31].
 // The compact table holds count = 1 - lo_g entries for inputs lo_g .. 0 and a zero past them
@@ -562,23 +583,17 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                 big |= (any >> 24) != 0;
             }
             if (h8 == 0) {
-                pack_plane<0, 8>(gm, keep[0]);
-                pack_plane<1, 8>(gm, keep[1]);
-                if (ep.gated_P == 4) {
-                    pack_plane<2, 8>(gm, keep[2]);
-                    pack_plane<3, 8>(gm, keep[3]);
-                }
+                if (ep.gated_P == 4) pack_planes<8, true>(gm, keep[0], keep[1], keep[2], keep[3]);
+                else pack_planes<8, false>(gm, keep[0], keep[1], keep[2], keep[3]);
             } else {
-                uint32_t w[2];
-                pack_plane<0, 8>(gm, w);
-                *reinterpret_cast<uint4*>(gdst) = make_uint4(keep[0][0], keep[0][1], w[0], w[1]);
-                pack_plane<1, 8>(gm, w);
-                *reinterpret_cast<uint4*>(gdst + plane_stride) = make_uint4(keep[1][0], keep[1][1], w[0], w[1]);
+                uint32_t w[4][2];
+                if (ep.gated_P == 4) pack_planes<8, true>(gm, w[0], w[1], w[2], w[3]);
+                else pack_planes<8, false>(gm, w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(gdst) = make_uint4(keep[0][0], keep[0][1], w[0][0], w[0][1]);
+                *reinterpret_cast<uint4*>(gdst + plane_stride) = make_uint4(keep[1][0], keep[1][1], w[1][0], w[1][1]);
                 if (ep.gated_P == 4) {
-                    pack_plane<2, 8>(gm, w);
-                    *reinterpret_cast<uint4*>(gdst + 2 * plane_stride) = make_uint4(keep[2][0], keep[2][1], w[0], w[1]);
-                    pack_plane<3, 8>(gm, w);
-                    *reinterpret_cast<uint4*>(gdst + 3 * plane_stride) = make_uint4(keep[3][0], keep[3][1], w[0], w[1]);
+                    *reinterpret_cast<uint4*>(gdst + 2 * plane_stride) = make_uint4(keep[2][0], keep[2][1], w[2][0], w[2][1]);
+                    *reinterpret_cast<uint4*>(gdst + 3 * plane_stride) = make_uint4(keep[3][0], keep[3][1], w[3][0], w[3][1]);
                 }
             }
         }
