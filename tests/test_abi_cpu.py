@@ -46,6 +46,12 @@ def test_status_and_errors_without_gpu(tmp_path):
     assert b"missing.bin" in L.eii_last_error()
     assert L.eii_open(None, 0, ctypes.byref(h)) == _eii.EII_ERR_ARG
     assert L.eii_forward(None, None, 1, 1, None, None, None, None) == _eii.EII_ERR_ARG
+    # decoder entry points: a null decoder is an argument error before any device call
+    assert L.eii_decoder_step_device(None, None, None, _eii.VOCAB, None, None) == _eii.EII_ERR_ARG
+    assert L.eii_decoder_step_device_async(None, None, None, _eii.VOCAB, None, None) == _eii.EII_ERR_ARG
+    assert b"decoder is null" in L.eii_last_error()
+    assert L.eii_decoder_sync(None, None) == _eii.EII_ERR_ARG
+    assert L.eii_decoder_position(None) == -1
     assert L.eii_kernel_name(2) == b"gemm_qkv_rope"
 
 
