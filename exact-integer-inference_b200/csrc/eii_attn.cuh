@@ -43,13 +43,6 @@ constexpr int ATTN_ET_BYTES = 8 * 512 * 16;
 //       e values | scores [128][144] int16 | E | j* [128] int32 | barrier, TMEM slot, abort
 constexpr int ATTN_TC_SMEM = 7 * ATTN_TC_TILE + 1024 + ATTN_ET_BYTES + 128 * ATTN_SS_PITCH * 2 + (DMAX + 1 + 3) * 4 + 128 * 4 + 64;
 
-// Two int32 saturated to int16 and packed: hi into bits 31..16, lo into bits 15..0.
-__device__ __forceinline__ uint32_t pack_sat_s16(int32_t hi, int32_t lo) {
-    uint32_t d;
-    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(d) : "r"(hi), "r"(lo));
-    return d;
-}
-
 // Byte offset of byte b of row r inside a 128-byte-row tile with the 128-byte swizzle.
 __device__ __forceinline__ int sw128(int r, int b) { return r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15); }
 

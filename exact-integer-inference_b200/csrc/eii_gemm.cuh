@@ -462,7 +462,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
             uint32_t va[P][8], vb[P][8];
             load_planes2<P, 8>(tacc + 64 * hl + d0, va, tacc + 64 * hl + 32 + d0, vb);
             if (!row_ok) continue;
-            int16_t oa[8], ob[8];
+            int32_t oa[8], ob[8];  // int16 values (the narrow RoPE path leaves SAT16 to the pack below)
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int4 ca = colp[64 * hl + d0 + i], cb = colp[64 * hl + 32 + d0 + i];
@@ -482,10 +482,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                     const int64_t t2 = static_cast<int64_t>(b) * rc[i] + static_cast<int64_t>(a) * rsn[i];
                     if constexpr (MODE == 2) {
                         const int64_t u1 = t1 + rrnd, u2 = t2 + rrnd;
-                        oa[i] = static_cast<int16_t>(clamp16(static_cast<int32_t>(__funnelshift_r(
-                            static_cast<uint32_t>(u1), static_cast<uint32_t>(static_cast<uint64_t>(u1) >> 32), rshift))));
-                        ob[i] = static_cast<int16_t>(clamp16(static_cast<int32_t>(__funnelshift_r(
-                            static_cast<uint32_t>(u2), static_cast<uint32_t>(static_cast<uint64_t>(u2) >> 32), rshift))));
+                        oa[i] = static_cast<int32_t>(__funnelshift_r(static_cast<uint32_t>(u1),
+                                                                     static_cast<uint32_t>(static_cast<uint64_t>(u1) >> 32), rshift));
+                        ob[i] = static_cast<int32_t>(__funnelshift_r(static_cast<uint32_t>(u2),
+                                                                     static_cast<uint32_t>(static_cast<uint64_t>(u2) >> 32), rshift));
                     } else if (ep.fast) {
                         int32_t hi;
                         uint32_t lo;
@@ -502,8 +502,13 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, uint32_t tacc
                     ob[i] = static_cast<int16_t>(b);
                 }
             }
-            *reinterpret_cast<uint4*>(sa + stg_off<32>(lane, h8 / 8)) = *reinterpret_cast<uint4*>(oa);
-            *reinterpret_cast<uint4*>(sb + stg_off<32>(lane, h8 / 8)) = *reinterpret_cast<uint4*>(ob);
+            // int16 pairs by saturating packs (value 2k in the low half)
+            *reinterpret_cast<uint4*>(sa + stg_off<32>(lane, h8 / 8)) =
+                make_uint4(pack_sat_s16(oa[1], oa[0]), pack_sat_s16(oa[3], oa[2]), pack_sat_s16(oa[5], oa[4]),
+                           pack_sat_s16(oa[7], oa[6]));
+            *reinterpret_cast<uint4*>(sb + stg_off<32>(lane, h8 / 8)) =
+                make_uint4(pack_sat_s16(ob[1], ob[0]), pack_sat_s16(ob[3], ob[2]), pack_sat_s16(ob[5], ob[4]),
+                           pack_sat_s16(ob[7], ob[6]));
         }
         fence_async_smem();
         __syncwarp();

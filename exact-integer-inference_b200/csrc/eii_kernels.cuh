@@ -275,12 +275,12 @@ __device__ __forceinline__ void rmsnorm_pair_finish(const int4 (&v)[9], int row,
             const int32_t z = static_cast<int32_t>(
                 __funnelshift_r(static_cast<uint32_t>(xu), static_cast<uint32_t>(static_cast<uint64_t>(xu) >> 32), 16));
             const int64_t t = static_cast<int64_t>(z) * (3 * g[q]) + rnd_out;
-            const int32_t r = static_cast<int32_t>(
+            o[q] = static_cast<int32_t>(
                 __funnelshift_r(static_cast<uint32_t>(t), static_cast<uint32_t>(static_cast<uint64_t>(t) >> 32), shift_out));
-            o[q] = min(max(r, -32768), 32767);
         }
-        const uint32_t w01 = __byte_perm(static_cast<uint32_t>(o[0]), static_cast<uint32_t>(o[1]), 0x5410);
-        const uint32_t w23 = __byte_perm(static_cast<uint32_t>(o[2]), static_cast<uint32_t>(o[3]), 0x5410);
+        // SAT16 and the int16 pairs (o0 | o1 << 16, o2 | o3 << 16) by saturating packs
+        const uint32_t w01 = pack_sat_s16(o[1], o[0]);
+        const uint32_t w23 = pack_sat_s16(o[3], o[2]);
         // plane 0 gets the low bytes (o0, o1, o2, o3), plane 1 the high bytes
         *reinterpret_cast<uint32_t*>(planes + static_cast<int64_t>(row) * D_MODEL + c) = __byte_perm(w01, w23, 0x6420);
         // top_flip = 0x80808080: offset-binary planes (the high byte's sign bit flipped)

@@ -68,6 +68,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// Two int32 saturated to int16 and packed: hi into bits 31..16, lo into bits 15..0.
+__device__ __forceinline__ uint32_t pack_sat_s16(int32_t hi, int32_t lo) {
+    uint32_t d;
+    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(d) : "r"(hi), "r"(lo));
+    return d;
+}
+
 // ------------------------------------------------------------------ programmatic dependent launch
 // griddep_wait: returns once the grids this one depends on (the previous kernel in the stream, when
 // launched with programmatic stream serialization) have completed and their writes are visible; a
