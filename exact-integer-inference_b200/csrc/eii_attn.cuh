@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                                 t += vj * 256;
                             }
                             int32_t r = t >> (ap.shift_c - 8);
-                            if (lim) r = min(max(r, -lim), lim - 1);
+                            if (lim && ap.P != 2) r = min(max(r, -lim), lim - 1);  // two planes: SAT16 by the pack below
                             out[q] = r;
                         }
                     } else {
@@ -412,20 +412,32 @@ __global__ void __launch_bounds__(ATTN_TC_THREADS, 1) k_attention_tc(AttnParams 
                             out[q] = static_cast<int32_t>(sat64(rs64(a, ap.shift_c), ap.bits_c));
                         }
                     }
-                    if (ap.offset) {  // offset binary: the bytes of ctx + 2^(8P - 1)
-                        const uint32_t flip = ap.P == 4 ? 0x80000000u : 0x8000u;
-#pragma unroll
-                        for (int q = 0; q < 16; ++q) out[q] = static_cast<int32_t>(static_cast<uint32_t>(out[q]) ^ flip);
-                    }
                     // row-blocked planes: this warp's 32 rows x 16 dims are 512 contiguous bytes per plane
                     const int64_t pstride = blocked_plane_stride(ap.M, D_MODEL);
                     uint4* dst = reinterpret_cast<uint4*>(ap.ctx_planes + blocked_off(row0 + pos, hh * 64 + col, D_MODEL));
-                    uint32_t w[4][4];
-                    if (ap.P == 4) pack_planes<16, true>(out, w[0], w[1], w[2], w[3]);
-                    else pack_planes<16, false>(out, w[0], w[1], w[2], w[3]);
-                    dst[0] = make_uint4(w[0][0], w[0][1], w[0][2], w[0][3]);
-                    dst[pstride / 16] = make_uint4(w[1][0], w[1][1], w[1][2], w[1][3]);
-                    if (ap.P == 4) {
+                    if (ap.P == 2) {
+                        // int16 pairs by saturating packs (SAT16), the offset-binary flip per pair, then the
+                        // low and high bytes of four values per word
+                        uint32_t wp[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) wp[k] = pack_sat_s16(out[2 * k + 1], out[2 * k]) ^ (ap.offset ? 0x80008000u : 0u);
+                        uint32_t w0[4], w1[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            w0[k] = __byte_perm(wp[2 * k], wp[2 * k + 1], 0x6420);
+                            w1[k] = __byte_perm(wp[2 * k], wp[2 * k + 1], 0x7531);
+                        }
+                        dst[0] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+                        dst[pstride / 16] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+                    } else {
+                        if (ap.offset) {  // offset binary: the bytes of ctx + 2^31
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) out[q] = static_cast<int32_t>(static_cast<uint32_t>(out[q]) ^ 0x80000000u);
+                        }
+                        uint32_t w[4][4];
+                        pack_planes<16, true>(out, w[0], w[1], w[2], w[3]);
+                        dst[0] = make_uint4(w[0][0], w[0][1], w[0][2], w[0][3]);
+                        dst[pstride / 16] = make_uint4(w[1][0], w[1][1], w[1][2], w[1][3]);
                         dst[2 * pstride / 16] = make_uint4(w[2][0], w[2][1], w[2][2], w[2][3]);
                         dst[3 * pstride / 16] = make_uint4(w[3][0], w[3][1], w[3][2], w[3][3]);
                     }
