@@ -501,18 +501,18 @@ int launch_gemm_p(eii_engine* e, int P, const CUtensorMap& A, const CUtensorMap&
     return fail(EII_ERR_FORMAT, "unsupported plane count %d", P);
 }
 
-template <int P, int KIND, bool RES>
+template <int P, int KIND, bool RES, bool NODIG = false>
 int launch_tgemm_r(eii_engine* e, const CUtensorMap& W, const CUtensorMap& A, const TEpi& ep, cudaStream_t st) {
     using C = TCfg<P, RES>;
     static std::atomic<unsigned long long> attr_done{0};  // one bit per device
     const unsigned long long bit = (e->device >= 0 && e->device < 64) ? (1ull << e->device) : 0ull;
     if (!bit || !(attr_done.load() & bit)) {
-        CK(cudaFuncSetAttribute(k_tgemm<P, KIND, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        CK(cudaFuncSetAttribute(k_tgemm<P, KIND, RES, NODIG>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_done.fetch_or(bit);
     }
     const int tiles = ((ep.N + C::BF - 1) / C::BF) * ((ep.M + C::BR - 1) / C::BR);
     const int grid = tiles < e->num_sms ? tiles : e->num_sms;
-    CK(launch_k(k_tgemm<P, KIND, RES>, dim3(grid), dim3(C::THREADS), C::SMEM, st, W, A, ep));
+    CK(launch_k(k_tgemm<P, KIND, RES, NODIG>, dim3(grid), dim3(C::THREADS), C::SMEM, st, W, A, ep));
     return EII_OK;
 }
 
@@ -522,7 +522,12 @@ int launch_tgemm(eii_engine* e, const CUtensorMap& W, const CUtensorMap& A, cons
                  int prof_kind) {
     ProfScope ps(e, prof_kind, st);
     const bool stream_only = getenv("EII_TGEMM_STREAM") != nullptr;
-    if (ep.K <= 128 * TCfg<P, true>::RES_KB && !stream_only) return launch_tgemm_r<P, KIND, true>(e, W, A, ep, st);
+    const bool res = ep.K <= 128 * TCfg<P, true>::RES_KB && !stream_only;
+    if constexpr (KIND == EPI_SWEEP && P == 4) {  // the sweep without digests: the spill-free no-digest kernel
+        if (!ep.dig && !ep.dig_acc)
+            return res ? launch_tgemm_r<P, KIND, true, true>(e, W, A, ep, st) : launch_tgemm_r<P, KIND, false, true>(e, W, A, ep, st);
+    }
+    if (res) return launch_tgemm_r<P, KIND, true>(e, W, A, ep, st);
     return launch_tgemm_r<P, KIND, false>(e, W, A, ep, st);
 }
 

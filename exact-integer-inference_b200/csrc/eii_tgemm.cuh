@@ -164,7 +164,9 @@ __device__ __forceinline__ uint64_t tg_acc(const uint32_t (&v)[P][16], int i, ui
 }
 
 // ---------------------------------------------------------------------------------------------
-template <int P, int KIND, bool RES>
+// NODIG: the contraction sweep without its per-row digests (the timed launches), compiled without the
+// digest code, which at four planes would otherwise push the epilogue past its 96 registers.
+template <int P, int KIND, bool RES, bool NODIG = false>
 __global__ void __launch_bounds__(TCfg<P, RES>::THREADS, 1)
     k_tgemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA, TEpi ep) {
     using C = TCfg<P, RES>;
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(TCfg<P, RES>::THREADS, 1)
     } else {
         const int quad = warp & 3, rsub = (warp - 2) >> 2;
         griddep_wait();
-        const bool digs = KIND == EPI_SWEEP && (ep.dig || ep.dig_acc);
+        const bool digs = !NODIG && KIND == EPI_SWEEP && (ep.dig || ep.dig_acc);
         const bool ldig = KIND == EPI_LOGITS && ep.dig != nullptr;
         // per-row digest sums of this warp's rows (lane: the row reduce_rows16_row names, per 16-row chunk)
         constexpr int NCH = C::ROWS_PER_WARP / 16;

@@ -73,6 +73,31 @@ def test_sweep_matches_reference_262144_rows(eng, base_model_path, c):
     assert do == c["out_blocks"], "out digests differ"
 
 
+@pytest.mark.parametrize("ci", range(len(sweep.CASES)), ids=[c[0] for c in sweep.CASES])
+def test_sweep_without_digests_equals_with(eng, base_model_path, ci):
+    """A plan run without digests (the timed launches; at four planes a kernel compiled without the
+    digest code) writes the same int32 outputs as the run with digests, which the reference pins."""
+    import torch
+    import _eii
+    M = 4096 + 96  # a ragged last row block
+    W, m, n = sweep.weights(base_model_path, ci)
+    bits_in, f_in, f_out, bits_out = sweep.case_formats(ci)
+    N, K = W.shape
+    a = torch.cat([torch.from_numpy(sweep.activation_block(ci, M, b, K, bits_in)) for b in range(sweep.blocks(M))]).cuda()
+    out_d = torch.empty((M, N), dtype=torch.int32, device="cuda")
+    out_n = torch.full((M, N), -7, dtype=torch.int32, device="cuda")
+    dig_out = torch.empty(M, dtype=torch.int64, device="cuda")
+    dig_acc = torch.empty(M, dtype=torch.int64, device="cuda")
+    plan = _eii.LinearPlan(eng, W, m, n, bits_in, f_in, f_out, bits_out)
+    try:
+        plan.run(a.data_ptr(), M, out_d.data_ptr(), N, dig_out.data_ptr(), dig_acc.data_ptr())
+        plan.run(a.data_ptr(), M, out_n.data_ptr(), N)
+        torch.cuda.synchronize()
+    finally:
+        plan.close()
+    assert torch.equal(out_d, out_n)
+
+
 def test_plan_rejects_out_of_range_activation(eng, base_model_path):
     """A value outside the input format is an argument error (reported by the split kernel), and
     the plan gives exact results afterwards."""
